@@ -1,0 +1,53 @@
+// ABI plumbing shared by the three launchers: per-thread error message,
+// the device error word and its query.
+#include "titan_common.cuh"
+
+#include <string.h>
+
+namespace titan {
+
+static thread_local char t_last_error[512] = "";
+
+void set_error(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return TITAN_OK;
+}
+
+}  // namespace titan
+
+extern "C" int titan_abi_version(void) { return 100; }
+
+extern "C" const char *titan_last_error(void) { return titan::t_last_error; }
+
+extern "C" int titan_device_error(int *error_out, int clear_after, titan_stream_t stream) {
+  if (error_out == nullptr) return titan::fail(TITAN_ERR_INVALID_ARGUMENT, "error_out is null");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return titan::fail(TITAN_ERR_CUDA, "stream sync: %s", cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, titan::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return titan::fail(TITAN_ERR_CUDA, "read error word: %s", cudaGetErrorString(e));
+  if (clear_after && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(titan::g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return titan::fail(TITAN_ERR_CUDA, "clear error word: %s", cudaGetErrorString(e));
+  }
+  *error_out = v;
+  return TITAN_OK;
+}

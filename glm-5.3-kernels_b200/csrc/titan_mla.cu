@@ -1,0 +1,487 @@
+// Sparse NoPE MLA decode over the INT8 528-byte-row cache.
+//
+// Semantics follow kernels/titan_mla.py (the reference Triton path):
+//   :59-182  per (token, 16-head group), over top-k positions of one range:
+//            s_j = (q . k_j) * scale_j * sm_scale * log2(e)   (k_j int8 -> bf16, exact)
+//            masked (index < 0, >= seq_kv, or past the range) -> -1e30, p = 0
+//            online softmax in base 2; acc += bf16(p_j * scale_j) * k_j
+//   :185-255 single range (num_kv_splits == 1): out = bf16(acc / l), l == 0 -> zeros
+//   :258-354 split range s of ceil(topk / S): partial acc / l (fp32) and
+//            lse = (m + log2 l) * ln 2
+//   :357-429 combine: sum_s exp(lse_s - M) o_s / sum_s exp(lse_s - M), bf16
+//
+// B200 design (one CTA per (token, split, head group), 8 warps):
+//  * Gather: warp 0 reads 32 indices per tile and issues one 528-byte bulk copy
+//    (cp.async.bulk, TMA engine) per valid row into a 4-stage shared-memory
+//    ring; completion is counted in bytes on a per-stage mbarrier.  Masked rows
+//    cost no traffic.
+//  * Warp w owns latent dims [64 w, 64 w + 64) for both products, so every
+//    int8 byte is converted to bf16 exactly once, in registers:
+//      QK: mma.sync m16n8k16 (A = 16 heads x 16 dims of q in registers,
+//          B = 16 dims x 8 rows from one 16-byte shared load per lane); the
+//          8 warps' partial scores meet in shared memory.
+//      PV: the same bf16 B fragments are transposed in registers with
+//          movmatrix (rows become the reduction dim), A = P from shared memory.
+//    The k-dimension of QK is permuted identically for q and k (lane c of a
+//    quad reads 16 contiguous bytes), which makes each PV accumulator lane own
+//    16 contiguous output dims.
+//  * Split partials go to a workspace; a combine kernel, launched as a
+//    programmatic dependent of the split kernel, merges them.
+#include "titan_common.cuh"
+
+namespace titan {
+namespace mla {
+
+constexpr int kD = TITAN_LATENT_DIM;       // 512
+constexpr int kRowBytes = TITAN_ROW_BYTES;  // 528
+constexpr int kHeads = TITAN_HEAD_GROUP;    // 16 heads per CTA
+constexpr int kWarps = 8;                   // 64 dims per warp
+constexpr int kThreads = kWarps * 32;
+constexpr int kBN = 32;                     // rows per tile
+constexpr int kStages = 4;                  // gather ring depth
+constexpr int kRowStride = 544;             // smem bytes per row (bank-conflict-free QK loads)
+constexpr int kRedStride = 40;              // floats per head row of a warp's partial scores
+constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (bf16, 32 rows + pad)
+constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct Smem {
+  uint8_t rows[kStages][kBN * kRowStride];
+  float red[kWarps][kHeads * kRedStride];
+  uint32_t p[kHeads * kPStrideWords];
+  float scale[kBN];
+  float alpha[kHeads];
+  float lsum[kHeads];
+  uint32_t valid[kStages];
+  alignas(8) uint64_t bar[kStages];
+};
+
+struct Params {
+  const __nv_bfloat16 *q;
+  int64_t q_st, q_sh;
+  const uint8_t *kv;
+  int64_t kv_rs, seq_kv;
+  const int32_t *idx;
+  int64_t idx_st, topk;
+  __nv_bfloat16 *out;
+  int64_t out_st, out_sh;
+  float *part_o;    // [T][S][Hp][512]
+  float *part_lse;  // [T][S][Hp]
+  int T, H, Hp, S;
+  int64_t split_topk;
+  float scale_log2;  // sm_scale * log2(e)
+};
+
+// Row of an n-tile that lane-quad index g reads: swaps bits 0 and 1 so the two
+// rows served in one quarter-warp phase of a 16-byte load sit 16 banks apart.
+__device__ __forceinline__ int row_perm(int g) { return (g & 4) | ((g & 1) << 1) | ((g >> 1) & 1); }
+
+template <bool kFinal>
+__global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int t = blockIdx.x / p.S;
+  const int split = blockIdx.x - t * p.S;
+  const int hg = blockIdx.y;
+
+  if constexpr (!kFinal) pdl_launch_dependents();
+
+  const int64_t start = (int64_t)split * p.split_topk;
+  const int64_t end = min(start + p.split_topk, p.topk);
+  const int n_rows = end > start ? (int)(end - start) : 0;
+  const int n_tiles = (n_rows + kBN - 1) / kBN;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) mbar_init(&sm.bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int32_t *idx_row = p.idx + (int64_t)t * p.idx_st;
+  const uint64_t evict_first = policy_evict_first();
+
+  // Producer: warp 0 gathers tile `i` into stage i % kStages.
+  auto issue = [&](int i) {
+    const int stage = i % kStages;
+    const int64_t pos = start + (int64_t)i * kBN + lane;
+    int64_t r = -1;
+    if (pos < end) r = idx_row[pos];
+    const bool ok = (r >= 0) && (r < p.seq_kv);
+    const uint32_t mask = __ballot_sync(0xffffffffu, ok);
+    if (lane == 0) {
+      sm.valid[stage] = mask;
+      mbar_arrive_expect_tx(&sm.bar[stage], (uint32_t)__popc(mask) * kRowBytes);
+    }
+    __syncwarp();
+    if (ok) bulk_g2s_hint(&sm.rows[stage][lane * kRowStride], p.kv + r * p.kv_rs, kRowBytes, &sm.bar[stage], evict_first);
+  };
+  if (warp == 0) {
+    const int pre = n_tiles < kStages ? n_tiles : kStages;
+    for (int i = 0; i < pre; ++i) issue(i);
+  }
+
+  // q fragments for this warp's 64 dims (A operand of QK), 4 k-steps.
+  uint32_t qa[4][4];
+  {
+    const int h0 = hg * kHeads + g, h1 = h0 + 8;
+    const int dim0 = warp * 64 + c * 16;
+    uint4 r0a = make_uint4(0, 0, 0, 0), r0b = r0a, r1a = r0a, r1b = r0a;
+    const __nv_bfloat16 *qt = p.q + (int64_t)t * p.q_st;
+    if (h0 < p.H) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(qt + (int64_t)h0 * p.q_sh + dim0);
+      r0a = src[0];
+      r0b = src[1];
+    }
+    if (h1 < p.H) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(qt + (int64_t)h1 * p.q_sh + dim0);
+      r1a = src[0];
+      r1b = src[1];
+    }
+    const uint32_t w0[8] = {r0a.x, r0a.y, r0a.z, r0a.w, r0b.x, r0b.y, r0b.z, r0b.w};
+    const uint32_t w1[8] = {r1a.x, r1a.y, r1a.z, r1a.w, r1b.x, r1b.y, r1b.z, r1b.w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      qa[s][0] = w0[2 * s];
+      qa[s][1] = w1[2 * s];
+      qa[s][2] = w0[2 * s + 1];
+      qa[s][3] = w1[2 * s + 1];
+    }
+  }
+
+  // Softmax state of head (2 warp + lane / 16), replicated over its 16 lanes.
+  float m_run = kNegLarge, l_run = 0.0f;
+  float acc[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+
+  const int red_h = tid >> 4;            // head reduced by this thread
+  const int red_j = (tid & 15) * 2;      // its two n-order positions
+  const int red_nt = red_j >> 3;
+  const int red_r0 = red_nt * 8 + row_perm(red_j & 7);
+  const int red_r1 = red_nt * 8 + row_perm((red_j & 7) + 1);
+
+  for (int i = 0; i < n_tiles; ++i) {
+    const int stage = i % kStages;
+    mbar_wait_bounded(&sm.bar[stage], (uint32_t)((i / kStages) & 1));
+    const uint8_t *buf = sm.rows[stage];
+
+    // ---- QK^T over this warp's 64 dims; keep the bf16 B fragments for PV.
+    uint32_t kf[4][4][2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const uint4 kw = *reinterpret_cast<const uint4 *>(buf + (nt * 8 + row_perm(g)) * kRowStride + warp * 64 + c * 16);
+      i8x4_to_bf16x4(kw.x, kf[nt][0][0], kf[nt][0][1]);
+      i8x4_to_bf16x4(kw.y, kf[nt][1][0], kf[nt][1][1]);
+      i8x4_to_bf16x4(kw.z, kf[nt][2][0], kf[nt][2][1]);
+      i8x4_to_bf16x4(kw.w, kf[nt][3][0], kf[nt][3][1]);
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 4; ++s) mma_bf16_16816(sacc, qa[s], kf[nt][s][0], kf[nt][s][1]);
+      float *red = sm.red[warp];
+      *reinterpret_cast<float2 *>(&red[g * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[0], sacc[1]);
+      *reinterpret_cast<float2 *>(&red[(g + 8) * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[2], sacc[3]);
+    }
+    if (lane < 4) sm.scale[warp * 4 + lane] = *reinterpret_cast<const float *>(buf + (warp * 4 + lane) * kRowStride + 512);
+    __syncthreads();
+
+    // ---- Reduce the 8 partial scores, scale, mask, online softmax, P.
+    {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float2 v = *reinterpret_cast<const float2 *>(&sm.red[w][red_h * kRedStride + red_j]);
+        s0 += v.x;
+        s1 += v.y;
+      }
+      const uint32_t vmask = sm.valid[stage];
+      const bool v0 = (vmask >> red_r0) & 1u, v1 = (vmask >> red_r1) & 1u;
+      const float sc0 = sm.scale[red_r0], sc1 = sm.scale[red_r1];
+      const float x0 = v0 ? (s0 * sc0) * p.scale_log2 : kNegLarge;
+      const float x1 = v1 ? (s1 * sc1) * p.scale_log2 : kNegLarge;
+      float mx = fmaxf(x0, x1);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = ex2_approx(m_run - m_new);
+      const float p0 = v0 ? ex2_approx(x0 - m_new) : 0.0f;
+      const float p1 = v1 ? ex2_approx(x1 - m_new) : 0.0f;
+      float ps = p0 + p1;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l_run = l_run * alpha + ps;
+      m_run = m_new;
+      sm.p[red_h * kPStrideWords + (red_j >> 1)] = pack_bf16x2(v0 ? p0 * sc0 : 0.0f, v1 ? p1 * sc1 : 0.0f);
+      if ((tid & 15) == 0) sm.alpha[red_h] = alpha;
+    }
+    __syncthreads();
+    if (warp == 0 && i + kStages < n_tiles) issue(i + kStages);
+
+    // ---- PV: acc[16 heads x 64 dims] += P[16 x 32] . V[32 x 64].
+    {
+      const float al0 = sm.alpha[g], al1 = sm.alpha[g + 8];
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        acc[n][0] *= al0;
+        acc[n][1] *= al0;
+        acc[n][2] *= al1;
+        acc[n][3] *= al1;
+      }
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t a[4];
+        a[0] = sm.p[g * kPStrideWords + 8 * ks + c];
+        a[1] = sm.p[(g + 8) * kPStrideWords + 8 * ks + c];
+        a[2] = sm.p[g * kPStrideWords + 8 * ks + 4 + c];
+        a[3] = sm.p[(g + 8) * kPStrideWords + 8 * ks + 4 + c];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const uint32_t b0 = movmatrix_trans(kf[2 * ks][s][x]);
+            const uint32_t b1 = movmatrix_trans(kf[2 * ks + 1][s][x]);
+            mma_bf16_16816(acc[2 * s + x], a, b0, b1);
+          }
+        }
+      }
+    }
+  }
+
+  // ---- Epilogue.
+  if ((tid & 15) == 0) sm.lsum[red_h] = l_run;
+  if (!kFinal && (tid & 15) == 0) {
+    const int h = hg * kHeads + red_h;
+    if (h < p.H) {
+      // (m + log2 l) * ln 2; l == 0 gives -inf, which the combine weighs as 0.
+      const float lse = (m_run + lg2_approx(l_run)) * kLn2;
+      p.part_lse[((int64_t)t * p.S + split) * p.Hp + h] = lse;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int hl = g + 8 * half;
+    const int h = hg * kHeads + hl;
+    if (h >= p.H) continue;
+    const float l = sm.lsum[hl];
+    const float inv = l > 0.0f ? 1.0f / l : 1.0f;
+    float v[16];
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        v[4 * s + 2 * x + 0] = acc[2 * s + x][2 * half + 0] * inv;
+        v[4 * s + 2 * x + 1] = acc[2 * s + x][2 * half + 1] * inv;
+      }
+    const int dim0 = warp * 64 + c * 16;
+    if constexpr (kFinal) {
+      uint4 o0, o1;
+      o0.x = pack_bf16x2(v[0], v[1]);
+      o0.y = pack_bf16x2(v[2], v[3]);
+      o0.z = pack_bf16x2(v[4], v[5]);
+      o0.w = pack_bf16x2(v[6], v[7]);
+      o1.x = pack_bf16x2(v[8], v[9]);
+      o1.y = pack_bf16x2(v[10], v[11]);
+      o1.z = pack_bf16x2(v[12], v[13]);
+      o1.w = pack_bf16x2(v[14], v[15]);
+      uint4 *dst = reinterpret_cast<uint4 *>(p.out + (int64_t)t * p.out_st + (int64_t)h * p.out_sh + dim0);
+      dst[0] = o0;
+      dst[1] = o1;
+    } else {
+      float4 *dst = reinterpret_cast<float4 *>(p.part_o + (((int64_t)t * p.S + split) * p.Hp + h) * kD + dim0);
+      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+      dst[2] = make_float4(v[8], v[9], v[10], v[11]);
+      dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+    }
+  }
+}
+
+// Combine: one CTA per (token, head group, chunk of kDC dims); thread owns one
+// head and 4 consecutive dims.  Online merge over splits in natural log,
+// kernels/titan_mla.py:403-427.
+template <int kDC>
+__global__ void __launch_bounds__(kHeads * kDC / 4) sparse_mla_combine_kernel(const Params p) {
+  pdl_wait_primary();
+  constexpr int kTpH = kDC / 4;  // threads per head
+  const int t = blockIdx.x;
+  const int hg = blockIdx.y;
+  const int chunk = blockIdx.z;
+  const int hl = threadIdx.x / kTpH;
+  const int h = hg * kHeads + hl;
+  if (h >= p.H) return;
+  const int dim = chunk * kDC + (threadIdx.x % kTpH) * 4;
+  const float *lse_base = p.part_lse + (int64_t)t * p.S * p.Hp + h;
+  const float *o_base = p.part_o + ((int64_t)t * p.S * p.Hp + h) * kD + dim;
+  const int64_t o_split_stride = (int64_t)p.Hp * kD;
+  constexpr float kLog2e = 1.4426950408889634f;
+  float e_max = kNegLarge, e_sum = 0.0f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int s = 0; s < p.S; ++s) {
+    const float lse = lse_base[(int64_t)s * p.Hp];
+    const float4 o = *reinterpret_cast<const float4 *>(o_base + s * o_split_stride);
+    const float n_max = fmaxf(lse, e_max);
+    const float old_scale = ex2_approx((e_max - n_max) * kLog2e);
+    const float w = ex2_approx((lse - n_max) * kLog2e);
+    acc.x = acc.x * old_scale + w * o.x;
+    acc.y = acc.y * old_scale + w * o.y;
+    acc.z = acc.z * old_scale + w * o.z;
+    acc.w = acc.w * old_scale + w * o.w;
+    e_sum = e_sum * old_scale + w;
+    e_max = n_max;
+  }
+  const float inv = e_sum > 0.0f ? 1.0f / e_sum : 1.0f;
+  uint2 r;
+  r.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  r.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2 *>(p.out + (int64_t)t * p.out_st + (int64_t)h * p.out_sh + dim) = r;
+}
+
+template <int kDC>
+static cudaError_t launch_combine(const Params &prm, int groups, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)prm.T, (unsigned)groups, (unsigned)(kD / kDC));
+  cfg.blockDim = dim3(kHeads * kDC / 4);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, sparse_mla_combine_kernel<kDC>, prm);
+}
+
+// Per-device one-time setup: the dynamic shared-memory opt-in of both kernel
+// variants and the SM count used to size the combine grid.
+static int g_sm_count[64] = {0};
+static bool g_smem_attr[64] = {false};
+
+static int ensure_smem_attribute(int smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64 && g_smem_attr[dev]) return TITAN_OK;
+  e = cudaFuncSetAttribute(sparse_mla_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(sparse_mla_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: shared-memory attribute: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64) g_smem_attr[dev] = true;
+  return TITAN_OK;
+}
+
+static int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+}  // namespace mla
+}  // namespace titan
+
+extern "C" int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_heads, int64_t num_kv_splits) {
+  using namespace titan::mla;
+  if (num_kv_splits <= 1 || num_tokens <= 0 || num_heads <= 0) return 0;
+  const int64_t hp = (num_heads + kHeads - 1) / kHeads * kHeads;
+  const int64_t o_bytes = num_tokens * num_kv_splits * hp * kD * 4;
+  const int64_t lse_bytes = num_tokens * num_kv_splits * hp * 4;
+  return o_bytes + ((lse_bytes + 255) / 256) * 256;
+}
+
+extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                                          const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                                          const int32_t *indices, int64_t indices_stride_token, int64_t topk,
+                                          void *out, int64_t out_stride_token, int64_t out_stride_head,
+                                          int64_t num_tokens, int64_t num_heads, float sm_scale,
+                                          int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
+                                          titan_stream_t stream) {
+  using namespace titan;
+  using namespace titan::mla;
+  if (num_tokens < 0 || num_heads <= 0 || topk < 0 || seq_kv < 0)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: invalid sizes");
+  if (num_tokens == 0) return TITAN_OK;
+  if (num_kv_splits < 1) return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: num_kv_splits must be >= 1");
+  if (q == nullptr || kv == nullptr || indices == nullptr || out == nullptr)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: null pointer");
+  if ((uintptr_t)kv % 16 || kv_row_stride % 16)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: kv base and row stride must be 16-byte aligned");
+  if ((uintptr_t)q % 16 || (q_stride_token * 2) % 16 || (q_stride_head * 2) % 16)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: q rows must be 16-byte aligned");
+  if ((uintptr_t)out % 16 || (out_stride_token * 2) % 16 || (out_stride_head * 2) % 16)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: out rows must be 16-byte aligned");
+  const int64_t groups = (num_heads + kHeads - 1) / kHeads;
+  if (groups > 65535) return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: too many heads");
+  if (num_tokens * num_kv_splits > 0x7fffffffLL) return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: grid too large");
+  const int64_t need = titan_mla_workspace_bytes(num_tokens, num_heads, num_kv_splits);
+  if (num_kv_splits > 1) {
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: workspace too small (%lld < %lld bytes)",
+                  (long long)workspace_bytes, (long long)need);
+    if ((uintptr_t)workspace % 16) return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: workspace must be 16-byte aligned");
+  }
+
+  Params prm;
+  prm.q = static_cast<const __nv_bfloat16 *>(q);
+  prm.q_st = q_stride_token;
+  prm.q_sh = q_stride_head;
+  prm.kv = static_cast<const uint8_t *>(kv);
+  prm.kv_rs = kv_row_stride;
+  prm.seq_kv = seq_kv;
+  prm.idx = indices;
+  prm.idx_st = indices_stride_token;
+  prm.topk = topk;
+  prm.out = static_cast<__nv_bfloat16 *>(out);
+  prm.out_st = out_stride_token;
+  prm.out_sh = out_stride_head;
+  prm.T = (int)num_tokens;
+  prm.H = (int)num_heads;
+  prm.Hp = (int)(groups * kHeads);
+  prm.S = (int)num_kv_splits;
+  prm.split_topk = (topk + num_kv_splits - 1) / num_kv_splits;
+  prm.scale_log2 = sm_scale * 1.4426950408889634f;
+  prm.part_o = nullptr;
+  prm.part_lse = nullptr;
+  if (num_kv_splits > 1) {
+    const int64_t o_bytes = num_tokens * num_kv_splits * prm.Hp * kD * 4;
+    prm.part_o = static_cast<float *>(workspace);
+    prm.part_lse = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + o_bytes);
+  }
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = sizeof(Smem) + 128;
+  const dim3 grid((unsigned)(num_tokens * num_kv_splits), (unsigned)groups);
+  int rc = ensure_smem_attribute((int)smem);
+  if (rc != TITAN_OK) return rc;
+  if (num_kv_splits == 1) {
+    sparse_mla_kernel<true><<<grid, kThreads, smem, s>>>(prm);
+    return check_launch("mla final launch");
+  }
+  sparse_mla_kernel<false><<<grid, kThreads, smem, s>>>(prm);
+  rc = check_launch("mla split launch");
+  if (rc != TITAN_OK) return rc;
+  // Combine grid sized from the SM count: the widest dim chunk that still
+  // gives every SM a CTA.
+  const int sms = device_sm_count();
+  const int64_t base = num_tokens * groups;
+  cudaError_t e;
+  if (base * (kD / 128) >= sms)
+    e = launch_combine<128>(prm, (int)groups, s);
+  else if (base * (kD / 64) >= sms)
+    e = launch_combine<64>(prm, (int)groups, s);
+  else if (base * (kD / 32) >= sms)
+    e = launch_combine<32>(prm, (int)groups, s);
+  else
+    e = launch_combine<16>(prm, (int)groups, s);
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla combine launch: %s", cudaGetErrorString(e));
+  return TITAN_OK;
+}

@@ -1,0 +1,127 @@
+// Small stable MoE route alignment: B1..8 tokens x top-8, 288 experts, block 8.
+//
+// Output contract of kernels/titan_moe_align.py:12-46 (the reference
+// `_align_small`), equal to the stable argsort layout of
+// benchmarks/moe_align.py:23-31 (`cpu_reference`):
+//   rank_j   = #{k < j valid : e_k == e_j}           count_e = #{valid : e}
+//   pad_e    = ceil(count_e / 8) * 8                  off_e   = sum of pad over experts < e
+//   sorted_ids[off_e + rank_j] = j  (rest = R),  expert_ids[off_e/8 + b] = e (rest = -1),
+//   postpad  = sum pad_e.
+//
+// B200 design: warp 0 computes everything with warp primitives instead of the
+// reference's R x R pairwise compare.  Routes j and j + 32 live in lane j.
+// Ranks come from __match_any_sync (peer mask) and a popcount of the lower
+// lanes; the 288 expert counts live in shared memory; the padded offsets are
+// a warp prefix scan with 9 experts per lane (32 x 9 = 288).  The result is
+// assembled in shared memory and written with coalesced stores by the whole CTA.
+#include "titan_common.cuh"
+
+namespace titan {
+
+constexpr int kMoeMaxRoutes = 64;  // B <= 8, top-8
+constexpr int kMoeExperts = TITAN_MOE_NUM_EXPERTS;
+constexpr int kMoePerLane = kMoeExperts / 32;  // 9
+static_assert(kMoePerLane * 32 == kMoeExperts, "expert count must split evenly over a warp");
+
+template <typename IdT>
+__global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restrict__ ids, int R,
+                                                              int32_t *__restrict__ sorted_ids,
+                                                              int32_t *__restrict__ expert_ids,
+                                                              int32_t *__restrict__ postpad) {
+  __shared__ int s_count[kMoeExperts];
+  __shared__ int s_offset[kMoeExperts];
+  __shared__ int s_sorted[kMoeMaxRoutes * 8];
+  __shared__ int s_experts[kMoeMaxRoutes];
+  __shared__ int s_total;
+
+  const int tid = threadIdx.x;
+  const int nthr = blockDim.x;
+  for (int i = tid; i < R * 8; i += nthr) s_sorted[i] = R;
+  for (int i = tid; i < R; i += nthr) s_experts[i] = -1;
+  for (int i = tid; i < kMoeExperts; i += nthr) s_count[i] = 0;
+  __syncthreads();
+
+  if (tid < 32) {
+    const int lane = tid;
+    const unsigned lt = (1u << lane) - 1u;
+    // Route lane (half 0) and lane + 32 (half 1).  Validity is decided on the
+    // full-width id, before narrowing (an int64 id of 2^32 + 5 is invalid).
+    int e0 = -1, e1 = -1;
+    if (lane < R) {
+      const long long raw = (long long)ids[lane];
+      if (raw >= 0 && raw < kMoeExperts) e0 = (int)raw;
+    }
+    if (lane + 32 < R) {
+      const long long raw = (long long)ids[lane + 32];
+      if (raw >= 0 && raw < kMoeExperts) e1 = (int)raw;
+    }
+    // Invalid routes get a key no valid expert uses; they never scatter.
+    const unsigned m0 = __match_any_sync(0xffffffffu, e0 >= 0 ? e0 : 0x7fffffff);
+    const int rank0 = __popc(m0 & lt);
+    if (e0 >= 0 && rank0 == 0) s_count[e0] = __popc(m0);
+    __syncwarp();
+    const int base1 = e1 >= 0 ? s_count[e1] : 0;  // routes of half 0 precede half 1
+    const unsigned m1 = __match_any_sync(0xffffffffu, e1 >= 0 ? e1 : 0x7fffffff);
+    const int rank1 = base1 + __popc(m1 & lt);
+    __syncwarp();
+    if (e1 >= 0 && __popc(m1 & lt) == 0) s_count[e1] = base1 + __popc(m1);
+    __syncwarp();
+
+    // Exclusive prefix of padded counts: lane owns experts [9 lane, 9 lane + 9).
+    int local[kMoePerLane];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < kMoePerLane; ++k) {
+      const int c = s_count[kMoePerLane * lane + k];
+      local[k] = sum;
+      sum += (c + 7) & ~7;
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int excl = incl - sum;
+#pragma unroll
+    for (int k = 0; k < kMoePerLane; ++k) {
+      const int e = kMoePerLane * lane + k;
+      const int off = excl + local[k];
+      s_offset[e] = off;
+      const int blocks = ((s_count[e] + 7) & ~7) >> 3;
+      for (int b = 0; b < blocks; ++b) s_experts[(off >> 3) + b] = e;
+    }
+    __syncwarp();
+    if (e0 >= 0) s_sorted[s_offset[e0] + rank0] = lane;
+    if (e1 >= 0) s_sorted[s_offset[e1] + rank1] = lane + 32;
+    if (lane == 31) s_total = incl;
+  }
+  __syncthreads();
+  for (int i = tid; i < R * 8; i += nthr) sorted_ids[i] = s_sorted[i];
+  for (int i = tid; i < R; i += nthr) expert_ids[i] = s_experts[i];
+  if (tid == 0) postpad[0] = s_total;
+}
+
+}  // namespace titan
+
+extern "C" int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int64_t num_routes,
+                                     int32_t *sorted_ids, int32_t *expert_ids, int32_t *postpad, int num_warps,
+                                     titan_stream_t stream) {
+  using namespace titan;
+  if (num_routes < 8 || num_routes > kMoeMaxRoutes || num_routes % 8 != 0)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_align_small: num_routes must be 8*B with B in 1..8, got %lld",
+                (long long)num_routes);
+  if (num_warps != 1 && num_warps != 2 && num_warps != 4)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_align_small: num_warps must be 1, 2 or 4");
+  if (topk_ids == nullptr || sorted_ids == nullptr || expert_ids == nullptr || postpad == nullptr)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_align_small: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int R = (int)num_routes;
+  if (ids_is_int64)
+    moe_align_small_kernel<long long><<<1, 32 * num_warps, 0, s>>>(static_cast<const long long *>(topk_ids), R,
+                                                                  sorted_ids, expert_ids, postpad);
+  else
+    moe_align_small_kernel<int32_t><<<1, 32 * num_warps, 0, s>>>(static_cast<const int32_t *>(topk_ids), R,
+                                                                 sorted_ids, expert_ids, postpad);
+  return check_launch("moe_align_small launch");
+}

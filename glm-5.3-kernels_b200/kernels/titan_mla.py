@@ -1,0 +1,158 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Sparse NoPE MLA over a per-token INT8 KV cache, for B200 (sm_100a).
+
+Drop-in for the reference `triton_mla_sparse_attention`
+(kernels/titan_mla.py:452-581) with the same argument order, defaults,
+assertions and split heuristic (`_choose_num_kv_splits`, :432-449).  The
+compute runs in libtitan_b200.so (csrc/titan_mla.cu): a bulk-copy (TMA) row
+gather into shared memory, bf16 tensor-core MMAs with fp32 online softmax, and
+a combine kernel for split-KV launches.
+
+528 bytes/token: 512 signed INT8 values followed by 1 FP32 scale + 12 zero bytes.
+"""
+
+import functools
+
+import torch
+
+try:
+    from . import titan_native as _native
+except ImportError:
+    import titan_native as _native
+
+LOG2E = 1.4426950408889634
+LOGE2 = 0.6931471805599453
+
+# GLM-5.3 sparse MLA shape constants (kernels/titan_mla.py:23-29).
+_BLOCK_DMODEL = 512
+_BLOCK_DPE = 64
+_BLOCK_DV = 512
+_DIM_QK = _BLOCK_DMODEL + _BLOCK_DPE  # 576
+_BLOCK_H = 16
+_ROW_BYTES = 528
+
+# Smallest top-k granule the API accepts (the reference's smallest BLOCK_N,
+# kernels/titan_mla.py:45-49); kept so the same inputs are accepted/rejected.
+_MIN_BLOCK_N = 32
+
+# Split-count candidates and heuristic constants (kernels/titan_mla.py:53-56).
+KV_SPLITS_CANDIDATES = (1, 2, 4, 8, 16)
+_MIN_TOPK_PER_SPLIT = 128
+_SPLIT_MAX_OCCUPANCY = 4
+
+
+def num_compute_units(device_index):
+    return torch.cuda.get_device_properties(device_index).multi_processor_count
+
+
+def _cdiv(a, b):
+    return -(-a // b)
+
+
+def _next_power_of_2(n):
+    return 1 if n <= 1 else 1 << (int(n) - 1).bit_length()
+
+
+@functools.lru_cache(maxsize=256)
+def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int, sm_count: int) -> int:
+    """Pick a power-of-2 split count that fills the device without dropping
+    per-split work below _MIN_TOPK_PER_SPLIT; 1 when the single-pass grid
+    already reaches ~1/_SPLIT_MAX_OCCUPANCY of the SMs.  Same policy and
+    results as kernels/titan_mla.py:432-449.
+    """
+    baseline = num_tokens * num_head_groups
+    if baseline == 0 or baseline * _SPLIT_MAX_OCCUPANCY >= sm_count:
+        return 1
+    ideal = _next_power_of_2(max(1, index_topk // _MIN_TOPK_PER_SPLIT))
+    max_splits = max(1, sm_count // baseline)
+    max_splits = 1 << (max_splits.bit_length() - 1)  # floor to a power of 2
+    num_kv_splits = min(ideal, max_splits)
+    while num_kv_splits > 1 and index_topk % num_kv_splits != 0:
+        num_kv_splits //= 2
+    return max(1, num_kv_splits)
+
+
+def _aligned16(t):
+    return t.data_ptr() % 16 == 0 and all((s * t.element_size()) % 16 == 0 for s in t.stride()[:-1])
+
+
+def triton_mla_sparse_attention(
+    q: torch.Tensor,
+    kv: torch.Tensor,
+    indices: torch.Tensor,
+    sm_scale: float,
+    num_kv_splits: int | None = None,
+    sm_count: int | None = None,
+) -> torch.Tensor:
+    """Sparse MLA attention over top-k indices.
+
+    Args:
+        q:         [num_tokens, num_heads_q, 512] bf16
+        kv:        [seq_kv, 1, 528] int8 packed cache (528-byte rows)
+        indices:   [num_tokens, 1, topk] int32; entries outside [0, seq_kv) are masked
+        sm_scale:  softmax scale
+        num_kv_splits: override the auto-heuristic; None/0 = auto, 1 = single pass.
+        sm_count:  cached device SM count for the split heuristic.
+
+    Returns:
+        out:   [num_tokens, num_heads_q, 512] bf16 (a new tensor)
+    """
+    num_tokens, num_heads_q, dim_qk = q.shape
+    # Shape contract of kernels/titan_mla.py:478-488.
+    assert dim_qk in (_BLOCK_DMODEL, _DIM_QK), (
+        f"sparse MLA kernel requires dim_qk={_BLOCK_DMODEL} (NoPE) or "
+        f"{_DIM_QK} (RoPE), got {dim_qk}"
+    )
+    block_dpe = dim_qk - _BLOCK_DMODEL
+    assert kv.shape[1] == 1 and kv.shape[2] == (_ROW_BYTES if kv.dtype == torch.int8 else dim_qk)
+    index_topk = indices.shape[2]
+    assert index_topk % _MIN_BLOCK_N == 0, (
+        f"topk ({index_topk}) must be a multiple of the smallest autotune "
+        f"BLOCK_N ({_MIN_BLOCK_N})"
+    )
+    # This build carries the INT8 NoPE path (GLM-5.3, qk_rope_head_dim = 0).
+    assert block_dpe == 0 and kv.dtype == torch.int8, (
+        "the B200 kernel implements the INT8 NoPE path: dim_qk=512 with a [seq_kv, 1, 528] int8 cache")
+    assert q.dtype == torch.bfloat16, "q must be bf16"
+    assert q.is_cuda and kv.is_cuda and indices.is_cuda, "sparse MLA runs on CUDA tensors only"
+    assert q.device == kv.device == indices.device, "q, kv and indices must share a device"
+
+    kv_group_num = num_heads_q
+    num_head_groups = _cdiv(num_heads_q, min(_BLOCK_H, kv_group_num))
+
+    if num_kv_splits is None or num_kv_splits == 0:
+        if sm_count is None:
+            sm_count = num_compute_units(q.device.index)
+        num_kv_splits = _choose_num_kv_splits(num_tokens, num_head_groups, index_topk, sm_count)
+
+    out = torch.empty((num_tokens, num_heads_q, _BLOCK_DV), dtype=torch.bfloat16, device=q.device)
+    if num_tokens == 0:
+        return out
+
+    seq_kv = kv.shape[0]
+    if q.stride(-1) != 1 or not _aligned16(q):
+        q = q.contiguous()
+    idx = indices[:, 0, :]
+    if idx.dtype != torch.int32:
+        # Out-of-range wide indices must stay masked after narrowing.
+        idx = torch.where((idx >= 0) & (idx < seq_kv), idx, -1).to(torch.int32)
+    if idx.stride(-1) != 1:
+        idx = idx.contiguous()
+    kv_row_stride = kv.stride(0)  # bytes (int8)
+
+    lib = _native.load()
+    ws_bytes = lib.titan_mla_workspace_bytes(num_tokens, num_heads_q, num_kv_splits)
+    # Split partials live in a caching-allocator buffer, like the reference's
+    # `mid_out` (kernels/titan_mla.py:533-537): graph-capture safe, no sync.
+    workspace = torch.empty(max(ws_bytes, 0), dtype=torch.uint8, device=q.device) if ws_bytes > 0 else None
+    with torch.cuda.device(q.device):
+        rc = lib.titan_mla_sparse_attention(
+            q.data_ptr(), q.stride(0), q.stride(1),
+            kv.data_ptr(), kv_row_stride, seq_kv,
+            idx.data_ptr(), idx.stride(0), index_topk,
+            out.data_ptr(), out.stride(0), out.stride(1),
+            num_tokens, num_heads_q, float(sm_scale), int(num_kv_splits),
+            workspace.data_ptr() if workspace is not None else None, ws_bytes,
+            _native.stream_of(q))
+    _native.check(rc, "triton_mla_sparse_attention")
+    return out

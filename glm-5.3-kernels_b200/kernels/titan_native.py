@@ -1,0 +1,86 @@
+# SPDX-License-Identifier: Apache-2.0
+"""ctypes binding of libtitan_b200.so, the C ABI declared in include/titan_b200.h.
+
+The library is loaded lazily on the first kernel call, so importing the
+titan_* modules touches neither the library nor CUDA (the reference's import
+contract, tests/test_cpu_contracts.py:33-53).  There is no fallback: a missing
+library or a failed launch raises.
+"""
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_PKG_ROOT = Path(__file__).resolve().parent.parent
+_DEFAULT_LIB = _PKG_ROOT / "lib" / "libtitan_b200.so"
+
+_lock = threading.Lock()
+_lib = None
+
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_vp = ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/titan_b200.h.
+SIGNATURES = {
+    "titan_abi_version": (_int, []),
+    "titan_last_error": (ctypes.c_char_p, []),
+    "titan_store_int8": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _int, _i64, _vp]),
+    "titan_mla_workspace_bytes": (_i64, [_i64, _i64, _i64]),
+    "titan_mla_sparse_attention": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+         ctypes.c_float, _i64, _vp, _i64, _vp],
+    ),
+    "titan_moe_align_small": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _int, _vp]),
+    "titan_device_error": (_int, [ctypes.POINTER(_int), _int, _vp]),
+}
+
+
+class TitanError(RuntimeError):
+    """A launcher of libtitan_b200.so returned a non-zero status."""
+
+
+def library_path():
+    return Path(os.environ.get("TITAN_B200_LIB", str(_DEFAULT_LIB)))
+
+
+def load():
+    """Return the loaded library (loading it on first use)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = library_path()
+            if not path.exists():
+                raise TitanError(
+                    f"{path} is missing: build it with `python glm-5.3-kernels_b200/build.py` "
+                    "(there is no CPU or Triton fallback)")
+            lib = ctypes.CDLL(str(path))
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = lib
+    return _lib
+
+
+def check(status, what):
+    if status != 0:
+        msg = load().titan_last_error().decode(errors="replace")
+        raise TitanError(f"{what} failed (status {status}): {msg}")
+
+
+def stream_of(tensor):
+    """Raw handle of torch's current stream on the tensor's device."""
+    import torch
+    return torch.cuda.current_stream(tensor.device).cuda_stream
+
+
+def device_error(tensor, clear=True):
+    """Synchronise and read the device error word (0 = none)."""
+    out = _int(0)
+    check(load().titan_device_error(ctypes.byref(out), 1 if clear else 0, stream_of(tensor)),
+          "titan_device_error")
+    return out.value

@@ -1,0 +1,137 @@
+/*
+ * titan_b200.h — C ABI of the B200 (sm_100a) GLM-5.3 sparse-MLA decode path.
+ *
+ * Three hot-path operations, each one `extern "C"` launcher that takes plain
+ * device pointers, sizes, strides and a CUDA stream, launches on that stream,
+ * never synchronises and never allocates.  The caller owns every buffer.
+ *
+ *   titan_store_int8              replaces kernels/titan_kv.py:23-28
+ *   titan_mla_sparse_attention    replaces kernels/titan_mla.py:452-581
+ *   titan_moe_align_small         replaces kernels/titan_moe_align.py:49-81
+ *
+ * The Python modules titan_kv / titan_mla / titan_moe_align keep the
+ * reference's names, argument meaning and exception types and call these
+ * entry points through ctypes.
+ *
+ * Return value: TITAN_OK (0) or a non-zero TITAN_ERR_* code; the message of
+ * the last failure on the calling thread is available from titan_last_error().
+ *
+ * Byte layout of one INT8 KV row ("528-byte row", kernels/titan_kv.py:19-21,
+ * kernels/titan_mla.py:4-7): bytes [0,512) int8 latent values, bytes [512,516)
+ * little-endian fp32 scale, bytes [516,528) zero.
+ */
+#ifndef TITAN_B200_H
+#define TITAN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t / CUstream handle (0 = legacy default stream). */
+typedef struct CUstream_st *titan_stream_t;
+
+#define TITAN_OK 0
+#define TITAN_ERR_INVALID_ARGUMENT 1 /* shape / dtype / alignment rejected on the host */
+#define TITAN_ERR_CUDA 2             /* a CUDA runtime call failed */
+#define TITAN_ERR_UNSUPPORTED 3      /* valid for the reference but not built here */
+
+#define TITAN_LATENT_DIM 512
+#define TITAN_ROW_BYTES 528
+#define TITAN_HEAD_GROUP 16
+#define TITAN_MOE_NUM_EXPERTS 288
+#define TITAN_MOE_TOPK 8
+#define TITAN_MOE_BLOCK 8
+
+/* ABI version (major * 100 + minor). */
+int titan_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *titan_last_error(void);
+
+/*
+ * INT8 latent KV writer.  Replaces `store_int8(x, cache, slots)`,
+ * kernels/titan_kv.py:23-28 (kernel body :7-21).
+ *
+ * For i < n_slots with s = slots[i] >= 0: quantise x[i, 0:512] (bf16) to the
+ * 528-byte row at cache + (s / block_size) * cache_stride0 + (s % block_size) *
+ * cache_stride1.  scale = max(max|x| / 127, 1e-12) (IEEE fp32 division),
+ * q = clamp(nearbyint(x / scale), -127, 127).  Negative slots are skipped.
+ * Slots whose block index is >= num_blocks are skipped as well (the reference
+ * would write out of bounds there).
+ *
+ *   x               bf16, row i at x + i * x_row_stride elements; last dim contiguous
+ *   cache           int8 (or uint8) base pointer
+ *   cache_stride0   bytes between blocks;  cache_stride1  bytes between slots of a block
+ *   slots           int64 (slots_is_int64 = 1) or int32 (0), n_slots entries
+ */
+int titan_store_int8(const void *x, int64_t x_row_stride,
+                     void *cache, int64_t num_blocks, int64_t block_size,
+                     int64_t cache_stride0, int64_t cache_stride1,
+                     const void *slots, int slots_is_int64, int64_t n_slots,
+                     titan_stream_t stream);
+
+/*
+ * Workspace bytes titan_mla_sparse_attention needs for a split-KV launch
+ * (0 when num_kv_splits == 1).  Mirrors the reference's `mid_out` buffer,
+ * kernels/titan_mla.py:533-537 (layout differs: fp32 partial outputs plus a
+ * separate natural-log LSE array).
+ */
+int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_heads,
+                                  int64_t num_kv_splits);
+
+/*
+ * Sparse NoPE MLA attention over an INT8 528-byte-row cache.  Replaces
+ * `triton_mla_sparse_attention(q, kv, indices, sm_scale, num_kv_splits,
+ * sm_count)`, kernels/titan_mla.py:452-581 (kernels :59-429).
+ *
+ *   q        bf16 [num_tokens, num_heads, 512]; strides in elements, last dim contiguous
+ *   kv       int8 rows; row r at kv + r * kv_row_stride bytes, r in [0, seq_kv)
+ *   indices  int32 [num_tokens, topk]; token stride in elements, last dim contiguous.
+ *            An index outside [0, seq_kv) is masked (contributes nothing).
+ *   out      bf16 [num_tokens, num_heads, 512]; strides in elements
+ *   sm_scale softmax scale (not pre-multiplied by log2 e)
+ *   num_kv_splits  >= 1; 1 = single pass, otherwise split-KV + combine
+ *   workspace      >= titan_mla_workspace_bytes(...) bytes of device memory, 16-byte aligned
+ *
+ * kv and kv_row_stride must be 16-byte aligned (each row is fetched by one bulk
+ * copy).  A token whose indices are all masked produces exact zeros.
+ */
+int titan_mla_sparse_attention(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                               const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                               const int32_t *indices, int64_t indices_stride_token, int64_t topk,
+                               void *out, int64_t out_stride_token, int64_t out_stride_head,
+                               int64_t num_tokens, int64_t num_heads, float sm_scale,
+                               int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
+                               titan_stream_t stream);
+
+/*
+ * Small stable MoE route alignment (B1..8, top-8, 288 experts, block 8).
+ * Replaces `titan_moe_align_small(topk_ids, ...)`, kernels/titan_moe_align.py:49-81
+ * (kernel :12-46).
+ *
+ *   topk_ids    int32 (ids_is_int64 = 0) or int64 (1), num_routes = 8 * B entries, contiguous
+ *   sorted_ids  int32 [8 * num_routes]   (padding entries hold num_routes)
+ *   expert_ids  int32 [num_routes]       (unused blocks hold -1)
+ *   postpad     int32 [1]                (sum of per-expert counts rounded up to 8)
+ *   num_warps   1, 2 or 4: CTA size; does not change the outputs
+ *
+ * Routes outside [0, 288) are ignored.
+ */
+int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int64_t num_routes,
+                          int32_t *sorted_ids, int32_t *expert_ids, int32_t *postpad,
+                          int num_warps, titan_stream_t stream);
+
+/*
+ * Device-side error word: kernels set it instead of trapping when a bounded
+ * wait gives up.  Reads (and, if clear_after is non-zero, resets) the word of
+ * the current device; synchronises the stream first.  0 = no error.
+ */
+int titan_device_error(int *error_out, int clear_after, titan_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TITAN_B200_H */

@@ -1,0 +1,200 @@
+# SPDX-License-Identifier: Apache-2.0
+"""CPU oracle for the sparse-MLA decode path — TEST INFRASTRUCTURE ONLY.
+
+Restates the reference algorithms on the CPU (numpy for the byte/integer work,
+torch-CPU fp32 for attention) so the CUDA path can be checked against them.
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may use
+this module, and only as the checker or the timed CPU baseline: the product
+(glm-5.3-kernels_b200/) never imports it.
+
+Pinning: store_int8_rows and moe_align_small are checked bit-exactly against
+golden vectors produced by the reference's own code (tests/golden/make_golden.py
+runs kernels/titan_kv.py, kernels/titan_moe_align.py and the
+benchmarks/moe_align.py oracles); mla_sparse_attention is checked against the
+reference MLA kernels' outputs within the path's tolerance.
+"""
+import numpy as np
+import torch
+
+LATENT_DIM = 512
+ROW_BYTES = 528
+NUM_EXPERTS = 288
+NEG_LARGE = -1.0e30
+
+
+# --------------------------------------------------------------------- INT8 KV
+def bf16_bits_to_f32(bits):
+    """uint16 bf16 bit patterns -> float32 (exact)."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def tensor_bf16_bits(t):
+    """torch bf16 tensor (any device) -> numpy uint16 bit patterns."""
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def store_int8_rows(x_bits):
+    """Quantise bf16 latents [N, 512] (uint16 bit patterns) to 528-byte rows.
+
+    Follows kernels/titan_kv.py:15-21 with IEEE fp32 arithmetic:
+      scale = max(max|x| / 127, 1e-12); q = clamp(nearbyint(x / scale), -127, 127)
+    Row bytes: [0,512) q as int8, [512,516) scale (fp32 LE), [516,528) zero.
+    Returns uint8 [N, 528].
+    """
+    x = bf16_bits_to_f32(np.asarray(x_bits).reshape(-1, LATENT_DIM))
+    amax = np.abs(x).max(axis=1)
+    scale = np.maximum(amax / np.float32(127.0), np.float32(1.0e-12)).astype(np.float32)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        q = np.rint(x / scale[:, None])  # np.rint rounds half to even, like nearbyint
+    q = np.clip(q, -127, 127).astype(np.int8)
+    rows = np.zeros((x.shape[0], ROW_BYTES), dtype=np.uint8)
+    rows[:, :LATENT_DIM] = q.view(np.uint8)
+    rows[:, LATENT_DIM:LATENT_DIM + 4] = scale.view(np.uint8).reshape(-1, 4)
+    return rows
+
+
+def store_int8(x_bits, cache, slots):
+    """In-place oracle of `store_int8(x, cache, slots)` (kernels/titan_kv.py:7-28).
+
+    cache: numpy uint8/int8 [num_blocks, block_size, 528]; slots: integer array.
+    Slot s >= 0 writes row s // block_size, s % block_size; s < 0 is skipped.
+    """
+    slots = np.asarray(slots).reshape(-1).astype(np.int64)
+    x_bits = np.asarray(x_bits).reshape(-1, LATENT_DIM)[: slots.size]
+    rows = store_int8_rows(x_bits)
+    flat = cache.view(np.uint8).reshape(-1, ROW_BYTES)
+    block = cache.shape[1]
+    keep = slots >= 0
+    dest = (slots[keep] // block) * block + slots[keep] % block
+    flat[dest] = rows[keep]
+    return cache
+
+
+def dequantize_rows(rows):
+    """528-byte rows (uint8/int8 [N, 528]) -> fp32 [N, 512] = int8 * scale."""
+    rows = np.ascontiguousarray(np.asarray(rows).view(np.uint8).reshape(-1, ROW_BYTES))
+    q = rows[:, :LATENT_DIM].view(np.int8).astype(np.float32)
+    scale = rows[:, LATENT_DIM:LATENT_DIM + 4].copy().view(np.float32)
+    return q * scale
+
+
+# ----------------------------------------------------------------- sparse MLA
+def choose_num_kv_splits(num_tokens, num_head_groups, index_topk, sm_count):
+    """Restatement of kernels/titan_mla.py:432-449."""
+    baseline = num_tokens * num_head_groups
+    if baseline == 0 or baseline * 4 >= sm_count:
+        return 1
+    n = max(1, index_topk // 128)
+    ideal = 1 if n <= 1 else 1 << (n - 1).bit_length()
+    max_splits = max(1, sm_count // baseline)
+    max_splits = 1 << (max_splits.bit_length() - 1)
+    s = min(ideal, max_splits)
+    while s > 1 and index_topk % s != 0:
+        s //= 2
+    return max(1, s)
+
+
+def mla_sparse_attention(q, rows, indices, sm_scale, threads=None):
+    """FP32 sparse attention over the dequantised cache.
+
+    The exact-arithmetic statement of kernels/titan_mla.py:59-255 and :357-429:
+    for each token t and head h, softmax over the valid top-k rows r
+    (0 <= r < seq_kv) of (q[t,h] . k_r) * sm_scale, where k_r = int8_r * scale_r,
+    then the softmax-weighted sum of the same k_r (NoPE: V = K).  A token with
+    no valid row gives zeros (kernels/titan_mla.py:246, :421).  Duplicate
+    indices count once per occurrence, as in the reference gather.
+
+    q: [T, H, 512] (torch, any float dtype); rows: uint8/int8 [seq_kv, 528]
+    (numpy or torch); indices: [T, topk] or [T, 1, topk] integer.  Returns
+    torch.float32 [T, H, 512] on the CPU.
+    """
+    if threads is not None:
+        torch.set_num_threads(threads)
+    rows_t = torch.as_tensor(np.ascontiguousarray(np.asarray(
+        rows.cpu().numpy() if isinstance(rows, torch.Tensor) else rows).view(np.uint8).reshape(-1, ROW_BYTES)))
+    seq_kv = rows_t.shape[0]
+    qf = q.detach().cpu().float()
+    idx = torch.as_tensor(indices).cpu().reshape(qf.shape[0], -1).long()
+    T, H, _ = qf.shape
+    out = torch.zeros(T, H, LATENT_DIM, dtype=torch.float32)
+    for t in range(T):
+        valid = (idx[t] >= 0) & (idx[t] < seq_kv)
+        r = idx[t][valid]
+        if r.numel() == 0:
+            continue
+        sel = rows_t[r]
+        k = sel[:, :LATENT_DIM].view(torch.int8).float() * sel[:, LATENT_DIM:LATENT_DIM + 4].contiguous().view(torch.float32)
+        logits = (qf[t] @ k.T) * sm_scale
+        out[t] = torch.softmax(logits, dim=-1) @ k
+    return out
+
+
+def mla_reference_test_metrics(out, q, original_bf16, indices, seq_kv, sm_scale):
+    """The reference test's own numerical criteria (tests/verify_mla.py:79-90):
+    FP32 softmax attention over the ORIGINAL bf16 latents; returns (nmse, cosine)."""
+    qf = q.detach().cpu().float()
+    idx = torch.as_tensor(indices).cpu().reshape(qf.shape[0], -1).long()
+    valid = (idx >= 0) & (idx < seq_kv)
+    chosen = original_bf16.detach().cpu().float()[idx.clamp(0, seq_kv - 1)]
+    chosen.masked_fill_(~valid[:, :, None], 0)
+    logits = torch.bmm(qf, chosen.transpose(1, 2)) * sm_scale
+    logits.masked_fill_(~valid[:, None, :], -float("inf"))
+    ref = torch.bmm(torch.nan_to_num(logits.softmax(-1), nan=0.0), chosen)
+    o = out.detach().cpu().float()
+    nmse = ((o - ref).square().sum() / ref.square().sum().clamp_min(1e-30)).item()
+    cos = torch.nn.functional.cosine_similarity(o.flatten(), ref.flatten(), dim=0).item()
+    return nmse, cos
+
+
+def mla_algorithmic_bytes(indices, seq_kv, num_heads):
+    """Bytes one call must move: valid gathered rows x 528 + the int32 indices
+    + q and out (bf16), counted per token (duplicates count each time)."""
+    idx = np.asarray(torch.as_tensor(indices).cpu()).reshape(np.shape(indices)[0], -1)
+    n_valid = int(((idx >= 0) & (idx < seq_kv)).sum())
+    T, topk = idx.shape
+    return n_valid * ROW_BYTES + T * topk * 4 + 2 * T * num_heads * LATENT_DIM * 2
+
+
+# --------------------------------------------------------------- MoE align
+def moe_align_small(routes):
+    """Stable expert-sorted layout of benchmarks/moe_align.py:23-31, vectorised.
+
+    routes: flat integer sequence of R = 8B expert ids.  Returns
+    (sorted_ids int32 [8R], expert_ids int32 [R], postpad int32 [1]).
+    Padding entries of sorted_ids hold R; unused expert blocks hold -1;
+    ids outside [0, 288) are ignored (kernels/titan_moe_align.py:17-46).
+    """
+    flat = np.asarray(routes, dtype=np.int64).reshape(-1)
+    R = flat.size
+    valid = (flat >= 0) & (flat < NUM_EXPERTS)
+    e = np.where(valid, flat, NUM_EXPERTS)
+    counts = np.bincount(e, minlength=NUM_EXPERTS + 1)[:NUM_EXPERTS]
+    padded = (counts + 7) // 8 * 8
+    offsets = np.cumsum(padded) - padded
+    order = np.argsort(e, kind="stable")
+    sorted_ids = np.full(R * 8, R, dtype=np.int32)
+    expert_ids = np.full(R, -1, dtype=np.int32)
+    rank_in_expert = np.zeros(R, dtype=np.int64)
+    seen = np.zeros(NUM_EXPERTS + 1, dtype=np.int64)
+    for j in order:  # stable: original route order within an expert
+        rank_in_expert[j] = seen[e[j]]
+        seen[e[j]] += 1
+    for j in np.nonzero(valid)[0]:
+        sorted_ids[offsets[e[j]] + rank_in_expert[j]] = j
+    for ex in np.nonzero(counts)[0]:
+        expert_ids[offsets[ex] // 8: offsets[ex] // 8 + padded[ex] // 8] = ex
+    return sorted_ids, expert_ids, np.array([padded.sum()], dtype=np.int32)
+
+
+def moe_align_small_loops(flat):
+    """Pure-Python restatement of benchmarks/moe_align.py:23-31 (small cases)."""
+    count = len(flat)
+    output, experts = [], []
+    for expert in range(NUM_EXPERTS):
+        members = [i for i, value in enumerate(flat) if value == expert]
+        padded = (len(members) + 7) // 8 * 8
+        output.extend(members + [count] * (padded - len(members)))
+        experts.extend([expert] * (padded // 8))
+    postpad = len(output)
+    return (output + [count] * (count * 8 - len(output)),
+            experts + [-1] * (count - len(experts)), [postpad])

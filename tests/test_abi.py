@@ -1,0 +1,51 @@
+# SPDX-License-Identifier: Apache-2.0
+"""The C-ABI library loads and exports every entry point include/titan_b200.h
+declares; host-side validation answers without a GPU."""
+import ctypes
+import re
+from pathlib import Path
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "titan_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(titan_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_path():
+    names = declared_functions()
+    for want in ("titan_store_int8", "titan_mla_sparse_attention", "titan_mla_workspace_bytes",
+                 "titan_moe_align_small", "titan_last_error", "titan_abi_version", "titan_device_error"):
+        assert want in names
+
+
+def test_every_declared_symbol_is_exported(native_lib):
+    for name in declared_functions():
+        assert hasattr(native_lib, name), name
+
+
+def test_python_binding_covers_header(native_lib):
+    from kernels import titan_native
+    assert set(titan_native.SIGNATURES) >= set(declared_functions())
+
+
+def test_version_and_workspace(native_lib):
+    assert native_lib.titan_abi_version() == 100
+    assert native_lib.titan_mla_workspace_bytes(1, 16, 1) == 0
+    # [T][S][Hp][512] fp32 partials + [T][S][Hp] fp32 LSE rounded up to 256 B
+    assert native_lib.titan_mla_workspace_bytes(1, 16, 32) == 32 * 16 * 512 * 4 + 2048
+    assert native_lib.titan_mla_workspace_bytes(2, 20, 4) == 2 * 4 * 32 * 512 * 4 + 1024
+
+
+def test_invalid_arguments_rejected_on_host(native_lib):
+    rc = native_lib.titan_moe_align_small(None, 0, 7, None, None, None, 1, None)
+    assert rc == 1 and b"num_routes" in native_lib.titan_last_error()
+    rc = native_lib.titan_moe_align_small(None, 0, 16, None, None, None, 3, None)
+    assert rc == 1 and b"num_warps" in native_lib.titan_last_error()
+    rc = native_lib.titan_mla_sparse_attention(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, 1, 16,
+                                               ctypes.c_float(0.1), 0, None, 0, None)
+    assert rc == 1
+    rc = native_lib.titan_store_int8(None, 512, None, 1, 256, 0, 0, None, 1, -1, None)
+    assert rc == 1
+    assert native_lib.titan_store_int8(None, 512, None, 1, 256, 0, 0, None, 1, 0, None) == 0  # nothing to do

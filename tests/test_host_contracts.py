@@ -1,0 +1,111 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Host-side contract of the drop-in modules: import behaviour, argument
+validation and exception types, the split heuristic.  No GPU, no kernel call."""
+import importlib.util
+import itertools
+import sys
+import types
+from pathlib import Path
+from unittest.mock import patch
+
+import pytest
+import torch
+
+from oracle import oracle as O
+
+PKG = Path(__file__).resolve().parents[1] / "glm-5.3-kernels_b200" / "kernels"
+
+
+def _load(name, path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_import_does_not_touch_cuda_or_library():
+    """Like tests/test_cpu_contracts.py:33-53: executing the modules with a torch
+    double whose torch.cuda raises on any attribute must succeed."""
+    fake_torch = types.ModuleType("torch")
+    fake_torch.Tensor = object
+
+    class NoCUDA:
+        def __getattr__(self, name):
+            raise AssertionError(f"import-time torch.cuda access: {name}")
+
+    fake_torch.cuda = NoCUDA()
+    with patch.dict(sys.modules, {"torch": fake_torch}):
+        sys.modules.pop("titan_native", None)
+        native = _load("titan_native", PKG / "titan_native.py")
+        assert native._lib is None
+        with patch.dict(sys.modules, {"titan_native": native}):
+            for filename, exported in (("titan_kv.py", "store_int8"),
+                                       ("titan_mla.py", "triton_mla_sparse_attention"),
+                                       ("titan_moe_align.py", "titan_moe_align_small")):
+                mod = _load("isolated_" + filename[:-3], PKG / filename)
+                assert callable(getattr(mod, exported))
+        assert native._lib is None, "importing must not load the library"
+
+
+def test_no_triton_or_vllm_imports():
+    import re
+    for f in PKG.glob("*.py"):
+        text = f.read_text()
+        assert not re.search(r"^\s*(import|from)\s+(triton|vllm)\b", text, re.M), f
+
+
+def test_split_heuristic_matches_restatement():
+    from kernels.titan_mla import _choose_num_kv_splits
+    for T, G, topk, sms in itertools.product((0, 1, 2, 3, 5, 8, 16, 37, 64), (1, 2, 3), (0, 32, 128, 256, 2176, 2048, 96),
+                                             (70, 132, 148, 160)):
+        assert _choose_num_kv_splits(T, G, topk, sms) == O.choose_num_kv_splits(T, G, topk, sms), (T, G, topk, sms)
+
+
+def test_moe_argument_errors_are_value_errors():
+    from kernels.titan_moe_align import titan_moe_align_small
+    ok = torch.zeros(2, 8, dtype=torch.int32)
+    with pytest.raises(ValueError):
+        titan_moe_align_small(torch.zeros(9, 8, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        titan_moe_align_small(torch.zeros(2, 4, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        titan_moe_align_small(ok, block_size=16)
+    with pytest.raises(ValueError):
+        titan_moe_align_small(ok, num_experts=256)
+    with pytest.raises(ValueError):
+        titan_moe_align_small(ok, expert_map=torch.arange(288))
+    with pytest.raises(ValueError):
+        titan_moe_align_small(ok, ignore_invalid_experts=False)
+    with pytest.raises(ValueError):  # CPU tensor: no CPU fallback
+        titan_moe_align_small(ok)
+
+
+def test_mla_argument_errors_are_assertions():
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    q = torch.zeros(1, 16, 512, dtype=torch.bfloat16)
+    kv = torch.zeros(64, 1, 528, dtype=torch.int8)
+    idx = torch.zeros(1, 1, 64, dtype=torch.int32)
+    with pytest.raises(AssertionError):
+        attn(torch.zeros(1, 16, 320, dtype=torch.bfloat16), kv, idx, 0.1)      # dim_qk
+    with pytest.raises(AssertionError):
+        attn(q, torch.zeros(64, 2, 528, dtype=torch.int8), idx, 0.1)           # kv heads
+    with pytest.raises(AssertionError):
+        attn(q, kv, torch.zeros(1, 1, 48, dtype=torch.int32), 0.1)             # topk % 32
+    with pytest.raises(AssertionError):
+        attn(torch.zeros(1, 16, 576, dtype=torch.bfloat16), torch.zeros(64, 1, 528, dtype=torch.int8), idx, 0.1)
+    with pytest.raises(AssertionError):
+        attn(q, kv, idx, 0.1)                                                    # CPU tensors
+
+
+def test_kv_argument_errors_are_assertions():
+    from kernels.titan_kv import store_int8
+    x = torch.zeros(4, 512, dtype=torch.bfloat16)
+    cache = torch.zeros(1, 8, 528, dtype=torch.int8)
+    with pytest.raises(AssertionError):
+        store_int8(torch.zeros(4, 256, dtype=torch.bfloat16), cache, torch.arange(4))
+    with pytest.raises(AssertionError):
+        store_int8(x, torch.zeros(1, 8, 512, dtype=torch.int8), torch.arange(4))
+    with pytest.raises(AssertionError):
+        store_int8(x, cache, torch.arange(5))
+    with pytest.raises(AssertionError):
+        store_int8(x, cache, torch.arange(4))                                    # CPU tensors

@@ -1,0 +1,124 @@
+# SPDX-License-Identifier: Apache-2.0
+"""The CPU oracle against golden vectors produced by the reference's own code
+(tests/golden/make_golden.py).  No GPU."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import c_oracle
+from oracle import oracle as O
+from tests.golden import cases as C
+
+GOLDEN = C.__file__.rsplit("/", 1)[0]
+
+
+@pytest.fixture(scope="module")
+def kv_golden():
+    return np.load(f"{GOLDEN}/kv_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def moe_golden():
+    return np.load(f"{GOLDEN}/moe_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def mla_golden():
+    return np.load(f"{GOLDEN}/mla_golden.npz")
+
+
+def test_kv_inputs_regenerate(kv_golden):
+    assert np.array_equal(O.tensor_bf16_bits(C.kv_latents()), kv_golden["x_bits"])
+    assert np.array_equal(C.kv_slots().numpy(), kv_golden["slots"])
+
+
+def test_kv_oracle_numpy_bit_exact(kv_golden):
+    cache = np.zeros((C.KV_BLOCKS, C.KV_BLOCK_SIZE, 528), np.uint8)
+    O.store_int8(kv_golden["x_bits"], cache, kv_golden["slots"])
+    assert np.array_equal(cache, kv_golden["cache"])
+
+
+def test_kv_oracle_c_bit_exact(kv_golden):
+    bits = np.ascontiguousarray(kv_golden["x_bits"])
+    rows = np.zeros((bits.shape[0], 528), np.uint8)
+    c_oracle().oracle_store_int8_rows(bits.ctypes.data, bits.shape[0], rows.ctypes.data)
+    flat = kv_golden["cache"].reshape(-1, 528)
+    slots = kv_golden["slots"]
+    keep = slots >= 0
+    assert np.array_equal(rows[keep], flat[slots[keep]])
+    # rows with a negative slot never reach the cache; untouched rows stay zero
+    touched = np.zeros(flat.shape[0], bool)
+    touched[slots[keep]] = True
+    assert not flat[~touched].any()
+
+
+def test_kv_reference_quantisation_criteria(kv_golden):
+    """tests/verify_mla.py:50-66 criteria hold for the oracle's bytes."""
+    x = O.bf16_bits_to_f32(kv_golden["x_bits"])
+    rows = O.store_int8_rows(kv_golden["x_bits"])
+    scales = rows[:, 512:516].copy().view(np.float32)[:, 0]
+    finite = np.isfinite(x).all(1)
+    expected = np.maximum(np.abs(x).max(1), 127e-12) / 127
+    np.testing.assert_allclose(scales[finite], expected[finite].astype(np.float32), rtol=1e-6, atol=1e-12)
+    ints = rows[:, :512].view(np.int8).astype(np.float32)
+    assert np.abs(ints - np.clip(np.round(x / scales[:, None]), -127, 127)).max() <= 1
+    assert not rows[:, 516:].any()
+
+
+def _moe_cases(golden):
+    for i in range(len(golden["batch"])):
+        R = int(golden["batch"][i]) * 8
+        yield (golden["routes"][i][:R], golden["sorted_ids"][i][:8 * R], golden["expert_ids"][i][:R],
+               int(golden["postpad"][i]))
+
+
+def test_moe_golden_case_count(moe_golden):
+    assert len(moe_golden["batch"]) == 856          # tests/test_cpu_contracts.py:26
+    assert int(moe_golden["interp_kernel_cases"]) == 112
+
+
+def test_moe_oracle_vectorised_bit_exact(moe_golden):
+    for routes, s, e, p in _moe_cases(moe_golden):
+        so, eo, po = O.moe_align_small(routes)
+        assert np.array_equal(so, s) and np.array_equal(eo, e) and po[0] == p
+
+
+def test_moe_oracle_loops_bit_exact(moe_golden):
+    for routes, s, e, p in _moe_cases(moe_golden):
+        so, eo, po = O.moe_align_small_loops(routes.tolist())
+        assert so == s.tolist() and eo == e.tolist() and po == [p]
+
+
+def test_moe_oracle_c_bit_exact(moe_golden):
+    lib = c_oracle()
+    for routes, s, e, p in _moe_cases(moe_golden):
+        ids = np.ascontiguousarray(routes, dtype=np.int64)
+        R = ids.size
+        so = np.empty(8 * R, np.int32)
+        eo = np.empty(R, np.int32)
+        po = np.empty(1, np.int32)
+        assert lib.oracle_moe_align_small(ids.ctypes.data, R, so.ctypes.data, eo.ctypes.data, po.ctypes.data) == 0
+        assert np.array_equal(so, s) and np.array_equal(eo, e) and po[0] == p
+
+
+@pytest.mark.parametrize("case", C.MLA_CASES, ids=lambda c: c.name)
+def test_mla_oracle_vs_reference_golden(case, mla_golden):
+    inp = C.mla_inputs(case)
+    assert bytes(mla_golden[f"{case.name}__input_sha256"]).hex() == C.mla_input_digest(inp)
+    rows = O.store_int8_rows(O.tensor_bf16_bits(inp["latent"]))
+    ref = O.mla_sparse_attention(inp["q"], rows, inp["indices"], case.sm_scale)
+    for s in case.splits:
+        gold = torch.from_numpy(O.bf16_bits_to_f32(mla_golden[f"{case.name}__s{s}"]).reshape(ref.shape))
+        # Path tolerance: |a - b| <= 2e-2 + 1e-2 |b|.
+        assert bool(((gold - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()), (case.name, s)
+        if case.pattern == "all_neg":
+            assert not gold.any()
+
+
+def test_split_heuristic_restatement_table():
+    """oracle.choose_num_kv_splits on the survey's worked cases (titan_mla.py:441-449)."""
+    assert O.choose_num_kv_splits(1, 1, 2176, 70) == 32
+    assert O.choose_num_kv_splits(1, 1, 2176, 148) == 32
+    assert O.choose_num_kv_splits(8, 1, 2176, 148) == 16
+    assert O.choose_num_kv_splits(37, 1, 2176, 148) == 1
+    assert O.choose_num_kv_splits(0, 1, 2176, 148) == 1
