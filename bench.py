@@ -1,0 +1,527 @@
+#!/usr/bin/env python3
+# SPDX-License-Identifier: Apache-2.0
+"""Benchmark of the GLM-5.3 sparse-MLA decode path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (one JSON line on rank 0): BASELINE config 2 — B=1 decode, 16 heads,
+262,144-row INT8 cache (1024 blocks x 256 x 528 B) filled by store_int8,
+2176 indices per token (2048 distinct valid + 128 x -1), sm_scale 512^-0.5.
+A step is one call of triton_mla_sparse_attention on one index set.  `value`
+is device time per call (CUDA events around a CUDA-graph replay of the call,
+L2 flushed by a 256 MiB write before every timed call), whole-job: per-rank
+mean, max over ranks, divided by the number of ranks (each rank serves its own
+independent B=1 requests; the path needs no collective).  `e2e` is the same
+call through the public API with inputs copied from pinned host memory and
+the output copied back inside the timed region.
+
+Secondary measurements ride along in "secondary": store_int8 cache fill
+(config 2 fill, 408.9 MB), B=8 decode sharded over ranks (config 3),
+prefill-shaped T=4096 (config 4, sharded over ranks) and MoE align B1/2/4/8
+(config 5).
+
+--impl reference times the reference algorithm's CPU restatement (oracle/,
+the only CPU implementation of this path; the reference ships Triton GPU
+kernels only) on the host cores for the same config and metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "glm-5.3-kernels_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "sparse MLA decode µs/call + achieved HBM GB/s vs peak at 1/2/4/8 B200"
+UNIT = "us/call"
+KV_ROWS = 262144
+BLOCK = 256
+TOPK = 2176
+VALID = 2048
+HEADS = 16
+SM_SCALE = 512 ** -0.5
+ROW_BYTES = 528
+FLUSH_BYTES = 256 << 20
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ------------------------------------------------------------------ plumbing
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+class Dist:
+    """torch.distributed for barriers and max-over-ranks timing only."""
+
+    def __init__(self, world, rank, local_rank):
+        self.world, self.rank, self.local_rank = world, rank, local_rank
+        self.pg = None
+        if world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            self.pg.barrier(device_ids=[self.local_rank])
+
+    def max(self, value):
+        if self.pg is None:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=torch.device("cuda", self.local_rank))
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) from
+    the committed ncu summary profiles/<name>.md, line `traffic_bytes_per_launch: N`."""
+    path = ROOT / "profiles" / f"{name}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed work runs."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.uuid = str(getattr(torch.cuda.get_device_properties(device), "uuid", ""))
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) != 9:
+                    continue
+                if self.uuid and self.uuid not in parts[0] and parts[0] not in self.uuid:
+                    continue
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        busy = [s for s in sm if s > 0]
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+class Flusher:
+    """Writes a buffer larger than L2 (126 MB) so every timed call starts cold."""
+
+    def __init__(self, device):
+        self.buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def capture(fn):
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # warm (and first-call setup) outside capture
+        with torch.cuda.graph(graph, stream=s):
+            out = fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    return graph, out
+
+
+def timed_cold(step, n, flush, before=None):
+    """n steps; each step: before(k) (untimed), L2 flush (untimed), then events
+    around step(k).  Returns per-step device milliseconds."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for k in range(n):
+        if before is not None:
+            before(k)
+        flush()
+        evs[k][0].record()
+        step(k)
+        evs[k][1].record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+# --------------------------------------------------------------- workloads
+def latents(n, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randn(n, 512, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+
+
+def decode_sets(batch, sets, seed, kv_rows=KV_ROWS, tail_mode="fixed"):
+    """CPU tensors: q [sets, batch, 16, 512] bf16 and indices [sets, batch, 1, 2176] int32."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(sets, batch, HEADS, 512, generator=g).to(torch.bfloat16)
+    idx = torch.full((sets, batch, 1, TOPK), -1, dtype=torch.int32)
+    for s in range(sets):
+        for b in range(batch):
+            if tail_mode == "fixed":   # config 2: 2048 distinct + 128 x -1
+                idx[s, b, 0, :VALID] = torch.randperm(kv_rows, generator=g)[:VALID].to(torch.int32)
+            else:                      # config 3: uniform with a random 0..256 tail of -1
+                tail = int(torch.randint(0, 257, (1,), generator=g))
+                idx[s, b, 0, :TOPK - tail] = torch.randint(0, kv_rows, (TOPK - tail,), generator=g,
+                                                           dtype=torch.int32)
+    return q, idx
+
+
+def prefill_indices(tokens, seed, t0=0):
+    """Config 4: token t draws min(t+1, 2176) + 65536 * (t // 1024) candidates
+    without replacement, padded to 2176 with -1."""
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.full((tokens, 1, TOPK), -1, dtype=torch.int32)
+    for i in range(tokens):
+        t = t0 + i
+        pool = min(t + 1, TOPK) + 65536 * (t // 1024)
+        k = min(pool, TOPK)
+        idx[i, 0, :k] = torch.randperm(pool, generator=g)[:k].to(torch.int32)
+    return idx
+
+
+def alg_bytes(idx_cpu):
+    i = idx_cpu.reshape(idx_cpu.shape[0], -1)
+    n_valid = int(((i >= 0) & (i < KV_ROWS)).sum())
+    return n_valid * ROW_BYTES + i.numel() * 4 + 2 * i.shape[0] * HEADS * 512 * 2
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, dist):
+    from kernels import titan_native
+    from kernels.titan_kv import store_int8
+    from kernels.titan_mla import _choose_num_kv_splits, triton_mla_sparse_attention as attn
+    from kernels.titan_moe_align import titan_moe_align_small
+
+    rank, world = dist.rank, dist.world
+    dev = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    peak, peak_kind = measured_peaks()
+    flush = Flusher(dev)
+    K, W = args.steps, args.warmup
+    sampler = ClockSampler(dev)
+
+    # ---- cache: config 2 fill by store_int8 (identical replica on every rank)
+    lat = latents(KV_ROWS, 1234, dev)
+    cache = torch.zeros(KV_ROWS // BLOCK, BLOCK, ROW_BYTES, dtype=torch.int8, device=dev)
+    slots = torch.arange(KV_ROWS, device=dev)
+    kv = cache.view(KV_ROWS, 1, ROW_BYTES)
+    store_int8(lat, cache, slots)
+    torch.cuda.synchronize()
+
+    sampler.start()
+    dist.barrier()
+    # ---- headline: B=1 decode, CUDA-graph replay, cold L2
+    sets = args.index_sets
+    q_sets, idx_sets = decode_sets(1, sets, 99 + rank)
+    q_dev, idx_dev = q_sets.to(dev), idx_sets.to(dev)
+    q_static = q_dev[0].clone()
+    idx_static = idx_dev[0].clone()
+    splits = _choose_num_kv_splits(1, 1, TOPK, sms)
+    graph, _ = capture(lambda: attn(q_static, kv, idx_static, SM_SCALE, sm_count=sms))
+
+    def load(k):
+        q_static.copy_(q_dev[k % sets])
+        idx_static.copy_(idx_dev[k % sets])
+
+    timed_cold(lambda k: graph.replay(), W, flush, load)
+    dist.barrier()
+    ms = timed_cold(lambda k: graph.replay(), K, flush, load)
+    dist.barrier()
+    mean_ms = statistics.fmean(ms)
+    rank_max_ms = dist.max(mean_ms)
+    value_us = rank_max_ms * 1000.0 / world
+    bytes_per_call = statistics.fmean(alg_bytes(idx_sets[k % sets]) for k in range(sets))
+    achieved = bytes_per_call / (mean_ms * 1e-3) / 1e9
+    achieved = dist.max(-achieved) * -1.0  # slowest rank's bandwidth
+    launches_per_call = 1 if splits == 1 else 2
+
+    # ---- e2e: public API, pinned host inputs and output inside the timed region
+    q_host = q_sets.pin_memory()
+    idx_host = idx_sets.pin_memory()
+    out_host = torch.empty((sets, 1, HEADS, 512), dtype=torch.bfloat16).pin_memory()
+    qd = torch.empty_like(q_dev[0])
+    idd = torch.empty_like(idx_dev[0])
+
+    def e2e_step(k):
+        qd.copy_(q_host[k % sets], non_blocking=True)
+        idd.copy_(idx_host[k % sets], non_blocking=True)
+        o = attn(qd, kv, idd, SM_SCALE, sm_count=sms)
+        out_host[k % sets].copy_(o, non_blocking=True)
+
+    timed_cold(e2e_step, W, flush)
+    dist.barrier()
+    e2e_ms = timed_cold(e2e_step, K, flush)
+    dist.barrier()
+    e2e_us = dist.max(statistics.fmean(e2e_ms)) * 1000.0 / world
+    graph.reset()
+
+    secondary = {}
+    # ---- store_int8: config 2 fill, 262,144 rows
+    fill_bytes = KV_ROWS * (1024 + ROW_BYTES + 8)
+    st_ms = timed_cold(lambda k: store_int8(lat, cache, slots), max(3, min(K, 20)), flush)
+    st_mean = dist.max(statistics.fmean(st_ms))
+    st_gbs = fill_bytes / (st_mean * 1e-3) / 1e9
+    perm = torch.randperm(KV_ROWS, device=dev)
+    stp_ms = timed_cold(lambda k: store_int8(lat, cache, perm), max(3, min(K, 20)), flush)
+    stp_mean = dist.max(statistics.fmean(stp_ms))
+    secondary["store_int8"] = {
+        "rows": KV_ROWS, "bytes": fill_bytes, "us": st_mean * 1000, "GBps": st_gbs,
+        "frac_of_hbm": st_gbs / peak, "random_perm_us": stp_mean * 1000,
+        "random_perm_GBps": fill_bytes / (stp_mean * 1e-3) / 1e9, "per_rank": True}
+    store_int8(lat, cache, slots)  # restore the arange layout
+
+    # ---- config 3: B=8 decode, tokens sharded contiguously over ranks
+    per = max(1, 8 // world)
+    q8, i8 = decode_sets(8, 8, 777, tail_mode="random")
+    lo = min(rank * per, 8 - per)
+    q8d, i8d = q8[:, lo:lo + per].contiguous().to(dev), i8[:, lo:lo + per].contiguous().to(dev)
+    q8s, i8s = q8d[0].clone(), i8d[0].clone()
+    g8, _ = capture(lambda: attn(q8s, kv, i8s, SM_SCALE, sm_count=sms))
+
+    def load8(k):
+        q8s.copy_(q8d[k % 8])
+        i8s.copy_(i8d[k % 8])
+
+    timed_cold(lambda k: g8.replay(), W, flush, load8)
+    dist.barrier()
+    b8_ms = dist.max(statistics.fmean(timed_cold(lambda k: g8.replay(), K, flush, load8)))
+    b8_bytes = statistics.fmean(alg_bytes(i8[k % 8, lo:lo + per]) for k in range(8))
+    secondary["decode_b8"] = {
+        "tokens_per_rank": per, "us_per_call": b8_ms * 1000, "tokens_per_s": per * world / (b8_ms * 1e-3),
+        "GBps_per_rank": b8_bytes / (b8_ms * 1e-3) / 1e9,
+        "splits": _choose_num_kv_splits(per, 1, TOPK, sms)}
+    g8.reset()
+
+    # ---- config 4: prefill-shaped, T=4096 tokens sharded over ranks
+    if not args.skip_prefill:
+        tp = 4096 // world
+        t0 = rank * tp
+        ip = prefill_indices(tp, 4242 + rank, t0=t0).to(dev)
+        qp = torch.randn(tp, HEADS, 512, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(
+            torch.bfloat16)
+        npf = max(3, min(K, 10))
+        timed_cold(lambda k: attn(qp, kv, ip, SM_SCALE, sm_count=sms), 2, flush)
+        pf_ms = dist.max(statistics.fmean(timed_cold(lambda k: attn(qp, kv, ip, SM_SCALE, sm_count=sms), npf,
+                                                     flush)))
+        nvalid = int(((ip >= 0) & (ip < KV_ROWS)).sum())
+        secondary["prefill_t4096"] = {
+            "tokens_per_rank": tp, "ms_per_call": pf_ms, "gathered_GBps": nvalid * ROW_BYTES / (pf_ms * 1e-3) / 1e9,
+            "tflops": nvalid * 4 * HEADS * 512 / (pf_ms * 1e-3) / 1e12, "tokens_per_s": tp * world / (pf_ms * 1e-3)}
+
+    # ---- config 5: MoE align, graph replay x100 (reference methodology)
+    moe = {}
+    gm = torch.Generator().manual_seed(37)
+    for B in (1, 2, 4, 8):
+        ids = torch.stack([torch.randperm(288, generator=gm)[:8] for _ in range(B)]).to(torch.int32).to(dev)
+        gr, _ = capture(lambda: titan_moe_align_small(ids))
+        for _ in range(5):
+            gr.replay()
+        samples = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(100):
+                gr.replay()
+            b.record()
+            torch.cuda.synchronize()
+            samples.append(a.elapsed_time(b) * 1000 / 100)
+        moe[f"B{B}_us"] = statistics.median(samples)
+        gr.reset()
+    secondary["moe_align_graph_replay"] = moe
+    clocks = sampler.stop()
+    dist.barrier()
+
+    err = titan_native.device_error(cache)
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+        cpu = cpu_baseline_b1(cache, q_sets, idx_sets, args.cpu_seconds)
+
+    if rank == 0:
+        traffic = profile_traffic("mla_decode_b1")
+        line = {
+            "metric": METRIC, "value": value_us, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": rank_max_ms, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": "config2: B=1 sparse MLA decode, 16 heads x 512 NoPE latent, 262144-row INT8 "
+                            "528-B-row cache filled by store_int8, 2176 indices (2048 distinct valid + 128 x -1)",
+                "kv_rows": KV_ROWS, "heads": HEADS, "topk": TOPK, "valid_per_token": VALID,
+                "index_sets": sets, "num_kv_splits": splits, "sm_count": sms,
+                "l2": "flushed (256 MiB write) before every timed call",
+                "timing": "CUDA graph replay of one call, CUDA events per call, mean over steps, max over ranks",
+                "parallelism": f"replicas x{world} (independent B=1 requests per GPU, no collective)"},
+            "per_gpu_us_per_call": rank_max_ms * 1000.0,
+            "tokens_per_s": world / (rank_max_ms * 1e-3),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_call": bytes_per_call,
+                         "kernel": "sparse_mla_kernel<split> + combine (whole call)"},
+            "e2e": {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": q_dev[0].numel() * 2 + idx_dev[0].numel() * 4,
+                    "d2h_bytes_per_step": HEADS * 512 * 2},
+            "gpu_launches": K * launches_per_call,
+            "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"],
+                       "samples": clocks["samples"]},
+            "secondary": secondary,
+            "device_error_word": err,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_b1(cache, q_sets, idx_sets, seconds):
+    """The oracle (CPU restatement of the reference algorithm) on the same B=1
+    workload, all host threads, bounded to ~`seconds` of work."""
+    from oracle import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = cache.view(KV_ROWS, ROW_BYTES).cpu()
+    sets = q_sets.shape[0]
+    O.mla_sparse_attention(q_sets[0], rows, idx_sets[0], SM_SCALE)  # warm
+    n, t0 = 0, time.perf_counter()
+    while n < 3 or (time.perf_counter() - t0 < seconds and n < 100000):
+        O.mla_sparse_attention(q_sets[n % sets], rows, idx_sets[n % sets], SM_SCALE)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": dt / n * 1e6, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} B=1 calls of oracle.mla_sparse_attention over the 262144-row cache "
+                      f"({dt:.1f} s, torch CPU fp32)"}
+
+
+# ------------------------------------------------------------ reference arm
+def run_reference(args):
+    """CPU restatement of the reference algorithm (oracle/) on the host cores:
+    the cache is filled by the oracle's store_int8 (C restatement) from the
+    same-shape latents, then K B=1 calls are timed."""
+    import numpy as np
+    from oracle import c_oracle
+    from oracle import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(1234)
+    lat = torch.randn(KV_ROWS, 512, generator=g).to(torch.bfloat16)
+    bits = np.ascontiguousarray(O.tensor_bf16_bits(lat))
+    rows = np.zeros((KV_ROWS, ROW_BYTES), np.uint8)
+    t0 = time.perf_counter()
+    c_oracle().oracle_store_int8_rows(bits.ctypes.data, KV_ROWS, rows.ctypes.data)
+    fill_s = time.perf_counter() - t0
+    rows_t = torch.from_numpy(rows)
+    q_sets, idx_sets = decode_sets(1, args.index_sets, 99)
+    sets = q_sets.shape[0]
+    for k in range(args.warmup):
+        O.mla_sparse_attention(q_sets[k % sets], rows_t, idx_sets[k % sets], SM_SCALE)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        O.mla_sparse_attention(q_sets[k % sets], rows_t, idx_sets[k % sets], SM_SCALE)
+    dt = time.perf_counter() - t0
+    us = dt / args.steps * 1e6
+    cores = torch.get_num_threads()
+    line = {
+        "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": us / 1000, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config2: B=1 sparse MLA decode, 16 heads, 262144-row INT8 cache, 2176 indices "
+                               "(2048 valid)", "index_sets": sets},
+        "cpu_baseline": {"value": us, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} B=1 calls of the CPU restatement (torch fp32); cache fill by the "
+                                   f"C restatement of store_int8 took {fill_s:.2f} s single-threaded"},
+        "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=None)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--index-sets", type=int, default=64)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-prefill", action="store_true")
+    ap.add_argument("--skip-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world, local_rank = env_rank()
+    if args.gpus is None:
+        args.gpus = world
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return 0
+    dist = Dist(world, rank, local_rank)
+    try:
+        run_ours(args, dist)
+    finally:
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -67,8 +67,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait: gives up after ~`limit_cycles` SM clocks, records the failure
 // in the device error word and returns false.  Never traps, never spins forever.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
-                                                  long long limit_cycles = 2000000000LL) {
+// Bulk copies land in microseconds; the first wait of a CTA allows ~0.1 s, and
+// after one failure the caller switches to kShortWaitCycles so a CTA with a
+// lost copy finishes its remaining tiles quickly instead of stalling the grid.
+constexpr long long kLongWaitCycles = 200000000LL;
+constexpr long long kShortWaitCycles = 1000000LL;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, long long limit_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {

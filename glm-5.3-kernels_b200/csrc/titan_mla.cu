@@ -165,9 +165,12 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
   const int red_r0 = red_nt * 8 + row_perm(red_j & 7);
   const int red_r1 = red_nt * 8 + row_perm((red_j & 7) + 1);
 
+  bool lost_copy = false;  // a bounded wait gave up (error word set); keep going, short waits
   for (int i = 0; i < n_tiles; ++i) {
     const int stage = i % kStages;
-    mbar_wait_bounded(&sm.bar[stage], (uint32_t)((i / kStages) & 1));
+    if (!mbar_wait_bounded(&sm.bar[stage], (uint32_t)((i / kStages) & 1),
+                           lost_copy ? kShortWaitCycles : kLongWaitCycles))
+      lost_copy = true;
     const uint8_t *buf = sm.rows[stage];
 
     // ---- QK^T over this warp's 64 dims; keep the bf16 B fragments for PV.
@@ -411,7 +414,9 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
     return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: invalid sizes");
   if (num_tokens == 0) return TITAN_OK;
   if (num_kv_splits < 1) return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: num_kv_splits must be >= 1");
-  if (q == nullptr || kv == nullptr || indices == nullptr || out == nullptr)
+  // indices may be null only when there is nothing to read (topk == 0), kv
+  // only when no index can be valid (seq_kv == 0).
+  if (q == nullptr || out == nullptr || (indices == nullptr && topk > 0) || (kv == nullptr && seq_kv > 0))
     return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: null pointer");
   if ((uintptr_t)kv % 16 || kv_row_stride % 16)
     return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: kv base and row stride must be 16-byte aligned");

@@ -1,0 +1,119 @@
+# SPDX-License-Identifier: Apache-2.0
+"""INT8 KV writer on the GPU vs the CPU oracle: bit-exact bytes."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import c_oracle
+from oracle import oracle as O
+from tests.golden import cases as C
+
+pytestmark = pytest.mark.gpu
+GOLDEN = C.__file__.rsplit("/", 1)[0]
+
+
+def _c_rows(x_bf16):
+    bits = np.ascontiguousarray(O.tensor_bf16_bits(x_bf16))
+    rows = np.zeros((bits.shape[0], 528), np.uint8)
+    c_oracle().oracle_store_int8_rows(bits.ctypes.data, bits.shape[0], rows.ctypes.data)
+    return rows
+
+
+def test_golden_bytes(native_lib, cuda_device):
+    from kernels.titan_kv import store_int8
+    gold = np.load(f"{GOLDEN}/kv_golden.npz")
+    x = C.kv_latents().to(cuda_device)
+    for slot_dtype in (torch.int64, torch.int32):
+        cache = torch.zeros(C.KV_BLOCKS, C.KV_BLOCK_SIZE, 528, dtype=torch.int8, device=cuda_device)
+        store_int8(x, cache, C.kv_slots().to(slot_dtype).to(cuda_device))
+        assert np.array_equal(cache.cpu().numpy().view(np.uint8), gold["cache"]), slot_dtype
+
+
+def test_uint8_cache_and_unaligned_rows(native_lib, cuda_device):
+    """A uint8 cache and an x view whose rows are not 16-byte aligned (scalar kernel)."""
+    from kernels.titan_kv import store_int8
+    g = torch.Generator().manual_seed(3)
+    big = torch.randn(96, 520, generator=g).to(torch.bfloat16)
+    x_cpu = big[:, 3:515]
+    cache = torch.zeros(1, 128, 528, dtype=torch.uint8, device=cuda_device)
+    slots = torch.randperm(128, generator=g)[:96]
+    store_int8(big.to(cuda_device)[:, 3:515], cache, slots.to(cuda_device))
+    want = np.zeros((1, 128, 528), np.uint8)
+    O.store_int8(O.tensor_bf16_bits(x_cpu), want, slots.numpy())
+    assert np.array_equal(cache.cpu().numpy(), want)
+
+
+def test_negative_and_out_of_range_slots_leave_cache(native_lib, cuda_device):
+    """tests/verify_mla.py:67-69: a negative slot modifies nothing.  A slot past
+    the last block is skipped too."""
+    from kernels.titan_kv import store_int8
+    x = C.kv_latents()[:4].to(cuda_device)
+    cache = torch.full((2, 4, 528), 7, dtype=torch.int8, device=cuda_device)
+    before = cache.clone()
+    store_int8(x, cache, torch.tensor([-1, -5, 8, 1 << 40], device=cuda_device))
+    assert torch.equal(cache, before)
+    store_int8(x[:0], cache, torch.empty(0, dtype=torch.int64, device=cuda_device))
+    assert torch.equal(cache, before)
+
+
+def test_block_strided_cache(native_lib, cuda_device):
+    """Cache viewed out of a larger allocation: block stride != block_size * 528."""
+    from kernels.titan_kv import store_int8
+    x = C.kv_latents()[:64]
+    storage = torch.zeros(3, 40, 528, dtype=torch.int8, device=cuda_device)
+    cache = storage[:, 4:36]                       # [3, 32, 528], stride0 = 40 * 528
+    slots = torch.arange(64) * 3 % 96
+    store_int8(x.to(cuda_device), cache, slots.to(cuda_device))
+    want = np.zeros((3, 32, 528), np.uint8)
+    O.store_int8(O.tensor_bf16_bits(x), want, slots.numpy())
+    assert np.array_equal(cache.cpu().numpy().view(np.uint8), want)
+    assert not storage[:, :4].any() and not storage[:, 36:].any()
+
+
+@pytest.mark.parametrize("order", ["arange", "permutation"])
+def test_full_cache_fill_bit_exact(native_lib, cuda_device, order):
+    """BASELINE config 2 fill (262,144 rows) and config 4's random-permutation
+    store, byte for byte against the C oracle, plus the reference test's
+    quantisation criteria (tests/verify_mla.py:50-66)."""
+    from kernels.titan_kv import store_int8
+    n = 262144
+    g = torch.Generator().manual_seed(20260910)
+    x = torch.randn(n, 512, generator=g)
+    x[:, :128] *= 0.05
+    x[:, 256:384] *= 8
+    x = x.to(torch.bfloat16)
+    x[0] = 0
+    slots = torch.arange(n) if order == "arange" else torch.randperm(n, generator=g)
+    cache = torch.zeros(n // 256, 256, 528, dtype=torch.int8, device=cuda_device)
+    store_int8(x.to(cuda_device), cache, slots.to(cuda_device))
+    got = cache.cpu().numpy().view(np.uint8).reshape(n, 528)
+    rows = _c_rows(x)
+    assert np.array_equal(got[slots.numpy()], rows)
+    scales = rows[:, 512:516].copy().view(np.float32)[:, 0]
+    xf = x.float().numpy()
+    deq = (rows[:, :512].view(np.int8).astype(np.float32) * scales[:, None])
+    deq = torch.from_numpy(deq).to(torch.bfloat16).float().numpy()
+    nmse = float(((deq - xf) ** 2).sum() / (xf ** 2).sum())
+    assert nmse < 3e-4
+
+
+def test_graph_capture_replay(native_lib, cuda_device):
+    from kernels.titan_kv import store_int8
+    x = C.kv_latents().to(cuda_device)
+    slots = C.kv_slots().to(cuda_device)
+    cache = torch.zeros(C.KV_BLOCKS, C.KV_BLOCK_SIZE, 528, dtype=torch.int8, device=cuda_device)
+    store_int8(x, cache, slots)  # warm-up outside capture
+    want = cache.clone()
+    cache.zero_()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            store_int8(x, cache, slots)
+    torch.cuda.current_stream().wait_stream(s)
+    cache.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(cache, want)
+    graph.reset()

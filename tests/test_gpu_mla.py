@@ -1,0 +1,177 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Sparse MLA on the GPU vs the CPU oracle and the reference-generated goldens.
+
+Tolerance: |out - ref| <= 2e-2 + 1e-2 |ref| elementwise,
+ref = FP32 attention over the dequantised cache.  Plus the reference test's own
+criteria vs the original bf16 latents: NMSE < 1e-3, cosine > 0.999
+(tests/verify_mla.py:79-90), and exact zeros for a token with no valid index.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.golden import cases as C
+
+pytestmark = pytest.mark.gpu
+GOLDEN = C.__file__.rsplit("/", 1)[0]
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def within(out, ref):
+    out = out.detach().float().cpu()
+    return bool(((out - ref).abs() <= ATOL + RTOL * ref.abs()).all()), (out - ref).abs().max().item()
+
+
+def _fill(latent, device):
+    from kernels.titan_kv import store_int8
+    n = latent.shape[0]
+    cache = torch.zeros((n + 255) // 256, 256, 528, dtype=torch.int8, device=device)
+    store_int8(latent.to(device), cache, torch.arange(n, device=device))
+    return cache
+
+
+@pytest.mark.parametrize("case", C.MLA_CASES, ids=lambda c: c.name)
+def test_golden_cases(case, native_lib, cuda_device):
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    gold = np.load(f"{GOLDEN}/mla_golden.npz")
+    inp = C.mla_inputs(case)
+    assert bytes(gold[f"{case.name}__input_sha256"]).hex() == C.mla_input_digest(inp)
+    cache = _fill(inp["latent"], cuda_device)
+    rows = cache.view(-1, 528)[: case.kv_rows]
+    kv = rows.view(-1, 1, 528)
+    ref = O.mla_sparse_attention(inp["q"], rows.cpu(), inp["indices"], case.sm_scale)
+    q = inp["q"].to(cuda_device)
+    idx = inp["indices"].to(cuda_device)
+    for splits in sorted(set(case.splits) | {0, 1, 2, 3, 16}):
+        out = attn(q, kv, idx, case.sm_scale, num_kv_splits=splits, sm_count=148)
+        assert out.shape == (case.tokens, case.heads, 512) and out.dtype == torch.bfloat16
+        ok, err = within(out, ref)
+        assert ok, (case.name, splits, err)
+        if splits in case.splits:
+            g = torch.from_numpy(O.bf16_bits_to_f32(gold[f"{case.name}__s{splits}"]).reshape(ref.shape))
+            ok, err = within(out, g)
+            assert ok, ("vs reference golden", case.name, splits, err)
+        if case.pattern == "all_neg":
+            assert not out.any()
+
+
+@pytest.fixture(scope="module")
+def big_cache(cuda_device):
+    """BASELINE config 2 cache: 262,144 rows written by store_int8."""
+    n = 262144
+    g = torch.Generator().manual_seed(1234)
+    latent = torch.randn(n, 512, generator=g).to(torch.bfloat16)
+    cache = _fill(latent, cuda_device)
+    return latent, cache, cache.view(n, 528).cpu()
+
+
+def test_config2_b1(big_cache, native_lib, cuda_device):
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(1, 16, 512, generator=g).to(torch.bfloat16)
+    idx = torch.full((1, 1, 2176), -1, dtype=torch.int32)
+    idx[0, 0, :2048] = torch.randperm(n, generator=g)[:2048].to(torch.int32)
+    ref = O.mla_sparse_attention(q, rows, idx, 512 ** -0.5)
+    for splits in (None, 1, 8, 16, 32, 64, 68):
+        out = attn(q.to(cuda_device), cache.view(n, 1, 528), idx.to(cuda_device), 512 ** -0.5,
+                   num_kv_splits=splits, sm_count=148)
+        ok, err = within(out, ref)
+        assert ok, (splits, err)
+        nmse, cos = O.mla_reference_test_metrics(out, q, latent, idx, n, 512 ** -0.5)
+        assert nmse < 1e-3 and cos > 0.999, (splits, nmse, cos)
+
+
+def test_config3_b8(big_cache, native_lib, cuda_device):
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(6)
+    q = (torch.randn(8, 16, 512, generator=g) * 0.15).to(torch.bfloat16)
+    idx = torch.randint(0, n, (8, 1, 2176), generator=g, dtype=torch.int32)
+    tails = torch.randint(0, 257, (8,), generator=g)
+    for t in range(8):
+        if tails[t] > 0:
+            idx[t, 0, -int(tails[t]):] = -1
+    ref = O.mla_sparse_attention(q, rows, idx, 512 ** -0.5)
+    for splits in (None, 1, 4, 16):
+        out = attn(q.to(cuda_device), cache.view(n, 1, 528), idx.to(cuda_device), 512 ** -0.5,
+                   num_kv_splits=splits, sm_count=148)
+        ok, err = within(out, ref)
+        assert ok, (splits, err)
+
+
+def test_prefill_shaped_slice(big_cache, native_lib, cuda_device):
+    """BASELINE config 4 index construction for a 192-token slice
+    (tokens t = 0..63, 1000..1063, 3000..3063), single pass."""
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(8)
+    toks = list(range(64)) + list(range(1000, 1064)) + list(range(3000, 3064))
+    idx = torch.full((len(toks), 1, 2176), -1, dtype=torch.int32)
+    for i, t in enumerate(toks):
+        pool = min(t + 1, 2176) + 65536 * (t // 1024)
+        k = min(pool, 2176)
+        idx[i, 0, :k] = torch.randperm(pool, generator=g)[:k].to(torch.int32)
+    q = torch.randn(len(toks), 16, 512, generator=g).to(torch.bfloat16)
+    ref = O.mla_sparse_attention(q, rows, idx, 512 ** -0.5)
+    out = attn(q.to(cuda_device), cache.view(n, 1, 528), idx.to(cuda_device), 512 ** -0.5, sm_count=148)
+    ok, err = within(out, ref)
+    assert ok, err
+
+
+def test_strided_q_and_int64_indices(big_cache, native_lib, cuda_device):
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(9)
+    qbig = torch.randn(3, 24, 512, generator=g).to(torch.bfloat16)
+    q = qbig[:, 4:20]                                   # head-strided view, 16 heads
+    idx = torch.randint(-50, n + 50, (3, 1, 256), generator=g, dtype=torch.int64)
+    idx[0, 0, 7] = (1 << 32) + 3                        # wide value must stay masked
+    ref = O.mla_sparse_attention(q, rows, idx, 0.07)
+    out = attn(q.to(cuda_device), cache.view(n, 1, 528), idx.to(cuda_device), 0.07)
+    ok, err = within(out, ref)
+    assert ok, err
+
+
+def test_deterministic_and_graph_capturable(big_cache, native_lib, cuda_device):
+    from kernels import titan_native
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(10)
+    q = torch.randn(2, 16, 512, generator=g).to(torch.bfloat16).to(cuda_device)
+    idx = torch.randint(0, n, (2, 1, 2176), generator=g, dtype=torch.int32).to(cuda_device)
+    kv = cache.view(n, 1, 528)
+    for splits in (1, 32):
+        a = attn(q, kv, idx, 512 ** -0.5, num_kv_splits=splits)
+        b = attn(q, kv, idx, 512 ** -0.5, num_kv_splits=splits)
+        assert torch.equal(a, b)
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                c = attn(q, kv, idx, 512 ** -0.5, num_kv_splits=splits)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(c, a)
+        graph.reset()
+    assert titan_native.device_error(q) == 0
+
+
+def test_empty_tokens_and_topk(native_lib, cuda_device):
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    kv = torch.zeros(64, 1, 528, dtype=torch.int8, device=cuda_device)
+    out = attn(torch.zeros(0, 16, 512, dtype=torch.bfloat16, device=cuda_device), kv,
+               torch.zeros(0, 1, 64, dtype=torch.int32, device=cuda_device), 0.1)
+    assert out.shape == (0, 16, 512)
+    out = attn(torch.ones(2, 16, 512, dtype=torch.bfloat16, device=cuda_device), kv,
+               torch.zeros(2, 1, 0, dtype=torch.int32, device=cuda_device), 0.1)
+    assert out.shape == (2, 16, 512) and not out.any()

@@ -1,0 +1,59 @@
+# SPDX-License-Identifier: Apache-2.0
+"""MoE route alignment on the GPU vs the reference-generated golden layouts:
+all 856 cases x int32/int64 x warps {1, 2, 4}, bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from tests.golden import cases as C
+
+pytestmark = pytest.mark.gpu
+GOLDEN = C.__file__.rsplit("/", 1)[0]
+
+
+def test_golden_layouts(native_lib, cuda_device):
+    from kernels.titan_moe_align import titan_moe_align_small
+    gold = np.load(f"{GOLDEN}/moe_golden.npz")
+    checked = 0
+    for i in range(len(gold["batch"])):
+        B = int(gold["batch"][i])
+        R = 8 * B
+        want = (gold["sorted_ids"][i][:8 * R], gold["expert_ids"][i][:R], gold["postpad"][i:i + 1])
+        for dtype in (torch.int32, torch.int64):
+            ids = torch.tensor(gold["routes"][i][:R], dtype=dtype).view(B, 8).to(cuda_device)
+            for warps in (1, 2, 4):
+                for pad in (False, True):
+                    got = titan_moe_align_small(ids, pad_sorted_ids=pad, num_warps=warps)
+                    for g, w in zip(got, want):
+                        assert g.dtype == torch.int32
+                        assert np.array_equal(g.cpu().numpy(), w), (i, dtype, warps)
+                    checked += 1
+    assert checked == 856 * 2 * 3 * 2
+
+
+def test_wide_ids_outside_int32_are_invalid(native_lib, cuda_device):
+    from kernels.titan_moe_align import titan_moe_align_small
+    from oracle import oracle as O
+    routes = [5, (1 << 32) + 5, 287, 288, -1, 5, 0, (1 << 40)]
+    ids = torch.tensor(routes, dtype=torch.int64, device=cuda_device).view(1, 8)
+    got = titan_moe_align_small(ids)
+    want = O.moe_align_small(routes)
+    for g, w in zip(got, want):
+        assert np.array_equal(g.cpu().numpy(), w)
+
+
+def test_graph_capture(native_lib, cuda_device):
+    from kernels.titan_moe_align import titan_moe_align_small
+    ids = torch.randint(0, 288, (8, 8), device=cuda_device, dtype=torch.int32)
+    want = titan_moe_align_small(ids)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            got = titan_moe_align_small(ids)
+    torch.cuda.current_stream().wait_stream(s)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, b) for a, b in zip(got, want))
+    graph.reset()
