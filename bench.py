@@ -495,6 +495,38 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_profile(args):
+    """Only the chosen workload's calls, eager and without L2 flushes (ncu
+    flushes caches itself between replay passes); prints nothing.  Used as the
+    target of the ncu captures summarised under profiles/."""
+    from kernels.titan_kv import store_int8
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lat = latents(KV_ROWS, 1234, dev)
+    cache = torch.zeros(KV_ROWS // BLOCK, BLOCK, ROW_BYTES, dtype=torch.int8, device=dev)
+    slots = torch.arange(KV_ROWS, device=dev)
+    store_int8(lat, cache, slots)
+    kv = cache.view(KV_ROWS, 1, ROW_BYTES)
+    n = args.warmup + args.steps
+    if args.profile == "store_int8":
+        for _ in range(n):
+            store_int8(lat, cache, slots)
+    elif args.profile in ("decode_b1", "decode_b8"):
+        batch = 1 if args.profile == "decode_b1" else 8
+        q, idx = decode_sets(batch, 8, 99, tail_mode="fixed" if batch == 1 else "random")
+        q, idx = q.to(dev), idx.to(dev)
+        for k in range(n):
+            attn(q[k % 8], kv, idx[k % 8], SM_SCALE)
+    elif args.profile == "prefill":
+        tp = 512
+        ip = prefill_indices(tp, 4242, t0=1024).to(dev)
+        qp = torch.randn(tp, HEADS, 512, device=dev).to(torch.bfloat16)
+        for _ in range(n):
+            attn(qp, kv, ip, SM_SCALE)
+    torch.cuda.synchronize()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=None)
@@ -505,12 +537,17 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill"), default=None,
+                    help="run only this workload (warmup + steps calls) as an ncu target; prints nothing")
     args = ap.parse_args()
     rank, world, local_rank = env_rank()
     if args.gpus is None:
         args.gpus = world
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.profile is not None:
+        run_profile(args)
+        return 0
     if args.impl == "reference":
         if rank == 0:
             run_reference(args)

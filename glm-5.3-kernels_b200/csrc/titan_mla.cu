@@ -105,12 +105,16 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
   const int32_t *idx_row = p.idx + (int64_t)t * p.idx_st;
   const uint64_t evict_first = policy_evict_first();
 
-  // Producer: warp 0 gathers tile `i` into stage i % kStages.
-  auto issue = [&](int i) {
-    const int stage = i % kStages;
+  // Producer: warp 0 gathers tile `i` into stage i % kStages.  Lane l owns
+  // position l of every tile.  Index loads never sit on the critical path:
+  // the first kStages tiles' indices are loaded together, and each later
+  // tile's index is prefetched into a register one tile ahead of its issue.
+  auto load_index = [&](int i) -> int64_t {
     const int64_t pos = start + (int64_t)i * kBN + lane;
-    int64_t r = -1;
-    if (pos < end) r = idx_row[pos];
+    return (i < n_tiles && pos < end) ? (int64_t)__ldg(idx_row + pos) : -1;
+  };
+  auto issue = [&](int i, int64_t r) {
+    const int stage = i % kStages;
     const bool ok = (r >= 0) && (r < p.seq_kv);
     const uint32_t mask = __ballot_sync(0xffffffffu, ok);
     if (lane == 0) {
@@ -120,9 +124,15 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
     __syncwarp();
     if (ok) bulk_g2s_hint(&sm.rows[stage][lane * kRowStride], p.kv + r * p.kv_rs, kRowBytes, &sm.bar[stage], evict_first);
   };
+  int64_t prefetched = -1;  // warp 0: index of tile (next issue) for this lane
   if (warp == 0) {
-    const int pre = n_tiles < kStages ? n_tiles : kStages;
-    for (int i = 0; i < pre; ++i) issue(i);
+    int64_t r[kStages];
+#pragma unroll
+    for (int i = 0; i < kStages; ++i) r[i] = load_index(i);
+    prefetched = load_index(kStages);
+#pragma unroll
+    for (int i = 0; i < kStages; ++i)
+      if (i < n_tiles) issue(i, r[i]);
   }
 
   // q fragments for this warp's 64 dims (A operand of QK), 4 k-steps.
@@ -222,7 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
       if ((tid & 15) == 0) sm.alpha[red_h] = alpha;
     }
     __syncthreads();
-    if (warp == 0 && i + kStages < n_tiles) issue(i + kStages);
+    if (warp == 0 && i + kStages < n_tiles) {
+      issue(i + kStages, prefetched);
+      prefetched = load_index(i + kStages + 1);
+    }
 
     // ---- PV: acc[16 heads x 64 dims] += P[16 x 32] . V[32 x 64].
     {
@@ -304,52 +317,93 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
   }
 }
 
-// Combine: one CTA per (token, head group, chunk of kDC dims); thread owns one
-// head and 4 consecutive dims.  Online merge over splits in natural log,
-// kernels/titan_mla.py:403-427.
-template <int kDC>
-__global__ void __launch_bounds__(kHeads * kDC / 4) sparse_mla_combine_kernel(const Params p) {
+// Combine: one CTA per (token, head group, 16-dim chunk), 256 threads.
+// Same merge as kernels/titan_mla.py:403-427 (natural-log LSE, max sentinel
+// -1e30, empty sum -> zeros), evaluated in parallel over the splits:
+//   1. 16 lanes per head stream the S LSE values: head max M and sum of
+//      exp(lse - M) by shuffle reduction;
+//   2. 4 split groups x 16 heads x 4 float4 columns accumulate
+//      sum_s exp(lse_s - M) * o_s with independent loads, then meet in smem.
+constexpr int kCombineDims = 16;
+constexpr int kCombineGroups = 4;
+constexpr int kCombineThreads = 256;
+
+__global__ void __launch_bounds__(kCombineThreads) sparse_mla_combine_kernel(const Params p) {
   pdl_wait_primary();
-  constexpr int kTpH = kDC / 4;  // threads per head
-  const int t = blockIdx.x;
-  const int hg = blockIdx.y;
-  const int chunk = blockIdx.z;
-  const int hl = threadIdx.x / kTpH;
-  const int h = hg * kHeads + hl;
-  if (h >= p.H) return;
-  const int dim = chunk * kDC + (threadIdx.x % kTpH) * 4;
-  const float *lse_base = p.part_lse + (int64_t)t * p.S * p.Hp + h;
-  const float *o_base = p.part_o + ((int64_t)t * p.S * p.Hp + h) * kD + dim;
-  const int64_t o_split_stride = (int64_t)p.Hp * kD;
+  __shared__ float s_max[kHeads];
+  __shared__ float s_inv[kHeads];
+  __shared__ float4 s_part[kCombineGroups][kHeads * kCombineDims / 4];
   constexpr float kLog2e = 1.4426950408889634f;
-  float e_max = kNegLarge, e_sum = 0.0f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-  for (int s = 0; s < p.S; ++s) {
-    const float lse = lse_base[(int64_t)s * p.Hp];
-    const float4 o = *reinterpret_cast<const float4 *>(o_base + s * o_split_stride);
-    const float n_max = fmaxf(lse, e_max);
-    const float old_scale = ex2_approx((e_max - n_max) * kLog2e);
-    const float w = ex2_approx((lse - n_max) * kLog2e);
-    acc.x = acc.x * old_scale + w * o.x;
-    acc.y = acc.y * old_scale + w * o.y;
-    acc.z = acc.z * old_scale + w * o.z;
-    acc.w = acc.w * old_scale + w * o.w;
-    e_sum = e_sum * old_scale + w;
-    e_max = n_max;
+  const int t = blockIdx.x, hg = blockIdx.y, chunk = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int S = p.S;
+  const float *lse_t = p.part_lse + (int64_t)t * S * p.Hp + hg * kHeads;
+
+  {  // 1. per-head max and normaliser
+    const int h = tid >> 4, j = tid & 15;
+    const bool live = hg * kHeads + h < p.H;
+    float m = kNegLarge;
+    if (live)
+      for (int s = j; s < S; s += 16) m = fmaxf(m, lse_t[(int64_t)s * p.Hp + h]);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.0f;
+    if (live)
+      for (int s = j; s < S; s += 16) sum += ex2_approx((lse_t[(int64_t)s * p.Hp + h] - m) * kLog2e);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (j == 0) {
+      s_max[h] = m;
+      s_inv[h] = sum > 0.0f ? 1.0f / sum : 1.0f;
+    }
   }
-  const float inv = e_sum > 0.0f ? 1.0f / e_sum : 1.0f;
-  uint2 r;
-  r.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-  r.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-  *reinterpret_cast<uint2 *>(p.out + (int64_t)t * p.out_st + (int64_t)h * p.out_sh + dim) = r;
+  __syncthreads();
+
+  // 2. weighted sum of the partial outputs
+  const int grp = tid >> 6;            // split group
+  const int pair = tid & 63;           // (head, float4 column)
+  const int h = pair >> 2, c4 = pair & 3;
+  const int hh = hg * kHeads + h;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (hh < p.H) {
+    const float m = s_max[h];
+    const int dim = chunk * kCombineDims + c4 * 4;
+    const float *o_t = p.part_o + ((int64_t)t * S * p.Hp + hh) * kD + dim;
+    const int64_t split_stride = (int64_t)p.Hp * kD;
+#pragma unroll 4
+    for (int s = grp; s < S; s += kCombineGroups) {
+      const float w = ex2_approx((lse_t[(int64_t)s * p.Hp + h] - m) * kLog2e);
+      const float4 o = *reinterpret_cast<const float4 *>(o_t + s * split_stride);
+      acc.x += w * o.x;
+      acc.y += w * o.y;
+      acc.z += w * o.z;
+      acc.w += w * o.w;
+    }
+  }
+  s_part[grp][pair] = acc;
+  __syncthreads();
+  if (grp == 0 && hh < p.H) {
+#pragma unroll
+    for (int g2 = 1; g2 < kCombineGroups; ++g2) {
+      const float4 v = s_part[g2][pair];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const float inv = s_inv[h];
+    uint2 r;
+    r.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+    r.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+    const int dim = chunk * kCombineDims + c4 * 4;
+    *reinterpret_cast<uint2 *>(p.out + (int64_t)t * p.out_st + (int64_t)hh * p.out_sh + dim) = r;
+  }
 }
 
-template <int kDC>
 static cudaError_t launch_combine(const Params &prm, int groups, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)prm.T, (unsigned)groups, (unsigned)(kD / kDC));
-  cfg.blockDim = dim3(kHeads * kDC / 4);
+  cfg.gridDim = dim3((unsigned)prm.T, (unsigned)groups, (unsigned)(kD / kCombineDims));
+  cfg.blockDim = dim3(kCombineThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -357,12 +411,11 @@ static cudaError_t launch_combine(const Params &prm, int groups, cudaStream_t s)
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, sparse_mla_combine_kernel<kDC>, prm);
+  return cudaLaunchKernelEx(&cfg, sparse_mla_combine_kernel, prm);
 }
 
 // Per-device one-time setup: the dynamic shared-memory opt-in of both kernel
-// variants and the SM count used to size the combine grid.
-static int g_sm_count[64] = {0};
+// variants.
 static bool g_smem_attr[64] = {false};
 
 static int ensure_smem_attribute(int smem) {
@@ -378,16 +431,7 @@ static int ensure_smem_attribute(int smem) {
   return TITAN_OK;
 }
 
-static int device_sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (g_sm_count[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_sm_count[dev] = n;
-  }
-  return g_sm_count[dev];
-}
+
 
 }  // namespace mla
 }  // namespace titan
@@ -474,19 +518,8 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   sparse_mla_kernel<false><<<grid, kThreads, smem, s>>>(prm);
   rc = check_launch("mla split launch");
   if (rc != TITAN_OK) return rc;
-  // Combine grid sized from the SM count: the widest dim chunk that still
-  // gives every SM a CTA.
-  const int sms = device_sm_count();
-  const int64_t base = num_tokens * groups;
-  cudaError_t e;
-  if (base * (kD / 128) >= sms)
-    e = launch_combine<128>(prm, (int)groups, s);
-  else if (base * (kD / 64) >= sms)
-    e = launch_combine<64>(prm, (int)groups, s);
-  else if (base * (kD / 32) >= sms)
-    e = launch_combine<32>(prm, (int)groups, s);
-  else
-    e = launch_combine<16>(prm, (int)groups, s);
+  // Combine: 32 CTAs per (token, head group), each merging 16 dims.
+  const cudaError_t e = launch_combine(prm, (int)groups, s);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla combine launch: %s", cudaGetErrorString(e));
   return TITAN_OK;
 }

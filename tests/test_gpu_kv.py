@@ -62,7 +62,7 @@ def test_block_strided_cache(native_lib, cuda_device):
     x = C.kv_latents()[:64]
     storage = torch.zeros(3, 40, 528, dtype=torch.int8, device=cuda_device)
     cache = storage[:, 4:36]                       # [3, 32, 528], stride0 = 40 * 528
-    slots = torch.arange(64) * 3 % 96
+    slots = torch.arange(64) * 5 % 96                 # distinct slots (5 is coprime with 96)
     store_int8(x.to(cuda_device), cache, slots.to(cuda_device))
     want = np.zeros((3, 32, 528), np.uint8)
     O.store_int8(O.tensor_bf16_bits(x), want, slots.numpy())
