@@ -10,50 +10,52 @@
 //            lse = (m + log2 l) * ln 2
 //   :357-429 combine: sum_s exp(lse_s - M) o_s / sum_s exp(lse_s - M), bf16
 //
-// B200 design (one CTA per (token, split, head group), 8 warps):
-//  * Gather: warp 0 reads 32 indices per tile and issues one 528-byte bulk copy
-//    (cp.async.bulk, TMA engine) per valid row into a 4-stage shared-memory
-//    ring; completion is counted in bytes on a per-stage mbarrier.  Masked rows
-//    cost no traffic.
-//  * Warp w owns latent dims [64 w, 64 w + 64) for both products, so every
-//    int8 byte is converted to bf16 exactly once, in registers:
-//      QK: mma.sync m16n8k16 (A = 16 heads x 16 dims of q in registers,
-//          B = 16 dims x 8 rows from one 16-byte shared load per lane); the
-//          8 warps' partial scores meet in shared memory.
-//      PV: the same bf16 B fragments are transposed in registers with
-//          movmatrix (rows become the reduction dim), A = P from shared memory.
-//    The k-dimension of QK is permuted identically for q and k (lane c of a
-//    quad reads 16 contiguous bytes), which makes each PV accumulator lane own
-//    16 contiguous output dims.
-//  * Split partials go to a workspace; a combine kernel, launched as a
-//    programmatic dependent of the split kernel, merges them.
+// B200 design: one CTA (8 warps) per (token, split, 16-head group).
+//  * Gather straight into registers: every 528-byte row is read once, so it is
+//    not staged in shared memory.  Warp w owns latent dims [64 w, 64 w + 64);
+//    lane (g, c) of the warp loads 16 bytes of row (8 nt + g) at byte
+//    64 w + 16 c for each of the tile's four 8-row n-tiles: exactly its MMA
+//    B fragments.  Loads run one tile ahead of the math (indices two tiles
+//    ahead); masked rows are never read.
+//  * QK: mma.sync m16n8k16 bf16 (A = 16 heads x 16 dims of q in registers).
+//    The k dimension is permuted identically for q and k so that each lane's
+//    16 contiguous bytes feed four k-steps.  The 8 warps' partial scores meet
+//    in shared memory; 16 lanes per head run the online softmax.
+//  * PV: the bf16 K fragments are transposed in registers with movmatrix (rows
+//    become the reduction dim), A = bf16(p * scale) from shared memory; each
+//    accumulator lane then owns 16 contiguous output dims.
+//  * Split merge: the C <= 16 splits of a (token, head group) that form one
+//    thread-block cluster merge through distributed shared memory, each CTA
+//    reducing 512 / C dims; a single cluster writes the bf16 output directly.
+//    With more clusters than one, each cluster writes one partial (o, lse) and
+//    a combine kernel, launched as a programmatic dependent, merges them.
 #include "titan_common.cuh"
 
 namespace titan {
 namespace mla {
 
 constexpr int kD = TITAN_LATENT_DIM;       // 512
-constexpr int kRowBytes = TITAN_ROW_BYTES;  // 528
 constexpr int kHeads = TITAN_HEAD_GROUP;    // 16 heads per CTA
 constexpr int kWarps = 8;                   // 64 dims per warp
 constexpr int kThreads = kWarps * 32;
-constexpr int kBN = 32;                     // rows per tile
-constexpr int kStages = 4;                  // gather ring depth
-constexpr int kRowStride = 544;             // smem bytes per row (bank-conflict-free QK loads)
+constexpr int kBN = 32;                     // rows per tile (four 8-row n-tiles)
 constexpr int kRedStride = 40;              // floats per head row of a warp's partial scores
 constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (bf16, 32 rows + pad)
+constexpr int kMbStride = kD + 16;          // floats per head row of the cluster merge buffer
+constexpr int kMaxCluster = 16;
 constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct Smem {
-  uint8_t rows[kStages][kBN * kRowStride];
-  float red[kWarps][kHeads * kRedStride];
-  uint32_t p[kHeads * kPStrideWords];
-  float scale[kBN];
+  float red[kWarps][kHeads * kRedStride];  // partial scores of each warp
+  uint32_t p[kHeads * kPStrideWords];      // bf16(p * scale), n-order
+  float mb[kHeads * kMbStride];            // this CTA's acc, read by the cluster
+  float scale[kBN];                        // row scales of the tile, n-order
+  uint32_t vword[4];                       // per n-tile: bit 4n = row n valid
   float alpha[kHeads];
-  float lsum[kHeads];
-  uint32_t valid[kStages];
-  alignas(8) uint64_t bar[kStages];
+  float2 ml[kHeads];                       // final (m, l) of this CTA
+  float cw[kMaxCluster][kHeads];           // cluster merge weights
+  float cM[kHeads], cL[kHeads];
 };
 
 struct Params {
@@ -65,18 +67,21 @@ struct Params {
   int64_t idx_st, topk;
   __nv_bfloat16 *out;
   int64_t out_st, out_sh;
-  float *part_o;    // [T][S][Hp][512]
-  float *part_lse;  // [T][S][Hp]
-  int T, H, Hp, S;
+  float *part_o;    // [T][NC][Hp][512]  (partials, one per cluster)
+  float *part_lse;  // [T][NC][Hp]
+  int T, H, Hp;
+  int S;            // splits per (token, head group)
+  int C;            // splits per cluster (1, 2, 4, 8 or 16; divides S)
+  int NC;           // clusters per (token, head group) = S / C = partials to combine
   int64_t split_topk;
   float scale_log2;  // sm_scale * log2(e)
 };
 
-// Row of an n-tile that lane-quad index g reads: swaps bits 0 and 1 so the two
-// rows served in one quarter-warp phase of a 16-byte load sit 16 banks apart.
-__device__ __forceinline__ int row_perm(int g) { return (g & 4) | ((g & 1) << 1) | ((g >> 1) & 1); }
+__device__ __forceinline__ int pick4(const int (&v)[4], int i) {
+  return i == 0 ? v[0] : i == 1 ? v[1] : i == 2 ? v[2] : v[3];
+}
 
-template <bool kFinal>
+template <bool kPartialOut>
 __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
@@ -88,52 +93,43 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
   const int split = blockIdx.x - t * p.S;
   const int hg = blockIdx.y;
 
-  if constexpr (!kFinal) pdl_launch_dependents();
+  if constexpr (kPartialOut) pdl_launch_dependents();
 
   const int64_t start = (int64_t)split * p.split_topk;
   const int64_t end = min(start + p.split_topk, p.topk);
   const int n_rows = end > start ? (int)(end - start) : 0;
   const int n_tiles = (n_rows + kBN - 1) / kBN;
-
-  if (tid == 0) {
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) mbar_init(&sm.bar[s], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-
   const int32_t *idx_row = p.idx + (int64_t)t * p.idx_st;
-  const uint64_t evict_first = policy_evict_first();
+  const uint8_t *kv_lane = p.kv + warp * 64 + c * 16;  // this lane's 16-byte column of a row
+  const int64_t seq_kv = p.seq_kv;
+  const bool scale_loader = warp < 4 && c == 0;          // loads scales of n-tile `warp`
 
-  // Producer: warp 0 gathers tile `i` into stage i % kStages.  Lane l owns
-  // position l of every tile.  Index loads never sit on the critical path:
-  // the first kStages tiles' indices are loaded together, and each later
-  // tile's index is prefetched into a register one tile ahead of its issue.
-  auto load_index = [&](int i) -> int64_t {
-    const int64_t pos = start + (int64_t)i * kBN + lane;
-    return (i < n_tiles && pos < end) ? (int64_t)__ldg(idx_row + pos) : -1;
-  };
-  auto issue = [&](int i, int64_t r) {
-    const int stage = i % kStages;
-    const bool ok = (r >= 0) && (r < p.seq_kv);
-    const uint32_t mask = __ballot_sync(0xffffffffu, ok);
-    if (lane == 0) {
-      sm.valid[stage] = mask;
-      mbar_arrive_expect_tx(&sm.bar[stage], (uint32_t)__popc(mask) * kRowBytes);
+  // Row indices of tile j for this lane: n-tile nt, n-order row g.
+  auto load_idx = [&](int j, int (&r)[4]) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int64_t pos = start + (int64_t)j * kBN + nt * 8 + g;
+      r[nt] = (j < n_tiles && pos < end) ? __ldg(idx_row + pos) : -1;
     }
-    __syncwarp();
-    if (ok) bulk_g2s_hint(&sm.rows[stage][lane * kRowStride], p.kv + r * p.kv_rs, kRowBytes, &sm.bar[stage], evict_first);
   };
-  int64_t prefetched = -1;  // warp 0: index of tile (next issue) for this lane
-  if (warp == 0) {
-    int64_t r[kStages];
+  auto row_ok = [&](int r) { return r >= 0 && (int64_t)r < seq_kv; };
+  auto load_rows = [&](const int (&r)[4], uint4 (&kb)[4], float &sc) {
 #pragma unroll
-    for (int i = 0; i < kStages; ++i) r[i] = load_index(i);
-    prefetched = load_index(kStages);
-#pragma unroll
-    for (int i = 0; i < kStages; ++i)
-      if (i < n_tiles) issue(i, r[i]);
-  }
+    for (int nt = 0; nt < 4; ++nt)
+      kb[nt] = row_ok(r[nt]) ? ld_global_nc_v4(kv_lane + (int64_t)r[nt] * p.kv_rs) : make_uint4(0, 0, 0, 0);
+    sc = 0.0f;
+    if (scale_loader) {
+      const int rs = pick4(r, warp);
+      if (row_ok(rs)) sc = ld_global_nc_f32(p.kv + (int64_t)rs * p.kv_rs + 512);
+    }
+  };
+
+  int r_cur[4], r_next[4];
+  uint4 kb_cur[4];
+  float sc_cur;
+  load_idx(0, r_cur);
+  load_idx(1, r_next);
+  load_rows(r_cur, kb_cur, sc_cur);
 
   // q fragments for this warp's 64 dims (A operand of QK), 4 k-steps.
   uint32_t qa[4][4];
@@ -163,43 +159,54 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
     }
   }
 
-  // Softmax state of head (2 warp + lane / 16), replicated over its 16 lanes.
+  // Softmax state of head red_h, replicated over its 16 lanes.
   float m_run = kNegLarge, l_run = 0.0f;
   float acc[8][4];
 #pragma unroll
   for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
 
-  const int red_h = tid >> 4;            // head reduced by this thread
-  const int red_j = (tid & 15) * 2;      // its two n-order positions
+  const int red_h = tid >> 4;        // head reduced by this thread
+  const int red_j = (tid & 15) * 2;  // its two n-order positions
   const int red_nt = red_j >> 3;
-  const int red_r0 = red_nt * 8 + row_perm(red_j & 7);
-  const int red_r1 = red_nt * 8 + row_perm((red_j & 7) + 1);
+  const int red_n = red_j & 7;
 
-  bool lost_copy = false;  // a bounded wait gave up (error word set); keep going, short waits
   for (int i = 0; i < n_tiles; ++i) {
-    const int stage = i % kStages;
-    if (!mbar_wait_bounded(&sm.bar[stage], (uint32_t)((i / kStages) & 1),
-                           lost_copy ? kShortWaitCycles : kLongWaitCycles))
-      lost_copy = true;
-    const uint8_t *buf = sm.rows[stage];
+    // Next tile's rows are in flight while this tile computes.
+    uint4 kb_nxt[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    float sc_nxt = 0.0f;
+    int r_nn[4];
+    if (i + 1 < n_tiles) load_rows(r_next, kb_nxt, sc_nxt);
+    load_idx(i + 2, r_nn);
 
     // ---- QK^T over this warp's 64 dims; keep the bf16 B fragments for PV.
     uint32_t kf[4][4][2];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
-      const uint4 kw = *reinterpret_cast<const uint4 *>(buf + (nt * 8 + row_perm(g)) * kRowStride + warp * 64 + c * 16);
-      i8x4_to_bf16x4(kw.x, kf[nt][0][0], kf[nt][0][1]);
-      i8x4_to_bf16x4(kw.y, kf[nt][1][0], kf[nt][1][1]);
-      i8x4_to_bf16x4(kw.z, kf[nt][2][0], kf[nt][2][1]);
-      i8x4_to_bf16x4(kw.w, kf[nt][3][0], kf[nt][3][1]);
-      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int s = 0; s < 4; ++s) mma_bf16_16816(sacc, qa[s], kf[nt][s][0], kf[nt][s][1]);
-      float *red = sm.red[warp];
-      *reinterpret_cast<float2 *>(&red[g * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[0], sacc[1]);
-      *reinterpret_cast<float2 *>(&red[(g + 8) * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[2], sacc[3]);
+      i8x4_to_bf16x4(kb_cur[nt].x, kf[nt][0][0], kf[nt][0][1]);
+      i8x4_to_bf16x4(kb_cur[nt].y, kf[nt][1][0], kf[nt][1][1]);
+      i8x4_to_bf16x4(kb_cur[nt].z, kf[nt][2][0], kf[nt][2][1]);
+      i8x4_to_bf16x4(kb_cur[nt].w, kf[nt][3][0], kf[nt][3][1]);
     }
-    if (lane < 4) sm.scale[warp * 4 + lane] = *reinterpret_cast<const float *>(buf + (warp * 4 + lane) * kRowStride + 512);
+    float sacc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+#pragma unroll
+    for (int s = 0; s < 4; ++s)  // k-step outer: four independent accumulator chains interleave
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_bf16_16816(sacc[nt], qa[s], kf[nt][s][0], kf[nt][s][1]);
+    {
+      float *red = sm.red[warp];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        *reinterpret_cast<float2 *>(&red[g * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[nt][0], sacc[nt][1]);
+        *reinterpret_cast<float2 *>(&red[(g + 8) * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[nt][2], sacc[nt][3]);
+      }
+    }
+    if (warp < 4) {
+      const uint32_t vb = __ballot_sync(0xffffffffu, c == 0 && row_ok(pick4(r_cur, warp)));
+      if (lane == 0) sm.vword[warp] = vb;
+      if (c == 0) sm.scale[warp * 8 + g] = sc_cur;
+    }
     __syncthreads();
 
     // ---- Reduce the 8 partial scores, scale, mask, online softmax, P.
@@ -211,9 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
         s0 += v.x;
         s1 += v.y;
       }
-      const uint32_t vmask = sm.valid[stage];
-      const bool v0 = (vmask >> red_r0) & 1u, v1 = (vmask >> red_r1) & 1u;
-      const float sc0 = sm.scale[red_r0], sc1 = sm.scale[red_r1];
+      const uint32_t vw = sm.vword[red_nt];
+      const bool v0 = (vw >> (4 * red_n)) & 1u, v1 = (vw >> (4 * red_n + 4)) & 1u;
+      const float sc0 = sm.scale[red_j], sc1 = sm.scale[red_j + 1];
       const float x0 = v0 ? (s0 * sc0) * p.scale_log2 : kNegLarge;
       const float x1 = v1 ? (s1 * sc1) * p.scale_log2 : kNegLarge;
       float mx = fmaxf(x0, x1);
@@ -232,10 +239,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
       if ((tid & 15) == 0) sm.alpha[red_h] = alpha;
     }
     __syncthreads();
-    if (warp == 0 && i + kStages < n_tiles) {
-      issue(i + kStages, prefetched);
-      prefetched = load_index(i + kStages + 1);
-    }
 
     // ---- PV: acc[16 heads x 64 dims] += P[16 x 32] . V[32 x 64].
     {
@@ -265,56 +268,138 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
         }
       }
     }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      kb_cur[nt] = kb_nxt[nt];
+      r_cur[nt] = r_next[nt];
+      r_next[nt] = r_nn[nt];
+    }
+    sc_cur = sc_nxt;
   }
 
-  // ---- Epilogue.
-  if ((tid & 15) == 0) sm.lsum[red_h] = l_run;
-  if (!kFinal && (tid & 15) == 0) {
-    const int h = hg * kHeads + red_h;
-    if (h < p.H) {
-      // (m + log2 l) * ln 2; l == 0 gives -inf, which the combine weighs as 0.
-      const float lse = (m_run + lg2_approx(l_run)) * kLn2;
-      p.part_lse[((int64_t)t * p.S + split) * p.Hp + h] = lse;
+  // ---- Epilogue.  Lane (g, c) of warp w holds, for heads g and g + 8,
+  // dims 64 w + 16 c + j at acc[2 s + x][2 half + e] with j = 4 s + 2 x + e.
+  if ((tid & 15) == 0) sm.ml[red_h] = make_float2(m_run, l_run);
+  const int dim0 = warp * 64 + c * 16;
+  const int C = p.C;
+  const int cl = split / C;  // partial index when kPartialOut
+  if (C == 1) {
+    __syncthreads();
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int hl = g + 8 * half;
+      const int h = hg * kHeads + hl;
+      if (h >= p.H) continue;
+      const float l = sm.ml[hl].y;
+      const float inv = l > 0.0f ? 1.0f / l : 1.0f;
+      float v[16];
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          v[4 * s + 2 * x + 0] = acc[2 * s + x][2 * half + 0] * inv;
+          v[4 * s + 2 * x + 1] = acc[2 * s + x][2 * half + 1] * inv;
+        }
+      if constexpr (!kPartialOut) {
+        uint4 o0, o1;
+        o0.x = pack_bf16x2(v[0], v[1]);
+        o0.y = pack_bf16x2(v[2], v[3]);
+        o0.z = pack_bf16x2(v[4], v[5]);
+        o0.w = pack_bf16x2(v[6], v[7]);
+        o1.x = pack_bf16x2(v[8], v[9]);
+        o1.y = pack_bf16x2(v[10], v[11]);
+        o1.z = pack_bf16x2(v[12], v[13]);
+        o1.w = pack_bf16x2(v[14], v[15]);
+        uint4 *dst = reinterpret_cast<uint4 *>(p.out + (int64_t)t * p.out_st + (int64_t)h * p.out_sh + dim0);
+        dst[0] = o0;
+        dst[1] = o1;
+      } else {
+        float4 *dst = reinterpret_cast<float4 *>(p.part_o + (((int64_t)t * p.NC + cl) * p.Hp + h) * kD + dim0);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        dst[2] = make_float4(v[8], v[9], v[10], v[11]);
+        dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+      }
     }
+    if constexpr (kPartialOut) {
+      if (tid < kHeads && hg * kHeads + tid < p.H) {
+        const float2 ml = sm.ml[tid];
+        // (m + log2 l) * ln 2; l == 0 gives -inf, which the combine weighs as 0.
+        p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (ml.x + lg2_approx(ml.y)) * kLn2;
+      }
+    }
+    return;
   }
-  __syncthreads();
+
+  // Cluster merge: publish this CTA's acc, then CTA `rank` reduces dims
+  // [rank * 512 / C, (rank + 1) * 512 / C) over the C CTAs of the cluster.
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    const int hl = g + 8 * half;
-    const int h = hg * kHeads + hl;
-    if (h >= p.H) continue;
-    const float l = sm.lsum[hl];
-    const float inv = l > 0.0f ? 1.0f / l : 1.0f;
-    float v[16];
+    float4 *dst = reinterpret_cast<float4 *>(&sm.mb[(g + 8 * half) * kMbStride + dim0]);
 #pragma unroll
     for (int s = 0; s < 4; ++s)
+      dst[s] = make_float4(acc[2 * s][2 * half], acc[2 * s][2 * half + 1], acc[2 * s + 1][2 * half],
+                           acc[2 * s + 1][2 * half + 1]);
+  }
+  cluster_sync();
+  if (tid < kHeads) {
+    float2 ml[kMaxCluster];
+    float M = kNegLarge;
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        v[4 * s + 2 * x + 0] = acc[2 * s + x][2 * half + 0] * inv;
-        v[4 * s + 2 * x + 1] = acc[2 * s + x][2 * half + 1] * inv;
+    for (int r = 0; r < kMaxCluster; ++r) {
+      if (r < C) {
+        ml[r] = ld_dsmem_f32x2(dsmem_map(&sm.ml[tid], (uint32_t)r));
+        M = fmaxf(M, ml[r].x);
       }
-    const int dim0 = warp * 64 + c * 16;
-    if constexpr (kFinal) {
-      uint4 o0, o1;
-      o0.x = pack_bf16x2(v[0], v[1]);
-      o0.y = pack_bf16x2(v[2], v[3]);
-      o0.z = pack_bf16x2(v[4], v[5]);
-      o0.w = pack_bf16x2(v[6], v[7]);
-      o1.x = pack_bf16x2(v[8], v[9]);
-      o1.y = pack_bf16x2(v[10], v[11]);
-      o1.z = pack_bf16x2(v[12], v[13]);
-      o1.w = pack_bf16x2(v[14], v[15]);
-      uint4 *dst = reinterpret_cast<uint4 *>(p.out + (int64_t)t * p.out_st + (int64_t)h * p.out_sh + dim0);
-      dst[0] = o0;
-      dst[1] = o1;
-    } else {
-      float4 *dst = reinterpret_cast<float4 *>(p.part_o + (((int64_t)t * p.S + split) * p.Hp + h) * kD + dim0);
-      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-      dst[2] = make_float4(v[8], v[9], v[10], v[11]);
-      dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+    }
+    float L = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) {
+      if (r < C) {
+        const float w = ex2_approx(ml[r].x - M);
+        sm.cw[r][tid] = w;
+        L += w * ml[r].y;
+      }
+    }
+    sm.cM[tid] = M;
+    sm.cL[tid] = L;
+  }
+  __syncthreads();
+  const uint32_t rank = cluster_ctarank();
+  const int D = kD / C;
+  const int pairs = kHeads * D / 2;  // float2 outputs of this CTA
+#pragma unroll 2
+  for (int pp = tid; pp < pairs; pp += kThreads) {
+    const int h = pp / (D / 2);
+    const int d = (int)rank * D + 2 * (pp - h * (D / 2));
+    float2 sum = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) {
+      if (r < C) {
+        const float2 v = ld_dsmem_f32x2(dsmem_map(&sm.mb[h * kMbStride + d], (uint32_t)r));
+        const float w = sm.cw[r][h];
+        sum.x += w * v.x;
+        sum.y += w * v.y;
+      }
+    }
+    const int hh = hg * kHeads + h;
+    if (hh < p.H) {
+      const float L = sm.cL[h];
+      const float inv = L > 0.0f ? 1.0f / L : 1.0f;
+      if constexpr (!kPartialOut) {
+        *reinterpret_cast<uint32_t *>(p.out + (int64_t)t * p.out_st + (int64_t)hh * p.out_sh + d) =
+            pack_bf16x2(sum.x * inv, sum.y * inv);
+      } else {
+        *reinterpret_cast<float2 *>(p.part_o + (((int64_t)t * p.NC + cl) * p.Hp + hh) * kD + d) =
+            make_float2(sum.x * inv, sum.y * inv);
+      }
     }
   }
+  if constexpr (kPartialOut) {
+    if (rank == 0 && tid < kHeads && hg * kHeads + tid < p.H)
+      p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (sm.cM[tid] + lg2_approx(sm.cL[tid])) * kLn2;
+  }
+  cluster_sync();  // keep this CTA's shared memory alive until the cluster has read it
 }
 
 // Combine: one CTA per (token, head group, 16-dim chunk), 256 threads.
@@ -336,7 +421,7 @@ __global__ void __launch_bounds__(kCombineThreads) sparse_mla_combine_kernel(con
   constexpr float kLog2e = 1.4426950408889634f;
   const int t = blockIdx.x, hg = blockIdx.y, chunk = blockIdx.z;
   const int tid = threadIdx.x;
-  const int S = p.S;
+  const int S = p.NC;  // partials to merge
   const float *lse_t = p.part_lse + (int64_t)t * S * p.Hp + hg * kHeads;
 
   {  // 1. per-head max and normaliser
@@ -414,24 +499,50 @@ static cudaError_t launch_combine(const Params &prm, int groups, cudaStream_t s)
   return cudaLaunchKernelEx(&cfg, sparse_mla_combine_kernel, prm);
 }
 
-// Per-device one-time setup: the dynamic shared-memory opt-in of both kernel
-// variants.
-static bool g_smem_attr[64] = {false};
+// Per-device one-time setup: dynamic shared-memory opt-in, non-portable
+// cluster size opt-in, and the largest cluster size the device can schedule
+// for this kernel (queried, not assumed).
+static bool g_dev_ready[64] = {false};
+static int g_max_cluster[64] = {0};
 
-static int ensure_smem_attribute(int smem) {
+static int prepare_device(size_t smem, int *max_cluster) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev >= 0 && dev < 64 && g_smem_attr[dev]) return TITAN_OK;
-  e = cudaFuncSetAttribute(sparse_mla_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(sparse_mla_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: shared-memory attribute: %s", cudaGetErrorString(e));
-  if (dev >= 0 && dev < 64) g_smem_attr[dev] = true;
+  if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "mla: device ordinal %d out of range", dev);
+  if (!g_dev_ready[dev]) {
+    void (*kernels[2])(const Params) = {sparse_mla_kernel<false>, sparse_mla_kernel<true>};
+    for (auto k : kernels) {
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: kernel attributes: %s", cudaGetErrorString(e));
+    }
+    int best = 1;
+    for (int cs = kMaxCluster; cs >= 2; cs >>= 1) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)cs, 1, 1);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)cs;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg) == cudaSuccess && n > 0) {
+        best = cs;
+        break;
+      }
+      cudaGetLastError();  // clear a rejected query
+    }
+    g_max_cluster[dev] = best;
+    g_dev_ready[dev] = true;
+  }
+  *max_cluster = g_max_cluster[dev];
   return TITAN_OK;
 }
-
-
 
 }  // namespace mla
 }  // namespace titan
@@ -479,6 +590,16 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
     if ((uintptr_t)workspace % 16) return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: workspace must be 16-byte aligned");
   }
 
+  const size_t smem = sizeof(Smem);
+  int max_cluster = 1;
+  int rc = prepare_device(smem, &max_cluster);
+  if (rc != TITAN_OK) return rc;
+  // Cluster size: the largest power of two <= the schedulable maximum that
+  // divides the split count; NC clusters (partials) per (token, head group).
+  int C = 1;
+  while (C * 2 <= max_cluster && num_kv_splits % (C * 2) == 0) C *= 2;
+  const int64_t NC = num_kv_splits / C;
+
   Params prm;
   prm.q = static_cast<const __nv_bfloat16 *>(q);
   prm.q_st = q_stride_token;
@@ -496,30 +617,37 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   prm.H = (int)num_heads;
   prm.Hp = (int)(groups * kHeads);
   prm.S = (int)num_kv_splits;
+  prm.C = C;
+  prm.NC = (int)NC;
   prm.split_topk = (topk + num_kv_splits - 1) / num_kv_splits;
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
   prm.part_o = nullptr;
   prm.part_lse = nullptr;
-  if (num_kv_splits > 1) {
-    const int64_t o_bytes = num_tokens * num_kv_splits * prm.Hp * kD * 4;
+  if (NC > 1) {
+    const int64_t o_bytes = num_tokens * NC * prm.Hp * kD * 4;
     prm.part_o = static_cast<float *>(workspace);
     prm.part_lse = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + o_bytes);
   }
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const size_t smem = sizeof(Smem) + 128;
-  const dim3 grid((unsigned)(num_tokens * num_kv_splits), (unsigned)groups);
-  int rc = ensure_smem_attribute((int)smem);
-  if (rc != TITAN_OK) return rc;
-  if (num_kv_splits == 1) {
-    sparse_mla_kernel<true><<<grid, kThreads, smem, s>>>(prm);
-    return check_launch("mla final launch");
-  }
-  sparse_mla_kernel<false><<<grid, kThreads, smem, s>>>(prm);
-  rc = check_launch("mla split launch");
-  if (rc != TITAN_OK) return rc;
-  // Combine: 32 CTAs per (token, head group), each merging 16 dims.
-  const cudaError_t e = launch_combine(prm, (int)groups, s);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(num_tokens * num_kv_splits), (unsigned)groups, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = C > 1 ? 1 : 0;
+  cudaError_t e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true>, prm)
+                         : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false>, prm);
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla launch (C=%d): %s", C, cudaGetErrorString(e));
+  if (NC == 1) return TITAN_OK;
+  // Combine the NC cluster partials: 32 CTAs per (token, head group).
+  e = launch_combine(prm, (int)groups, s);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla combine launch: %s", cudaGetErrorString(e));
   return TITAN_OK;
 }
