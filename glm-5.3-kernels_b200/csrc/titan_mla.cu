@@ -651,3 +651,62 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla combine launch: %s", cudaGetErrorString(e));
   return TITAN_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of titan_mla_sparse_attention.
+//
+// The split-KV path needs scratch memory for the per-cluster partial outputs.
+// Callers that cannot allocate device memory themselves — a plugin running
+// inside a host engine whose pool owns all device memory, or code issuing
+// work while a stream is being captured in global capture mode, where
+// cudaMalloc is not permitted — use this entry point instead: the scratch is a
+// file-scope device array of kNoAllocScratchBytes (8 MiB) that every GPU which
+// loads this library holds until the process exits.
+namespace titan {
+namespace mla {
+
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static void *g_noalloc_scratch_ptr[64] = {nullptr};
+
+}  // namespace mla
+}  // namespace titan
+
+extern "C" int64_t titan_mla_noalloc_scratch_bytes(void) { return titan::mla::kNoAllocScratchBytes; }
+
+extern "C" int titan_mla_sparse_attention_noalloc(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                                                  const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                                                  const int32_t *indices, int64_t indices_stride_token,
+                                                  int64_t topk, void *out, int64_t out_stride_token,
+                                                  int64_t out_stride_head, int64_t num_tokens, int64_t num_heads,
+                                                  float sm_scale, int64_t num_kv_splits, titan_stream_t stream) {
+  using namespace titan;
+  using namespace titan::mla;
+  const int64_t need = titan_mla_workspace_bytes(num_tokens, num_heads, num_kv_splits);
+  if (need > kNoAllocScratchBytes)
+    return fail(TITAN_ERR_INVALID_ARGUMENT,
+                "mla noalloc: this call needs %lld bytes of split scratch but the static scratch holds %lld; "
+                "lower num_kv_splits or num_tokens, or call titan_mla_sparse_attention with a workspace",
+                (long long)need, (long long)kNoAllocScratchBytes);
+  void *scratch = nullptr;
+  if (need > 0) {
+    // Host code cannot use the array's name as a device address: look up the
+    // address once per device, with that device current.
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "mla noalloc: device ordinal %d out of range", dev);
+    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+      void *ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess || ptr == nullptr)
+        return fail(TITAN_ERR_CUDA, "mla noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      g_noalloc_scratch_ptr[dev] = ptr;
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  return titan_mla_sparse_attention(q, q_stride_token, q_stride_head, kv, kv_row_stride, seq_kv, indices,
+                                    indices_stride_token, topk, out, out_stride_token, out_stride_head, num_tokens,
+                                    num_heads, sm_scale, num_kv_splits, scratch, need > 0 ? kNoAllocScratchBytes : 0,
+                                    stream);
+}

@@ -32,6 +32,12 @@ SIGNATURES = {
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
          ctypes.c_float, _i64, _vp, _i64, _vp],
     ),
+    "titan_mla_noalloc_scratch_bytes": (_i64, []),
+    "titan_mla_sparse_attention_noalloc": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+         ctypes.c_float, _i64, _vp],
+    ),
     "titan_moe_align_small": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _int, _vp]),
     "titan_device_error": (_int, [ctypes.POINTER(_int), _int, _vp]),
 }

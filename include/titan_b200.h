@@ -107,6 +107,28 @@ int titan_mla_sparse_attention(const void *q, int64_t q_stride_token, int64_t q_
                                titan_stream_t stream);
 
 /*
+ * Allocation-free variant of titan_mla_sparse_attention (no counterpart in the
+ * reference).  For callers that cannot allocate device memory — a plugin whose
+ * host engine owns the whole device pool, or work issued while another thread
+ * captures a stream in global capture mode, where cudaMalloc is refused.  The
+ * split-KV scratch is a static device array of titan_mla_noalloc_scratch_bytes()
+ * bytes (8 MiB) that every GPU loading the library holds until exit; a call that
+ * needs more (titan_mla_workspace_bytes(T, H, num_kv_splits) > 8 MiB) fails with
+ * TITAN_ERR_INVALID_ARGUMENT.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls on a device share the one array: calls that overlap on the
+ * GPU (different streams, no ordering) race.  Nothing in the scratch needs to
+ * start at zero; each call overwrites what it reads.  Allocates nothing.
+ */
+int64_t titan_mla_noalloc_scratch_bytes(void);
+int titan_mla_sparse_attention_noalloc(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                                       const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                                       const int32_t *indices, int64_t indices_stride_token, int64_t topk,
+                                       void *out, int64_t out_stride_token, int64_t out_stride_head,
+                                       int64_t num_tokens, int64_t num_heads, float sm_scale,
+                                       int64_t num_kv_splits, titan_stream_t stream);
+
+/*
  * Small stable MoE route alignment (B1..8, top-8, 288 experts, block 8).
  * Replaces `titan_moe_align_small(topk_ids, ...)`, kernels/titan_moe_align.py:49-81
  * (kernel :12-46).
