@@ -62,26 +62,38 @@ def env_rank():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
-class Dist:
-    """torch.distributed for barriers and max-over-ranks timing only."""
+def token_block(total, world, rank):
+    """Contiguous block [lo, hi) of `total` independent requests owned by `rank`
+    (the path has no cross-request exchange, so ranks never communicate data)."""
+    return total * rank // world, total * (rank + 1) // world
 
-    def __init__(self, world, rank, local_rank):
+
+class Dist:
+    """torch.distributed for barriers and max-over-ranks timing only (NCCL on
+    GPUs; gloo for the CPU tests of this host logic)."""
+
+    def __init__(self, world, rank, local_rank, backend="nccl"):
         self.world, self.rank, self.local_rank = world, rank, local_rank
+        self.backend = backend
         self.pg = None
         if world > 1:
             import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                    device_id=torch.device("cuda", local_rank))
+            kw = {"device_id": torch.device("cuda", local_rank)} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=timedelta(seconds=300), **kw)
             self.pg = dist
 
     def barrier(self):
         if self.pg is not None:
-            self.pg.barrier(device_ids=[self.local_rank])
+            if self.backend == "nccl":
+                self.pg.barrier(device_ids=[self.local_rank])
+            else:
+                self.pg.barrier()
 
     def max(self, value):
         if self.pg is None:
             return value
-        t = torch.tensor([value], dtype=torch.float64, device=torch.device("cuda", self.local_rank))
+        dev = torch.device("cuda", self.local_rank) if self.backend == "nccl" else torch.device("cpu")
+        t = torch.tensor([value], dtype=torch.float64, device=dev)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
@@ -338,9 +350,10 @@ def run_ours(args, dist):
     store_int8(lat, cache, slots)  # restore the arange layout
 
     # ---- config 3: B=8 decode, tokens sharded contiguously over ranks
-    per = max(1, 8 // world)
+    lo, hi = token_block(8, world, rank)
+    per = max(1, hi - lo)
+    lo = min(lo, 8 - per)
     q8, i8 = decode_sets(8, 8, 777, tail_mode="random")
-    lo = min(rank * per, 8 - per)
     q8d, i8d = q8[:, lo:lo + per].contiguous().to(dev), i8[:, lo:lo + per].contiguous().to(dev)
     q8s, i8s = q8d[0].clone(), i8d[0].clone()
     g8, _ = capture(lambda: attn(q8s, kv, i8s, SM_SCALE, sm_count=sms))
@@ -361,8 +374,8 @@ def run_ours(args, dist):
 
     # ---- config 4: prefill-shaped, T=4096 tokens sharded over ranks
     if not args.skip_prefill:
-        tp = 4096 // world
-        t0 = rank * tp
+        t0, t1 = token_block(4096, world, rank)
+        tp = t1 - t0
         ip = prefill_indices(tp, 4242 + rank, t0=t0).to(dev)
         qp = torch.randn(tp, HEADS, 512, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(
             torch.bfloat16)

@@ -95,8 +95,8 @@ int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_heads,
  *   num_kv_splits  >= 1; 1 = single pass, otherwise split-KV + combine
  *   workspace      >= titan_mla_workspace_bytes(...) bytes of device memory, 16-byte aligned
  *
- * kv and kv_row_stride must be 16-byte aligned (each row is fetched by one bulk
- * copy).  A token whose indices are all masked produces exact zeros.
+ * kv and kv_row_stride must be 16-byte aligned (rows are read with 16-byte
+ * loads).  A token whose indices are all masked produces exact zeros.
  */
 int titan_mla_sparse_attention(const void *q, int64_t q_stride_token, int64_t q_stride_head,
                                const void *kv, int64_t kv_row_stride, int64_t seq_kv,
