@@ -7,13 +7,17 @@
 Headline (one JSON line on rank 0): BASELINE config 2 — B=1 decode, 16 heads,
 262,144-row INT8 cache (1024 blocks x 256 x 528 B) filled by store_int8,
 2176 indices per token (2048 distinct valid + 128 x -1), sm_scale 512^-0.5.
-A step is one call of triton_mla_sparse_attention on one index set.  `value`
-is device time per call (CUDA events around a CUDA-graph replay of the call,
-L2 flushed by a 256 MiB write before every timed call), whole-job: per-rank
-mean, max over ranks, divided by the number of ranks (each rank serves its own
-independent B=1 requests; the path needs no collective).  `e2e` is the same
-call through the public API with inputs copied from pinned host memory and
-the output copied back inside the timed region.
+A step is one call of triton_mla_sparse_attention on one token's index set.
+The K timed calls run back to back inside CUDA graphs, like the layers of one
+decode step: call j reads cache replica j % 8 (8 x 138 MB, far above the
+126 MB L2) with its own index set, and an L2-flushing write precedes every
+timed graph replay, so gathered rows come from HBM.  `value` = device time per
+call (CUDA events around each replay / calls), whole-job: max over ranks,
+divided by the number of ranks (each rank serves its own independent B=1
+requests; the path needs no collective).  `e2e` is the same call through the
+public API with inputs copied from pinned host memory and the output copied
+back inside the timed region.  Per-call CUDA events tick at 2.048 us on this
+platform, so single-call latency (`secondary.isolated_call_us`) is coarse.
 
 Secondary measurements ride along in "secondary": store_int8 cache fill
 (config 2 fill, 408.9 MB), B=8 decode sharded over ranks (config 3),
@@ -264,10 +268,61 @@ def alg_bytes(idx_cpu):
 
 
 # ------------------------------------------------------------------ our arm
+REPLICAS = 8          # KV-cache replicas (one per "layer"), 8 x 138 MB >> 126 MB L2
+MAX_CALLS_PER_GRAPH = 512
+
+
+def graph_calls(k):
+    """Calls per captured graph so that k timed calls are whole graph replays."""
+    if k <= MAX_CALLS_PER_GRAPH:
+        return k
+    return max(d for d in range(1, MAX_CALLS_PER_GRAPH + 1) if k % d == 0)
+
+
+class DecodeBench:
+    """`calls` decode calls captured back to back in one CUDA graph, call j on
+    cache replica j % REPLICAS with its own index set, like consecutive layers
+    of one decode step.  Every timed replay starts after an L2-flushing write,
+    and one replay touches calls x ~1.1 MB of distinct rows, so the gathered
+    rows come from HBM; q and indices are per call, as the producers leave them."""
+
+    def __init__(self, attn, kvs, batch, calls, seed, tail_mode, sms, splits=None):
+        q, idx = decode_sets(batch, calls, seed, tail_mode=tail_mode)
+        self.bytes_per_call = statistics.fmean(alg_bytes(idx[j]) for j in range(calls))
+        dev = kvs[0].device
+        self.q, self.idx = q.to(dev), idx.to(dev)
+        self.calls = calls
+        kw = {"num_kv_splits": splits} if splits else {"sm_count": sms}
+
+        def run():
+            for j in range(calls):
+                attn(self.q[j], kvs[j % len(kvs)], self.idx[j], SM_SCALE, **kw)
+        self.graph, _ = capture(run)
+
+    def time(self, replays, flush):
+        """Device ms of each replay (CUDA events), L2 flushed before each."""
+        return timed_cold(lambda k: self.graph.replay(), replays, flush)
+
+    def close(self):
+        self.graph.reset()
+
+
+def splits_and_launches(batch, sms, device_index):
+    """Split count the B200 policy picks and kernel launches per call."""
+    from kernels.titan_mla import _choose_kv_splits_b200, _max_active_clusters
+    table = _max_active_clusters(device_index)
+    S = _choose_kv_splits_b200(batch, 1, TOPK, sms, table)
+    max_c = max([c for c, n in table.items() if n > 0] or [1])
+    C = 1
+    while C * 2 <= min(16, max_c) and S % (C * 2) == 0:
+        C *= 2
+    return S, C, (1 if S // C == 1 else 2)
+
+
 def run_ours(args, dist):
     from kernels import titan_native
     from kernels.titan_kv import store_int8
-    from kernels.titan_mla import _choose_num_kv_splits, triton_mla_sparse_attention as attn
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
     from kernels.titan_moe_align import titan_moe_align_small
 
     rank, world = dist.rank, dist.world
@@ -279,98 +334,116 @@ def run_ours(args, dist):
     K, W = args.steps, args.warmup
     sampler = ClockSampler(dev)
 
-    # ---- cache: config 2 fill by store_int8 (identical replica on every rank)
+    # ---- caches: config 2 (262,144 rows x 528 B), filled by store_int8; the
+    # same seeded replicas on every rank
     lat = latents(KV_ROWS, 1234, dev)
-    cache = torch.zeros(KV_ROWS // BLOCK, BLOCK, ROW_BYTES, dtype=torch.int8, device=dev)
     slots = torch.arange(KV_ROWS, device=dev)
-    kv = cache.view(KV_ROWS, 1, ROW_BYTES)
-    store_int8(lat, cache, slots)
+    caches = []
+    for r in range(REPLICAS):
+        c = torch.empty(KV_ROWS // BLOCK, BLOCK, ROW_BYTES, dtype=torch.int8, device=dev)
+        store_int8(latents(KV_ROWS, 1234 + r, dev) if r else lat, c, slots)
+        caches.append(c)
+    kvs = [c.view(KV_ROWS, 1, ROW_BYTES) for c in caches]
     torch.cuda.synchronize()
 
     sampler.start()
     dist.barrier()
-    # ---- headline: B=1 decode, CUDA-graph replay, cold L2
-    sets = args.index_sets
-    q_sets, idx_sets = decode_sets(1, sets, 99 + rank)
-    q_dev, idx_dev = q_sets.to(dev), idx_sets.to(dev)
-    q_static = q_dev[0].clone()
-    idx_static = idx_dev[0].clone()
-    splits = _choose_num_kv_splits(1, 1, TOPK, sms)
-    graph, _ = capture(lambda: attn(q_static, kv, idx_static, SM_SCALE, sm_count=sms))
-
-    def load(k):
-        q_static.copy_(q_dev[k % sets])
-        idx_static.copy_(idx_dev[k % sets])
-
-    timed_cold(lambda k: graph.replay(), W, flush, load)
+    # ---- headline: B=1 decode, K calls back to back (CUDA graphs), cold rows
+    J = graph_calls(K)
+    S1, C1, launches_per_call = splits_and_launches(1, sms, dev.index)
+    d1 = DecodeBench(attn, kvs, 1, J, 99 + rank, "fixed", sms)
+    d1.time(max(1, W // J + 1), flush)                     # warm-up replays (>= W calls)
     dist.barrier()
-    ms = timed_cold(lambda k: graph.replay(), K, flush, load)
+    ms = d1.time(K // J, flush)
     dist.barrier()
-    mean_ms = statistics.fmean(ms)
-    rank_max_ms = dist.max(mean_ms)
+    per_call_ms = sum(ms) / K
+    rank_max_ms = dist.max(per_call_ms)
     value_us = rank_max_ms * 1000.0 / world
-    bytes_per_call = statistics.fmean(alg_bytes(idx_sets[k % sets]) for k in range(sets))
-    achieved = bytes_per_call / (mean_ms * 1e-3) / 1e9
-    achieved = dist.max(-achieved) * -1.0  # slowest rank's bandwidth
-    launches_per_call = 1 if splits == 1 else 2
+    bytes_per_call = d1.bytes_per_call
+    achieved = dist.max(-(bytes_per_call / (per_call_ms * 1e-3) / 1e9)) * -1.0  # slowest rank
+    d1.close()
 
-    # ---- e2e: public API, pinned host inputs and output inside the timed region
+    # ---- isolated single call (flush, then one call): latency, 2.048-us event ticks
+    q1, i1 = decode_sets(1, 16, 7 + rank)
+    q1d, i1d = q1.to(dev), i1.to(dev)
+    qs, ids = q1d[0].clone(), i1d[0].clone()
+    g1, _ = capture(lambda: attn(qs, kvs[0], ids, SM_SCALE, sm_count=sms))
+
+    def load1(k):
+        qs.copy_(q1d[k % 16])
+        ids.copy_(i1d[k % 16])
+
+    timed_cold(lambda k: g1.replay(), 3, flush, load1)
+    iso_us = statistics.fmean(timed_cold(lambda k: g1.replay(), max(10, min(K, 100)), flush, load1)) * 1000
+    g1.reset()
+
+    # ---- e2e: public API, pinned host inputs and output copy inside the timed region
+    sets = 64
+    q_sets, idx_sets = decode_sets(1, sets, 199 + rank)
     q_host = q_sets.pin_memory()
     idx_host = idx_sets.pin_memory()
     out_host = torch.empty((sets, 1, HEADS, 512), dtype=torch.bfloat16).pin_memory()
-    qd = torch.empty_like(q_dev[0])
-    idd = torch.empty_like(idx_dev[0])
+    qd = torch.empty(1, HEADS, 512, dtype=torch.bfloat16, device=dev)
+    idd = torch.empty(1, 1, TOPK, dtype=torch.int32, device=dev)
 
     def e2e_step(k):
         qd.copy_(q_host[k % sets], non_blocking=True)
         idd.copy_(idx_host[k % sets], non_blocking=True)
-        o = attn(qd, kv, idd, SM_SCALE, sm_count=sms)
+        o = attn(qd, kvs[k % REPLICAS], idd, SM_SCALE, sm_count=sms)
         out_host[k % sets].copy_(o, non_blocking=True)
 
-    timed_cold(e2e_step, W, flush)
+    for k in range(W):
+        e2e_step(k)
+    flush()
     dist.barrier()
-    e2e_ms = timed_cold(e2e_step, K, flush)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for k in range(K):
+        e2e_step(k)
+    b.record()
+    torch.cuda.synchronize()
     dist.barrier()
-    e2e_us = dist.max(statistics.fmean(e2e_ms)) * 1000.0 / world
-    graph.reset()
+    e2e_us = dist.max(a.elapsed_time(b) / K) * 1000.0 / world
 
-    secondary = {}
-    # ---- store_int8: config 2 fill, 262,144 rows
+    secondary = {"isolated_call_us": iso_us}
+    # ---- store_int8: config 2 fill, 262,144 rows, 10 fills back to back
     fill_bytes = KV_ROWS * (1024 + ROW_BYTES + 8)
-    st_ms = timed_cold(lambda k: store_int8(lat, cache, slots), max(3, min(K, 20)), flush)
-    st_mean = dist.max(statistics.fmean(st_ms))
-    st_gbs = fill_bytes / (st_mean * 1e-3) / 1e9
+    nf = 10
+    for _ in range(2):
+        store_int8(lat, caches[0], slots)
+    a.record()
+    for _ in range(nf):
+        store_int8(lat, caches[0], slots)
+    b.record()
+    torch.cuda.synchronize()
+    st_ms = dist.max(a.elapsed_time(b) / nf)
     perm = torch.randperm(KV_ROWS, device=dev)
-    stp_ms = timed_cold(lambda k: store_int8(lat, cache, perm), max(3, min(K, 20)), flush)
-    stp_mean = dist.max(statistics.fmean(stp_ms))
+    a.record()
+    for _ in range(nf):
+        store_int8(lat, caches[1], perm)
+    b.record()
+    torch.cuda.synchronize()
+    stp_ms = dist.max(a.elapsed_time(b) / nf)
     secondary["store_int8"] = {
-        "rows": KV_ROWS, "bytes": fill_bytes, "us": st_mean * 1000, "GBps": st_gbs,
-        "frac_of_hbm": st_gbs / peak, "random_perm_us": stp_mean * 1000,
-        "random_perm_GBps": fill_bytes / (stp_mean * 1e-3) / 1e9, "per_rank": True}
-    store_int8(lat, cache, slots)  # restore the arange layout
+        "rows": KV_ROWS, "bytes": fill_bytes, "us": st_ms * 1000, "GBps": fill_bytes / (st_ms * 1e-3) / 1e9,
+        "frac_of_hbm": fill_bytes / (st_ms * 1e-3) / 1e9 / peak, "random_perm_us": stp_ms * 1000,
+        "random_perm_GBps": fill_bytes / (stp_ms * 1e-3) / 1e9, "per_rank": True}
+    store_int8(lat, caches[0], slots)
+    store_int8(latents(KV_ROWS, 1235, dev), caches[1], slots)
 
     # ---- config 3: B=8 decode, tokens sharded contiguously over ranks
     lo, hi = token_block(8, world, rank)
     per = max(1, hi - lo)
-    lo = min(lo, 8 - per)
-    q8, i8 = decode_sets(8, 8, 777, tail_mode="random")
-    q8d, i8d = q8[:, lo:lo + per].contiguous().to(dev), i8[:, lo:lo + per].contiguous().to(dev)
-    q8s, i8s = q8d[0].clone(), i8d[0].clone()
-    g8, _ = capture(lambda: attn(q8s, kv, i8s, SM_SCALE, sm_count=sms))
-
-    def load8(k):
-        q8s.copy_(q8d[k % 8])
-        i8s.copy_(i8d[k % 8])
-
-    timed_cold(lambda k: g8.replay(), W, flush, load8)
+    J8 = graph_calls(min(K, 256))
+    d8 = DecodeBench(attn, kvs, per, J8, 777 + rank, "random", sms)
+    d8.time(1, flush)
     dist.barrier()
-    b8_ms = dist.max(statistics.fmean(timed_cold(lambda k: g8.replay(), K, flush, load8)))
-    b8_bytes = statistics.fmean(alg_bytes(i8[k % 8, lo:lo + per]) for k in range(8))
+    b8_ms = dist.max(sum(d8.time(max(1, min(K, 256) // J8), flush)) / (max(1, min(K, 256) // J8) * J8))
+    S8, C8, _ = splits_and_launches(per, sms, dev.index)
     secondary["decode_b8"] = {
         "tokens_per_rank": per, "us_per_call": b8_ms * 1000, "tokens_per_s": per * world / (b8_ms * 1e-3),
-        "GBps_per_rank": b8_bytes / (b8_ms * 1e-3) / 1e9,
-        "splits": _choose_num_kv_splits(per, 1, TOPK, sms)}
-    g8.reset()
+        "GBps_per_rank": d8.bytes_per_call / (b8_ms * 1e-3) / 1e9, "splits": S8, "cluster": C8}
+    d8.close()
 
     # ---- config 4: prefill-shaped, T=4096 tokens sharded over ranks
     if not args.skip_prefill:
@@ -380,8 +453,8 @@ def run_ours(args, dist):
         qp = torch.randn(tp, HEADS, 512, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(
             torch.bfloat16)
         npf = max(3, min(K, 10))
-        timed_cold(lambda k: attn(qp, kv, ip, SM_SCALE, sm_count=sms), 2, flush)
-        pf_ms = dist.max(statistics.fmean(timed_cold(lambda k: attn(qp, kv, ip, SM_SCALE, sm_count=sms), npf,
+        timed_cold(lambda k: attn(qp, kvs[0], ip, SM_SCALE, sm_count=sms), 2, flush)
+        pf_ms = dist.max(statistics.fmean(timed_cold(lambda k: attn(qp, kvs[0], ip, SM_SCALE, sm_count=sms), npf,
                                                      flush)))
         nvalid = int(((ip >= 0) & (ip < KV_ROWS)).sum())
         secondary["prefill_t4096"] = {
@@ -398,7 +471,6 @@ def run_ours(args, dist):
             gr.replay()
         samples = []
         for _ in range(5):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             for _ in range(100):
                 gr.replay()
@@ -411,10 +483,10 @@ def run_ours(args, dist):
     clocks = sampler.stop()
     dist.barrier()
 
-    err = titan_native.device_error(cache)
+    err = titan_native.device_error(caches[0])
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
-        cpu = cpu_baseline_b1(cache, q_sets, idx_sets, args.cpu_seconds)
+        cpu = cpu_baseline_b1(caches[0], q_sets, idx_sets, args.cpu_seconds)
 
     if rank == 0:
         traffic = profile_traffic("mla_decode_b1")
@@ -426,17 +498,20 @@ def run_ours(args, dist):
                 "workload": "config2: B=1 sparse MLA decode, 16 heads x 512 NoPE latent, 262144-row INT8 "
                             "528-B-row cache filled by store_int8, 2176 indices (2048 distinct valid + 128 x -1)",
                 "kv_rows": KV_ROWS, "heads": HEADS, "topk": TOPK, "valid_per_token": VALID,
-                "index_sets": sets, "num_kv_splits": splits, "sm_count": sms,
-                "l2": "flushed (256 MiB write) before every timed call",
-                "timing": "CUDA graph replay of one call, CUDA events per call, mean over steps, max over ranks",
+                "num_kv_splits": S1, "cluster": C1, "sm_count": sms,
+                "l2": f"inputs larger than L2: {REPLICAS} cache replicas ({REPLICAS * KV_ROWS * ROW_BYTES / 1e9:.2f} GB) "
+                      f"rotated per call and {J} distinct index sets per graph replay, plus a 256 MiB L2-flushing "
+                      "write before each timed replay",
+                "timing": f"{J} calls back to back per CUDA graph replay, CUDA events per replay, per-call mean, "
+                          "max over ranks",
                 "parallelism": f"replicas x{world} (independent B=1 requests per GPU, no collective)"},
             "per_gpu_us_per_call": rank_max_ms * 1000.0,
             "tokens_per_s": world / (rank_max_ms * 1e-3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "algorithmic_bytes_per_call": bytes_per_call,
-                         "kernel": "sparse_mla_kernel<split> + combine (whole call)"},
-            "e2e": {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": q_dev[0].numel() * 2 + idx_dev[0].numel() * 4,
+                         "kernel": "sparse_mla_kernel + combine (whole call, back to back)"},
+            "e2e": {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": q_sets[0].numel() * 2 + idx_sets[0].numel() * 4,
                     "d2h_bytes_per_step": HEADS * 512 * 2},
             "gpu_launches": K * launches_per_call,
             "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"],

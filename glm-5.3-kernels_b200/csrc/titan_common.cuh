@@ -189,17 +189,20 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Address of the same shared-memory variable in CTA `rank` of this cluster.
-__device__ __forceinline__ uint32_t dsmem_map(const void *p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
+// Split cluster barrier: arrive early (non-blocking), wait later.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ float2 ld_dsmem_f32x2(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
-  return v;
+// Generic pointer to the same shared-memory variable in CTA `rank` of this
+// cluster.  Loads through it are ordinary loads (the compiler may batch them);
+// cluster_sync()'s memory clobber keeps them after the barrier.
+template <typename T>
+__device__ __forceinline__ T *dsmem_ptr(T *p, uint32_t rank) {
+  uint64_t r;
+  asm("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+  return reinterpret_cast<T *>(r);
 }
 
 __device__ __forceinline__ float ld_global_nc_f32(const void *p) {

@@ -41,7 +41,6 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kBN = 32;                     // rows per tile (four 8-row n-tiles)
 constexpr int kRedStride = 40;              // floats per head row of a warp's partial scores
 constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (bf16, 32 rows + pad)
-constexpr int kMbStride = kD + 16;          // floats per head row of the cluster merge buffer
 constexpr int kMaxCluster = 16;
 constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
 constexpr float kLn2 = 0.6931471805599453f;
@@ -49,7 +48,8 @@ constexpr float kLn2 = 0.6931471805599453f;
 struct Smem {
   float red[kWarps][kHeads * kRedStride];  // partial scores of each warp
   uint32_t p[kHeads * kPStrideWords];      // bf16(p * scale), n-order
-  float mb[kHeads * kMbStride];            // this CTA's acc, read by the cluster
+  float rcv[kHeads * kD];                  // cluster merge: [C][16][512/C] slices pushed by the peers
+  float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
   float scale[kBN];                        // row scales of the tile, n-order
   uint32_t vword[4];                       // per n-tile: bit 4n = row n valid
   float alpha[kHeads];
@@ -72,6 +72,7 @@ struct Params {
   int T, H, Hp;
   int S;            // splits per (token, head group)
   int C;            // splits per cluster (1, 2, 4, 8 or 16; divides S)
+  int logC;         // log2(C)
   int NC;           // clusters per (token, head group) = S / C = partials to combine
   int64_t split_topk;
   float scale_log2;  // sm_scale * log2(e)
@@ -93,7 +94,14 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
   const int split = blockIdx.x - t * p.S;
   const int hg = blockIdx.y;
 
-  if constexpr (kPartialOut) pdl_launch_dependents();
+  // Launched as a programmatic dependent of whatever ran before on the stream:
+  // CTAs may be resident early, but nothing is read before the previous grid
+  // has completed and flushed.
+  pdl_wait_primary();
+  pdl_launch_dependents();  // the combine (or the next call) may become resident now
+  // Cluster peers must be running before anyone writes into their shared
+  // memory: arrive now, wait right before the first remote store.
+  if (p.C > 1) cluster_arrive_relaxed();
 
   const int64_t start = (int64_t)split * p.split_topk;
   const int64_t end = min(start + p.split_topk, p.topk);
@@ -331,58 +339,63 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
     return;
   }
 
-  // Cluster merge: publish this CTA's acc, then CTA `rank` reduces dims
-  // [rank * 512 / C, (rank + 1) * 512 / C) over the C CTAs of the cluster.
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    float4 *dst = reinterpret_cast<float4 *>(&sm.mb[(g + 8 * half) * kMbStride + dim0]);
-#pragma unroll
-    for (int s = 0; s < 4; ++s)
-      dst[s] = make_float4(acc[2 * s][2 * half], acc[2 * s][2 * half + 1], acc[2 * s + 1][2 * half],
-                           acc[2 * s + 1][2 * half + 1]);
+  // Cluster merge (push): CTA `rank` owns dims [rank * D, rank * D + D),
+  // D = 512 / C.  Every CTA stores its (m, l) into all peers and each of its
+  // 16-dim acc pieces into the owner's slot for it; after one cluster barrier
+  // each owner reduces its slice from its own shared memory.
+  const uint32_t rank = cluster_ctarank();
+  const int D = kD / C;
+  cluster_wait();  // all peers have started (arrived at kernel entry)
+  if ((tid & 15) == 0) {
+    const float2 ml = make_float2(m_run, l_run);
+    for (int r = 0; r < C; ++r) *dsmem_ptr(&sm.cml[rank][red_h], (uint32_t)r) = ml;
   }
-  cluster_sync();
-  if (tid < kHeads) {
-    float2 ml[kMaxCluster];
-    float M = kNegLarge;
+  {
+    const int owner = dim0 / D;  // 16 | D, so a lane's 16 dims have one owner
+    const int dd = dim0 - owner * D;
 #pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) {
-      if (r < C) {
-        ml[r] = ld_dsmem_f32x2(dsmem_map(&sm.ml[tid], (uint32_t)r));
-        M = fmaxf(M, ml[r].x);
-      }
+    for (int half = 0; half < 2; ++half) {
+      const int hl = g + 8 * half;
+      float4 *dst = reinterpret_cast<float4 *>(dsmem_ptr(&sm.rcv[((int)rank * kHeads + hl) * D + dd], (uint32_t)owner));
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        dst[s] = make_float4(acc[2 * s][2 * half], acc[2 * s][2 * half + 1], acc[2 * s + 1][2 * half],
+                             acc[2 * s + 1][2 * half + 1]);
     }
+  }
+  cluster_sync();  // all pushes landed; from here on only local shared memory is read
+  if (tid < kHeads) {
+    float M = kNegLarge;
+    for (int r = 0; r < C; ++r) M = fmaxf(M, sm.cml[r][tid].x);
     float L = 0.0f;
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) {
-      if (r < C) {
-        const float w = ex2_approx(ml[r].x - M);
-        sm.cw[r][tid] = w;
-        L += w * ml[r].y;
-      }
+    for (int r = 0; r < C; ++r) {
+      const float w = ex2_approx(sm.cml[r][tid].x - M);
+      sm.cw[r][tid] = w;
+      L += w * sm.cml[r][tid].y;
     }
     sm.cM[tid] = M;
     sm.cL[tid] = L;
   }
   __syncthreads();
-  const uint32_t rank = cluster_ctarank();
-  const int D = kD / C;
-  const int pairs = kHeads * D / 2;  // float2 outputs of this CTA
-#pragma unroll 2
+  const int pair_shift = 8 - p.logC;       // log2(D / 2)
+  const int pairs = kHeads << pair_shift;  // float2 outputs of this CTA
   for (int pp = tid; pp < pairs; pp += kThreads) {
-    const int h = pp / (D / 2);
-    const int d = (int)rank * D + 2 * (pp - h * (D / 2));
+    const int h = pp >> pair_shift;
+    const int dd = 2 * (pp - (h << pair_shift));
+    float2 v[kMaxCluster];
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r)  // issue every load before any use
+      if (r < C) v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + h) * D + dd]);
     float2 sum = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) {
+    for (int r = 0; r < kMaxCluster; ++r)
       if (r < C) {
-        const float2 v = ld_dsmem_f32x2(dsmem_map(&sm.mb[h * kMbStride + d], (uint32_t)r));
         const float w = sm.cw[r][h];
-        sum.x += w * v.x;
-        sum.y += w * v.y;
+        sum.x += w * v[r].x;
+        sum.y += w * v[r].y;
       }
-    }
     const int hh = hg * kHeads + h;
+    const int d = (int)rank * D + dd;
     if (hh < p.H) {
       const float L = sm.cL[h];
       const float inv = L > 0.0f ? 1.0f / L : 1.0f;
@@ -399,7 +412,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
     if (rank == 0 && tid < kHeads && hg * kHeads + tid < p.H)
       p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (sm.cM[tid] + lg2_approx(sm.cL[tid])) * kLn2;
   }
-  cluster_sync();  // keep this CTA's shared memory alive until the cluster has read it
 }
 
 // Combine: one CTA per (token, head group, 16-dim chunk), 256 threads.
@@ -415,6 +427,7 @@ constexpr int kCombineThreads = 256;
 
 __global__ void __launch_bounds__(kCombineThreads) sparse_mla_combine_kernel(const Params p) {
   pdl_wait_primary();
+  pdl_launch_dependents();
   __shared__ float s_max[kHeads];
   __shared__ float s_inv[kHeads];
   __shared__ float4 s_part[kCombineGroups][kHeads * kCombineDims / 4];
@@ -423,40 +436,63 @@ __global__ void __launch_bounds__(kCombineThreads) sparse_mla_combine_kernel(con
   const int tid = threadIdx.x;
   const int S = p.NC;  // partials to merge
   const float *lse_t = p.part_lse + (int64_t)t * S * p.Hp + hg * kHeads;
+  const int grp = tid >> 6;            // split group
+  const int pair = tid & 63;           // (head, float4 column)
+  const int h = pair >> 2, c4 = pair & 3;
+  const int hh = hg * kHeads + h;
+  const int dim = chunk * kCombineDims + c4 * 4;
+  const float *o_t = p.part_o + ((int64_t)t * S * p.Hp + hh) * kD + dim;
+  const int64_t split_stride = (int64_t)p.Hp * kD;
+
+  // 0. issue this thread's first partial loads before the max/sum phase
+  constexpr int kPre = 2;
+  float4 o_pre[kPre];
+  float lse_pre[kPre];
+#pragma unroll
+  for (int k = 0; k < kPre; ++k) {
+    const int s = grp + kCombineGroups * k;
+    o_pre[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    lse_pre[k] = -INFINITY;
+    if (s < S && hh < p.H) {
+      o_pre[k] = *reinterpret_cast<const float4 *>(o_t + s * split_stride);
+      lse_pre[k] = lse_t[(int64_t)s * p.Hp + h];
+    }
+  }
 
   {  // 1. per-head max and normaliser
-    const int h = tid >> 4, j = tid & 15;
-    const bool live = hg * kHeads + h < p.H;
+    const int hr = tid >> 4, j = tid & 15;
+    const bool live = hg * kHeads + hr < p.H;
     float m = kNegLarge;
     if (live)
-      for (int s = j; s < S; s += 16) m = fmaxf(m, lse_t[(int64_t)s * p.Hp + h]);
+      for (int s = j; s < S; s += 16) m = fmaxf(m, lse_t[(int64_t)s * p.Hp + hr]);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float sum = 0.0f;
     if (live)
-      for (int s = j; s < S; s += 16) sum += ex2_approx((lse_t[(int64_t)s * p.Hp + h] - m) * kLog2e);
+      for (int s = j; s < S; s += 16) sum += ex2_approx((lse_t[(int64_t)s * p.Hp + hr] - m) * kLog2e);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (j == 0) {
-      s_max[h] = m;
-      s_inv[h] = sum > 0.0f ? 1.0f / sum : 1.0f;
+      s_max[hr] = m;
+      s_inv[hr] = sum > 0.0f ? 1.0f / sum : 1.0f;
     }
   }
   __syncthreads();
 
   // 2. weighted sum of the partial outputs
-  const int grp = tid >> 6;            // split group
-  const int pair = tid & 63;           // (head, float4 column)
-  const int h = pair >> 2, c4 = pair & 3;
-  const int hh = hg * kHeads + h;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (hh < p.H) {
     const float m = s_max[h];
-    const int dim = chunk * kCombineDims + c4 * 4;
-    const float *o_t = p.part_o + ((int64_t)t * S * p.Hp + hh) * kD + dim;
-    const int64_t split_stride = (int64_t)p.Hp * kD;
+#pragma unroll
+    for (int k = 0; k < kPre; ++k) {
+      const float w = ex2_approx((lse_pre[k] - m) * kLog2e);
+      acc.x += w * o_pre[k].x;
+      acc.y += w * o_pre[k].y;
+      acc.z += w * o_pre[k].z;
+      acc.w += w * o_pre[k].w;
+    }
 #pragma unroll 4
-    for (int s = grp; s < S; s += kCombineGroups) {
+    for (int s = grp + kCombineGroups * kPre; s < S; s += kCombineGroups) {
       const float w = ex2_approx((lse_t[(int64_t)s * p.Hp + h] - m) * kLog2e);
       const float4 o = *reinterpret_cast<const float4 *>(o_t + s * split_stride);
       acc.x += w * o.x;
@@ -480,7 +516,6 @@ __global__ void __launch_bounds__(kCombineThreads) sparse_mla_combine_kernel(con
     uint2 r;
     r.x = pack_bf16x2(acc.x * inv, acc.y * inv);
     r.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-    const int dim = chunk * kCombineDims + c4 * 4;
     *reinterpret_cast<uint2 *>(p.out + (int64_t)t * p.out_st + (int64_t)hh * p.out_sh + dim) = r;
   }
 }
@@ -503,9 +538,9 @@ static cudaError_t launch_combine(const Params &prm, int groups, cudaStream_t s)
 // cluster size opt-in, and the largest cluster size the device can schedule
 // for this kernel (queried, not assumed).
 static bool g_dev_ready[64] = {false};
-static int g_max_cluster[64] = {0};
+static int g_cluster_capacity[64][kMaxCluster + 1];  // [dev][C] co-resident clusters of C CTAs
 
-static int prepare_device(size_t smem, int *max_cluster) {
+static int prepare_device(size_t smem, const int **capacity) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: cudaGetDevice: %s", cudaGetErrorString(e));
@@ -517,8 +552,11 @@ static int prepare_device(size_t smem, int *max_cluster) {
       if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: kernel attributes: %s", cudaGetErrorString(e));
     }
-    int best = 1;
-    for (int cs = kMaxCluster; cs >= 2; cs >>= 1) {
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    for (int cs = 0; cs <= kMaxCluster; ++cs) g_cluster_capacity[dev][cs] = 0;
+    g_cluster_capacity[dev][1] = sms;
+    for (int cs = 2; cs <= kMaxCluster; cs <<= 1) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3((unsigned)cs, 1, 1);
       cfg.blockDim = dim3(kThreads);
@@ -531,21 +569,57 @@ static int prepare_device(size_t smem, int *max_cluster) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg) == cudaSuccess && n > 0) {
-        best = cs;
-        break;
+      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg) != cudaSuccess) {
+        cudaGetLastError();  // clear a rejected query: that size is not schedulable
+        n = 0;
       }
-      cudaGetLastError();  // clear a rejected query
+      g_cluster_capacity[dev][cs] = n;
     }
-    g_max_cluster[dev] = best;
     g_dev_ready[dev] = true;
   }
-  *max_cluster = g_max_cluster[dev];
+  *capacity = g_cluster_capacity[dev];
   return TITAN_OK;
+}
+
+// Cluster size for `clusters_per_split_unit` (= tokens x head groups) units of
+// S splits: the largest power of two <= 16 that divides S and whose clusters
+// all fit on the device at once (else the grid would run in waves and the
+// cluster merge would wait on the second wave).
+static int choose_cluster(int64_t units, int64_t S, const int *capacity) {
+  int C = 1;
+  for (int cs = 2; cs <= kMaxCluster; cs <<= 1) {
+    if (S % cs != 0) break;
+    if (units * (S / cs) <= capacity[cs]) C = cs;
+  }
+  return C;
 }
 
 }  // namespace mla
 }  // namespace titan
+
+extern "C" int titan_mla_max_active_clusters(int cluster_size) {
+  using namespace titan::mla;
+  if (cluster_size < 1 || cluster_size > kMaxCluster) return -1;
+  const int *capacity = nullptr;
+  if (prepare_device(sizeof(Smem), &capacity) != TITAN_OK) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cluster_size, 1, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sizeof(Smem);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster_size;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return n;
+}
 
 extern "C" int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_heads, int64_t num_kv_splits) {
   using namespace titan::mla;
@@ -591,13 +665,11 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   }
 
   const size_t smem = sizeof(Smem);
-  int max_cluster = 1;
-  int rc = prepare_device(smem, &max_cluster);
+  const int *capacity = nullptr;
+  int rc = prepare_device(smem, &capacity);
   if (rc != TITAN_OK) return rc;
-  // Cluster size: the largest power of two <= the schedulable maximum that
-  // divides the split count; NC clusters (partials) per (token, head group).
-  int C = 1;
-  while (C * 2 <= max_cluster && num_kv_splits % (C * 2) == 0) C *= 2;
+  // NC clusters (partials) of C splits per (token, head group).
+  const int C = choose_cluster(num_tokens * groups, num_kv_splits, capacity);
   const int64_t NC = num_kv_splits / C;
 
   Params prm;
@@ -618,6 +690,8 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   prm.Hp = (int)(groups * kHeads);
   prm.S = (int)num_kv_splits;
   prm.C = C;
+  prm.logC = 0;
+  while ((1 << prm.logC) < C) ++prm.logC;
   prm.NC = (int)NC;
   prm.split_topk = (topk + num_kv_splits - 1) / num_kv_splits;
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
@@ -635,13 +709,15 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)C;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = C > 1 ? 1 : 0;
+  cfg.numAttrs = C > 1 ? 2 : 1;
   cudaError_t e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true>, prm)
                          : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false>, prm);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla launch (C=%d): %s", C, cudaGetErrorString(e));

@@ -72,6 +72,58 @@ def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int
     return max(1, num_kv_splits)
 
 
+# Cost model of the B200 kernel, fitted to back-to-back B=1 / B=8 sweeps on
+# B200 (microseconds): one 32-row tile per CTA, the cluster merge, and the
+# combine launch (with a small per-partial term) when a token has >1 cluster.
+_TILE_ROWS = 32
+_COST_TILE_US = 1.25
+_COST_CLUSTER_MERGE_US = 0.6
+_COST_COMBINE_US = 1.4
+_COST_COMBINE_PER_PARTIAL_US = 0.025
+_MAX_CLUSTER = 16
+_max_clusters_cache = {}
+
+
+def _max_active_clusters(device_index):
+    """{cluster size: co-resident clusters} of the MLA kernel on this device."""
+    if device_index not in _max_clusters_cache:
+        lib = _native.load()
+        with torch.cuda.device(device_index):
+            table = {c: lib.titan_mla_max_active_clusters(c) for c in (1, 2, 4, 8, 16)}
+        _max_clusters_cache[device_index] = table
+    return _max_clusters_cache[device_index]
+
+
+def _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count, max_clusters):
+    """Auto split count for the B200 kernel.
+
+    Candidates are split counts S whose whole grid (tokens x groups x S CTAs,
+    one per SM) and whose clusters (C = largest power of two <= 16 dividing S
+    that the device can co-schedule in one wave) fit at once; the cheapest
+    under the cost model above wins (ties: more splits).  The reference's
+    `_choose_num_kv_splits` targets its own SM80 kernel and stays available.
+    """
+    units = num_tokens * num_head_groups
+    if units == 0 or units >= sm_count:
+        return 1
+    best, best_cost = 1, None
+    for S in range(1, sm_count // units + 1):
+        C = 1  # same rule as the launcher: largest power of two dividing S whose clusters all fit
+        cs = 2
+        while cs <= _MAX_CLUSTER and S % cs == 0:
+            if units * (S // cs) <= max(0, max_clusters.get(cs, 0)):
+                C = cs
+            cs *= 2
+        nc = S // C
+        rows = -(-index_topk // S)
+        cost = max(1, -(-rows // _TILE_ROWS)) * _COST_TILE_US
+        cost += _COST_CLUSTER_MERGE_US if C > 1 else 0.0
+        cost += (_COST_COMBINE_US + _COST_COMBINE_PER_PARTIAL_US * nc) if nc > 1 else 0.0
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = S, cost
+    return best
+
+
 def _aligned16(t):
     return t.data_ptr() % 16 == 0 and all((s * t.element_size()) % 16 == 0 for s in t.stride()[:-1])
 
@@ -91,7 +143,8 @@ def triton_mla_sparse_attention(
         kv:        [seq_kv, 1, 528] int8 packed cache (528-byte rows)
         indices:   [num_tokens, 1, topk] int32; entries outside [0, seq_kv) are masked
         sm_scale:  softmax scale
-        num_kv_splits: override the auto-heuristic; None/0 = auto, 1 = single pass.
+        num_kv_splits: override the auto-heuristic; None/0 = auto (the B200 policy,
+                   `_choose_kv_splits_b200`), 1 = single pass.
         sm_count:  cached device SM count for the split heuristic.
 
     Returns:
@@ -123,7 +176,8 @@ def triton_mla_sparse_attention(
     if num_kv_splits is None or num_kv_splits == 0:
         if sm_count is None:
             sm_count = num_compute_units(q.device.index)
-        num_kv_splits = _choose_num_kv_splits(num_tokens, num_head_groups, index_topk, sm_count)
+        num_kv_splits = _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count,
+                                               _max_active_clusters(q.device.index))
 
     out = torch.empty((num_tokens, num_heads_q, _BLOCK_DV), dtype=torch.bfloat16, device=q.device)
     if num_tokens == 0:

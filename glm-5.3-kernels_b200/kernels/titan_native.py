@@ -27,6 +27,7 @@ SIGNATURES = {
     "titan_last_error": (ctypes.c_char_p, []),
     "titan_store_int8": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _int, _i64, _vp]),
     "titan_mla_workspace_bytes": (_i64, [_i64, _i64, _i64]),
+    "titan_mla_max_active_clusters": (_int, [_int]),
     "titan_mla_sparse_attention": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64,

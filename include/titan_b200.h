@@ -82,6 +82,13 @@ int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_heads,
                                   int64_t num_kv_splits);
 
 /*
+ * Diagnostic: how many thread-block clusters of `cluster_size` CTAs (1..16) of
+ * the MLA kernel the current device can hold at once (-1 on error).  The
+ * launcher uses the same query to pick its cluster size.
+ */
+int titan_mla_max_active_clusters(int cluster_size);
+
+/*
  * Sparse NoPE MLA attention over an INT8 528-byte-row cache.  Replaces
  * `triton_mla_sparse_attention(q, kv, indices, sm_scale, num_kv_splits,
  * sm_count)`, kernels/titan_mla.py:452-581 (kernels :59-429).
