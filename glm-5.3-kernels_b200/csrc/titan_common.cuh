@@ -176,6 +176,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// 16-byte asynchronous global -> shared copy (per thread), grouped per thread.
+__device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
 // Thread-block cluster helpers (distributed shared memory).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -12,6 +12,8 @@
 // HBM traffic per row: 1024 B read + 528 B written + 8 B slot.
 #include "titan_common.cuh"
 
+#include <algorithm>
+
 namespace titan {
 
 constexpr int kKvWarpsPerCta = 8;
@@ -23,31 +25,40 @@ constexpr int kKvRowsPerWarp = 4;
 constexpr float kRoundMagic = 12582912.0f;
 
 // Quantise 16 values to 4 packed int8 words: q = rint(v / scale) with the
-// correctly rounded quotient.  y = v * fl(1/scale) differs from v / scale by
-// less than 2^-22 relative (|y| <= 127.1, so < 2^-15 absolute), hence
-// rint(y) == rint(fl(v / scale)) unless y lies within 2^-10 of a
-// half-integer; any lane that meets such a value recomputes its 16 values with
-// the IEEE division.  |q| <= 127 needs no clamp: scale >= fl(amax / 127)
-// keeps |v / scale| <= 127 (1 + 2^-24), which rounds to at most 127.
+// correctly rounded quotient.  With r = fl(1/scale), y = fl(v * r) satisfies
+// |y - v/scale| <= |v/scale| (2u + u^2) <= 1.52e-5 (u = 2^-24, |v/scale| <=
+// 127.00002), and the correctly rounded quotient is within half an ulp
+// (<= 3.9e-6) of v/scale, so |y - fl(v/scale)| < 1.91e-5.  rint(y) therefore
+// equals rint(fl(v/scale)) unless y lies within 1.91e-5 of a half-integer; such
+// values (window 2^-14 = 6.1e-5, ~3x margin) are recomputed one by one with
+// the IEEE division.  |q| <= 127 needs no clamp: scale >= fl(amax / 127) keeps
+// |v / scale| <= 127 (1 + 2^-24), which rounds to at most 127.
 __device__ __forceinline__ void quant16(const float (&v)[16], float scale, float rcp, uint32_t (&out)[4]) {
   float m[16];
-  bool near_half = false;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const float y = v[i] * rcp;
     m[i] = y + kRoundMagic;
     const float r = m[i] - kRoundMagic;
-    near_half |= fabsf(y - r) > 0.4990234375f;  // 0.5 - 2^-10
-  }
-  if (near_half) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) m[i] = __fdiv_rn(v[i], scale) + kRoundMagic;
+    if (fabsf(y - r) > 0.49993896484375f) m[i] = __fdiv_rn(v[i], scale) + kRoundMagic;  // 0.5 - 2^-14
   }
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
     const uint32_t lo = prmt(__float_as_uint(m[4 * w + 0]), __float_as_uint(m[4 * w + 1]), 0x0040u);
     const uint32_t hi = prmt(__float_as_uint(m[4 * w + 2]), __float_as_uint(m[4 * w + 3]), 0x0040u);
     out[w] = prmt(lo, hi, 0x5410u);
+  }
+}
+
+// Cache row of a slot: block = slot / block_size, offset = slot % block_size;
+// a shift when the block size is a power of two (block_shift >= 0).
+__device__ __forceinline__ void split_slot(int64_t slot, int64_t block, int block_shift, int64_t &blk, int64_t &off) {
+  if (block_shift >= 0) {
+    blk = slot >> block_shift;
+    off = slot & (block - 1);
+  } else {
+    blk = slot / block;
+    off = slot - blk * block;
   }
 }
 
@@ -70,7 +81,7 @@ __device__ __forceinline__ float row_scale(float amax) { return fmaxf(__fdiv_rn(
 template <typename SlotT>
 __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
     store_int8_vec_kernel(const __nv_bfloat16 *__restrict__ x, int64_t x_row_stride, int8_t *__restrict__ cache,
-                          int64_t num_blocks, int64_t block, int64_t cs0, int64_t cs1,
+                          int64_t num_blocks, int64_t block, int block_shift, int64_t cs0, int64_t cs1,
                           const SlotT *__restrict__ slots, int64_t n) {
   const int lane = threadIdx.x & 31;
   const int64_t row0 = ((int64_t)blockIdx.x * kKvWarpsPerCta + (threadIdx.x >> 5)) * kKvRowsPerWarp;
@@ -91,9 +102,9 @@ __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
 #pragma unroll
   for (int r = 0; r < kKvRowsPerWarp; ++r) {
     if (slot[r] < 0) continue;
-    const int64_t blk = slot[r] / block;
+    int64_t blk, off;
+    split_slot(slot[r], block, block_shift, blk, off);
     if (blk >= num_blocks) continue;
-    const int64_t off = slot[r] - blk * block;
     float v[16];
     bf16x2_to_f32(a[r].x, v[0], v[1]);
     bf16x2_to_f32(a[r].y, v[2], v[3]);
@@ -115,21 +126,140 @@ __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
   }
 }
 
+// Streaming kernel for 16-byte-aligned rows.  Persistent CTAs; every warp
+// independently quantises two rows per step (one per half-warp), streaming
+// its rows through a private 4-stage shared-memory ring filled with cp.async
+// (16 bytes per lane per copy), so ~8 KB per warp stay in flight without
+// holding registers.  Lane j of a half-warp owns 16-byte chunks j, j+16, j+32,
+// j+48 of its row (values [8j, 8j+8) + 128 k): conflict-free shared loads and
+// four coalesced 8-byte stores.  The abs-max runs on bf16 bit patterns
+// (max.u16x2), the quantisation on packed f32x2 arithmetic.
+constexpr int kKvStreamWarps = 8;
+constexpr int kKvStreamStages = 4;
+constexpr int kKvStageBytes = 2 * 1024;  // two rows
+constexpr size_t kKvStreamSmem = (size_t)kKvStreamWarps * kKvStreamStages * kKvStageBytes;
+
+__device__ __forceinline__ uint32_t umax16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// 32 values (16 bf16x2 words) of one row held by one lane -> 8 packed int8
+// words, four values at a time (same arithmetic and fallback as quant16).
+__device__ __forceinline__ void quant32(const uint32_t (&w)[16], float scale, float rcp, uint32_t (&out)[8]) {
+  const float2 rcp2 = make_float2(rcp, rcp);
+  const float2 mag2 = make_float2(kRoundMagic, kRoundMagic);
+  const float2 nmag2 = make_float2(-kRoundMagic, -kRoundMagic);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float2 m[2];
+    float dmax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const uint32_t wd = w[2 * k + e];
+      const float2 y = __fmul2_rn(make_float2(__uint_as_float(wd << 16), __uint_as_float(wd & 0xFFFF0000u)), rcp2);
+      m[e] = __fadd2_rn(y, mag2);
+      const float2 r = __fadd2_rn(m[e], nmag2);
+      dmax = fmaxf(dmax, fmaxf(fabsf(y.x - r.x), fabsf(y.y - r.y)));
+    }
+    if (dmax > 0.49993896484375f) {  // a value within 2^-14 of a half-integer: exact quotient
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t wd = w[2 * k + e];
+        m[e].x = __fdiv_rn(__uint_as_float(wd << 16), scale) + kRoundMagic;
+        m[e].y = __fdiv_rn(__uint_as_float(wd & 0xFFFF0000u), scale) + kRoundMagic;
+      }
+    }
+    const uint32_t lo = prmt(__float_as_uint(m[0].x), __float_as_uint(m[0].y), 0x0040u);
+    const uint32_t hi = prmt(__float_as_uint(m[1].x), __float_as_uint(m[1].y), 0x0040u);
+    out[k] = prmt(lo, hi, 0x5410u);
+  }
+}
+
+template <typename SlotT>
+__global__ void __launch_bounds__(kKvStreamWarps * 32, 3)
+    store_int8_stream_kernel(const __nv_bfloat16 *__restrict__ x, int64_t x_row_stride, int8_t *__restrict__ cache,
+                             int64_t num_blocks, int64_t block, int block_shift, int64_t cs0, int64_t cs1,
+                             const SlotT *__restrict__ slots, int64_t n) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, j = lane & 15;
+  uint8_t *ring = smem + (size_t)warp * kKvStreamStages * kKvStageBytes;
+  const int64_t gwarp = (int64_t)blockIdx.x * kKvStreamWarps + warp;
+  const int64_t nwarps = (int64_t)gridDim.x * kKvStreamWarps;
+  const int64_t pairs = (n + 1) / 2;
+  const int64_t my_steps = gwarp < pairs ? (pairs - 1 - gwarp) / nwarps + 1 : 0;
+  // Step i of this warp covers rows 2 (gwarp + i nwarps) + {0, 1}.
+  auto row_of = [&](int64_t i) { return 2 * (gwarp + i * nwarps) + half; };
+  auto fetch = [&](int64_t i) {  // this lane's 4 chunks of its row of step i
+    if (i < my_steps) {
+      const int64_t row = row_of(i);
+      if (row < n) {
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(x + row * x_row_stride);
+        uint8_t *dst = ring + (int)(i % kKvStreamStages) * kKvStageBytes + half * 1024;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) cp_async_16(dst + (j + 16 * k) * 16, src + (j + 16 * k) * 16);
+      }
+    }
+    cp_async_commit();  // empty groups keep the group count uniform
+  };
+#pragma unroll
+  for (int i = 0; i < kKvStreamStages - 1; ++i) fetch(i);
+  int64_t slot_next = (my_steps > 0 && row_of(0) < n) ? (int64_t)slots[row_of(0)] : -1;
+  for (int64_t i = 0; i < my_steps; ++i) {
+    fetch(i + kKvStreamStages - 1);
+    const int64_t slot = slot_next;
+    slot_next = (i + 1 < my_steps && row_of(i + 1) < n) ? (int64_t)slots[row_of(i + 1)] : -1;
+    cp_async_wait<kKvStreamStages - 1>();
+    __syncwarp();
+    const uint8_t *row = ring + (int)(i % kKvStreamStages) * kKvStageBytes + half * 1024;
+    uint32_t w[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 c = *reinterpret_cast<const uint4 *>(row + (j + 16 * k) * 16);
+      w[4 * k + 0] = c.x;
+      w[4 * k + 1] = c.y;
+      w[4 * k + 2] = c.z;
+      w[4 * k + 3] = c.w;
+    }
+    uint32_t mx = 0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) mx = umax16x2(mx, w[k] & 0x7FFF7FFFu);
+    mx = max(mx & 0xFFFFu, mx >> 16);  // |x| as bf16 bits; integer order = value order
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float scale = row_scale(__uint_as_float(mx << 16));
+    uint32_t q[8];
+    quant32(w, scale, __frcp_rn(scale), q);
+    __syncwarp();  // the stage may be refilled once every lane has read it
+    int64_t blk = 0, off = 0;
+    if (slot >= 0) split_slot(slot, block, block_shift, blk, off);
+    if (slot >= 0 && blk < num_blocks) {
+      int8_t *dst = cache + blk * cs0 + off * cs1;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) *reinterpret_cast<uint2 *>(dst + 8 * j + 128 * k) = make_uint2(q[2 * k], q[2 * k + 1]);
+      if (j == 0) *reinterpret_cast<uint4 *>(dst + 512) = make_uint4(__float_as_uint(scale), 0u, 0u, 0u);
+    }
+  }
+  cp_async_wait<0>();
+}
+
 // Unaligned fallback (x rows or cache rows not 16-byte aligned): lane l owns
 // values l + 32 k, byte stores.  Same arithmetic.
 template <typename SlotT>
 __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
     store_int8_scalar_kernel(const __nv_bfloat16 *__restrict__ x, int64_t x_row_stride, int8_t *__restrict__ cache,
-                             int64_t num_blocks, int64_t block, int64_t cs0, int64_t cs1,
+                             int64_t num_blocks, int64_t block, int block_shift, int64_t cs0, int64_t cs1,
                              const SlotT *__restrict__ slots, int64_t n) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kKvWarpsPerCta + (threadIdx.x >> 5);
   if (row >= n) return;
   const int64_t slot = (int64_t)slots[row];
   if (slot < 0) return;
-  const int64_t blk = slot / block;
+  int64_t blk, off;
+  split_slot(slot, block, block_shift, blk, off);
   if (blk >= num_blocks) return;
-  const int64_t off = slot - blk * block;
   const __nv_bfloat16 *src = x + row * x_row_stride;
   float v[16];
   float amax = 0.0f;
@@ -163,12 +293,47 @@ extern "C" int titan_store_int8(const void *x, int64_t x_row_stride, void *cache
   if (block_size <= 0 || num_blocks < 0)
     return fail(TITAN_ERR_INVALID_ARGUMENT, "store_int8: invalid cache geometry");
   const int64_t rows_per_cta_vec = kKvWarpsPerCta * kKvRowsPerWarp;
+  int block_shift = -1;
+  if ((block_size & (block_size - 1)) == 0) {
+    block_shift = 0;
+    while ((int64_t(1) << block_shift) < block_size) ++block_shift;
+  }
   const bool aligned = ((uintptr_t)x % 16 == 0) && ((x_row_stride * 2) % 16 == 0) && ((uintptr_t)cache % 16 == 0) &&
                        (cache_stride0 % 16 == 0) && (cache_stride1 % 16 == 0);
   const int64_t ctas = aligned ? (n_slots + rows_per_cta_vec - 1) / rows_per_cta_vec
                                : (n_slots + kKvWarpsPerCta - 1) / kKvWarpsPerCta;
   if (ctas > 0x7fffffffLL) return fail(TITAN_ERR_INVALID_ARGUMENT, "store_int8: too many rows");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (aligned && cache_stride1 % 8 == 0 && n_slots >= 1024) {
+    // Large batches: persistent streaming kernel, three CTAs per SM.
+    static bool attr_done[64] = {false};
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(store_int8_stream_kernel<int64_t>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kKvStreamSmem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(store_int8_stream_kernel<int32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kKvStreamSmem);
+      if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "store_int8: smem attribute: %s", cudaGetErrorString(e));
+      attr_done[dev] = true;
+    }
+    const int64_t warps_needed = (n_slots + 1) / 2;
+    const int64_t ctas_needed = (warps_needed + kKvStreamWarps - 1) / kKvStreamWarps;
+    const unsigned grid_s = (unsigned)std::min<int64_t>(ctas_needed, 3 * (int64_t)sms);
+    const __nv_bfloat16 *xb = static_cast<const __nv_bfloat16 *>(x);
+    int8_t *cb = static_cast<int8_t *>(cache);
+    if (slots_is_int64)
+      store_int8_stream_kernel<int64_t><<<grid_s, kKvStreamWarps * 32, kKvStreamSmem, s>>>(
+          xb, x_row_stride, cb, num_blocks, block_size, block_shift, cache_stride0, cache_stride1,
+          static_cast<const int64_t *>(slots), n_slots);
+    else
+      store_int8_stream_kernel<int32_t><<<grid_s, kKvStreamWarps * 32, kKvStreamSmem, s>>>(
+          xb, x_row_stride, cb, num_blocks, block_size, block_shift, cache_stride0, cache_stride1,
+          static_cast<const int32_t *>(slots), n_slots);
+    return check_launch("store_int8 (stream) launch");
+  }
   const dim3 grid((unsigned)ctas), block(kKvWarpsPerCta * 32);
   const __nv_bfloat16 *xb = static_cast<const __nv_bfloat16 *>(x);
   int8_t *cb = static_cast<int8_t *>(cache);
@@ -176,18 +341,18 @@ extern "C" int titan_store_int8(const void *x, int64_t x_row_stride, void *cache
     const int64_t *sl = static_cast<const int64_t *>(slots);
     if (aligned)
       store_int8_vec_kernel<int64_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                            cache_stride0, cache_stride1, sl, n_slots);
+                                                            block_shift, cache_stride0, cache_stride1, sl, n_slots);
     else
       store_int8_scalar_kernel<int64_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                               cache_stride0, cache_stride1, sl, n_slots);
+                                                               block_shift, cache_stride0, cache_stride1, sl, n_slots);
   } else {
     const int32_t *sl = static_cast<const int32_t *>(slots);
     if (aligned)
       store_int8_vec_kernel<int32_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                            cache_stride0, cache_stride1, sl, n_slots);
+                                                            block_shift, cache_stride0, cache_stride1, sl, n_slots);
     else
       store_int8_scalar_kernel<int32_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                               cache_stride0, cache_stride1, sl, n_slots);
+                                                               block_shift, cache_stride0, cache_stride1, sl, n_slots);
   }
   return check_launch("store_int8 launch");
 }

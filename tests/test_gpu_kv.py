@@ -97,6 +97,22 @@ def test_full_cache_fill_bit_exact(native_lib, cuda_device, order):
     assert nmse < 3e-4
 
 
+@pytest.mark.parametrize("n,slot_dtype", [(5000, torch.int32), (4097, torch.int64)])
+def test_bulk_path_partial_chunks(native_lib, cuda_device, n, slot_dtype):
+    """Contiguous latents above the bulk-path threshold with a row count that
+    leaves a partial last chunk, some negative slots, random slot order."""
+    from kernels.titan_kv import store_int8
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(n, 512, generator=g).to(torch.bfloat16)
+    slots = torch.randperm(8192, generator=g)[:n]
+    slots[::97] = -1
+    cache = torch.zeros(32, 256, 528, dtype=torch.int8, device=cuda_device)
+    store_int8(x.to(cuda_device), cache, slots.to(slot_dtype).to(cuda_device))
+    want = np.zeros((32, 256, 528), np.uint8)
+    O.store_int8(O.tensor_bf16_bits(x), want, slots.numpy())
+    assert np.array_equal(cache.cpu().numpy().view(np.uint8), want)
+
+
 def test_graph_capture_replay(native_lib, cuda_device):
     from kernels.titan_kv import store_int8
     x = C.kv_latents().to(cuda_device)
