@@ -205,6 +205,41 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
+// Shared::cluster address of the same shared-memory variable in CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Asynchronous remote stores into a peer CTA's shared memory that complete
+// (in bytes) on the peer's mbarrier; the sender never waits.
+__device__ __forceinline__ void st_async_f32x4(uint32_t addr, float4 v, uint32_t mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(mbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float2 v, uint32_t mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "f"(v.x), "f"(v.y), "r"(mbar)
+               : "memory");
+}
+
+// Bulk copy (TMA engine) from this CTA's shared memory into a peer CTA's shared
+// memory, completing in bytes on the peer's mbarrier.  dst/src 16-byte aligned,
+// bytes a multiple of 16.  The source must stay untouched until
+// bulk_wait_read_all() returns.
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, const void *src, uint32_t bytes,
+                                               uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // Generic pointer to the same shared-memory variable in CTA `rank` of this
 // cluster.  Loads through it are ordinary loads (the compiler may batch them);
 // cluster_sync()'s memory clobber keeps them after the barrier.

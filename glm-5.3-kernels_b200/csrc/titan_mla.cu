@@ -49,6 +49,7 @@ struct Smem {
   float red[kWarps][kHeads * kRedStride];  // partial scores of each warp
   uint32_t p[kHeads * kPStrideWords];      // bf16(p * scale), n-order
   float rcv[kHeads * kD];                  // cluster merge: [C][16][512/C] slices pushed by the peers
+  float stage[kHeads * kD];                // cluster merge: this CTA's acc as [owner][16][512/C]
   float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
   float scale[kBN];                        // row scales of the tile, n-order
   uint32_t vword[4];                       // per n-tile: bit 4n = row n valid
@@ -56,6 +57,7 @@ struct Smem {
   float2 ml[kHeads];                       // final (m, l) of this CTA
   float cw[kMaxCluster][kHeads];           // cluster merge weights
   float cM[kHeads], cL[kHeads];
+  alignas(8) uint64_t merge_bar;           // counts the bytes the cluster pushes here
 };
 
 struct Params {
@@ -99,9 +101,17 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
   // has completed and flushed.
   pdl_wait_primary();
   pdl_launch_dependents();  // the combine (or the next call) may become resident now
-  // Cluster peers must be running before anyone writes into their shared
-  // memory: arrive now, wait right before the first remote store.
-  if (p.C > 1) cluster_arrive_relaxed();
+  // Cluster peers must be running, with their merge barrier initialised,
+  // before anyone writes into their shared memory: initialise, publish to the
+  // cluster, arrive now, wait right before the first remote store.
+  if (p.C > 1) {
+    if (tid == 0) {
+      mbar_init(&sm.merge_bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    cluster_arrive_relaxed();
+  }
 
   const int64_t start = (int64_t)split * p.split_topk;
   const int64_t end = min(start + p.split_topk, p.topk);
@@ -345,36 +355,57 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
   // each owner reduces its slice from its own shared memory.
   const uint32_t rank = cluster_ctarank();
   const int D = kD / C;
-  cluster_wait();  // all peers have started (arrived at kernel entry)
+  cluster_wait();  // all peers have started and initialised their merge barrier
+  // Bytes this CTA receives: from each of the C CTAs, its 16 x D slice of acc
+  // and its 16 (m, l) pairs.
+  if (tid == 0) mbar_arrive_expect_tx(&sm.merge_bar, (uint32_t)(C * kHeads * (D * 4 + 8)));
   if ((tid & 15) == 0) {
     const float2 ml = make_float2(m_run, l_run);
-    for (int r = 0; r < C; ++r) *dsmem_ptr(&sm.cml[rank][red_h], (uint32_t)r) = ml;
+    for (int r = 0; r < C; ++r)
+      st_async_f32x2(dsmem_addr(&sm.cml[rank][red_h], (uint32_t)r), ml, dsmem_addr(&sm.merge_bar, (uint32_t)r));
   }
   {
+    // Stage acc locally as [owner][head][dd] so each owner's slice is one
+    // contiguous 16 x D block, then ship each block with one bulk copy.
     const int owner = dim0 / D;  // 16 | D, so a lane's 16 dims have one owner
     const int dd = dim0 - owner * D;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int hl = g + 8 * half;
-      float4 *dst = reinterpret_cast<float4 *>(dsmem_ptr(&sm.rcv[((int)rank * kHeads + hl) * D + dd], (uint32_t)owner));
+      float4 *dst = reinterpret_cast<float4 *>(&sm.stage[(owner * kHeads + hl) * D + dd]);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
         dst[s] = make_float4(acc[2 * s][2 * half], acc[2 * s][2 * half + 1], acc[2 * s + 1][2 * half],
                              acc[2 * s + 1][2 * half + 1]);
     }
   }
-  cluster_sync();  // all pushes landed; from here on only local shared memory is read
-  if (tid < kHeads) {
-    float M = kNegLarge;
-    for (int r = 0; r < C; ++r) M = fmaxf(M, sm.cml[r][tid].x);
-    float L = 0.0f;
-    for (int r = 0; r < C; ++r) {
-      const float w = ex2_approx(sm.cml[r][tid].x - M);
-      sm.cw[r][tid] = w;
-      L += w * sm.cml[r][tid].y;
+  fence_proxy_async_smem();  // make the staged block visible to the bulk-copy engine
+  __syncthreads();
+  if (tid < C) {
+    const uint32_t bytes = (uint32_t)(kHeads * D * 4);
+    bulk_s2cluster(dsmem_addr(&sm.rcv[(int)rank * kHeads * D], (uint32_t)tid), &sm.stage[tid * kHeads * D], bytes,
+                   dsmem_addr(&sm.merge_bar, (uint32_t)tid));
+    bulk_commit();
+  }
+  // Every byte this CTA owns (C slices and C (m, l) sets) has landed once the
+  // barrier's phase completes; only after that may it read them or exit.  No
+  // cluster-wide barrier follows, and only local shared memory is read.
+  mbar_wait_bounded(&sm.merge_bar, 0u, kLongWaitCycles);
+  {  // merge weights: 16 lanes per head, lane r holds peer r's (m, l)
+    const int h = tid >> 4, r = tid & 15;
+    const float2 ml = r < C ? sm.cml[r][h] : make_float2(kNegLarge, 0.0f);
+    float M = ml.x;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float w = r < C ? ex2_approx(ml.x - M) : 0.0f;
+    float L = w * ml.y;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (r < C) sm.cw[r][h] = w;
+    if (r == 0) {
+      sm.cM[h] = M;
+      sm.cL[h] = L;
     }
-    sm.cM[tid] = M;
-    sm.cL[tid] = L;
   }
   __syncthreads();
   const int pair_shift = 8 - p.logC;       // log2(D / 2)
@@ -412,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p)
     if (rank == 0 && tid < kHeads && hg * kHeads + tid < p.H)
       p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (sm.cM[tid] + lg2_approx(sm.cL[tid])) * kLn2;
   }
+  if (tid < C) bulk_wait_read_all();  // the stage is read by the copy engine until here
 }
 
 // Combine: one CTA per (token, head group, 16-dim chunk), 256 threads.
