@@ -8,12 +8,13 @@
 //   sorted_ids[off_e + rank_j] = j  (rest = R),  expert_ids[off_e/8 + b] = e (rest = -1),
 //   postpad  = sum pad_e.
 //
-// B200 design: warp 0 computes everything with warp primitives instead of the
-// reference's R x R pairwise compare.  Routes j and j + 32 live in lane j.
+// B200 design: one warp computes everything with warp primitives instead of
+// the reference's R x R pairwise compare.  Routes j and j + 32 live in lane j.
 // Ranks come from __match_any_sync (peer mask) and a popcount of the lower
 // lanes; the 288 expert counts live in shared memory; the padded offsets are
 // a warp prefix scan with 9 experts per lane (32 x 9 = 288).  The result is
-// assembled in shared memory and written with coalesced stores by the whole CTA.
+// assembled in shared memory and written with 16-byte stores (4-byte stores
+// when an output is not 16-byte aligned).
 #include "titan_common.cuh"
 
 namespace titan {
@@ -27,79 +28,83 @@ template <typename IdT>
 __global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restrict__ ids, int R,
                                                               int32_t *__restrict__ sorted_ids,
                                                               int32_t *__restrict__ expert_ids,
-                                                              int32_t *__restrict__ postpad) {
-  __shared__ int s_count[kMoeExperts];
-  __shared__ int s_offset[kMoeExperts];
-  __shared__ int s_sorted[kMoeMaxRoutes * 8];
-  __shared__ int s_experts[kMoeMaxRoutes];
-  __shared__ int s_total;
+                                                              int32_t *__restrict__ postpad, bool vec_out) {
+  // The whole layout is built by warp 0: no CTA-wide barrier sits on the
+  // critical path, which starts with the route-id loads.  Extra warps (the
+  // caller's num_warps) have nothing to do.
+  if (threadIdx.x >= 32) return;
+  __shared__ __align__(16) int s_count[kMoeExperts];
+  __shared__ __align__(16) int s_offset[kMoeExperts];
+  __shared__ __align__(16) int s_sorted[kMoeMaxRoutes * 8];
+  __shared__ __align__(16) int s_experts[kMoeMaxRoutes];
+  const int lane = threadIdx.x;
+  const unsigned lt = (1u << lane) - 1u;
 
-  const int tid = threadIdx.x;
-  const int nthr = blockDim.x;
-  for (int i = tid; i < R * 8; i += nthr) s_sorted[i] = R;
-  for (int i = tid; i < R; i += nthr) s_experts[i] = -1;
-  for (int i = tid; i < kMoeExperts; i += nthr) s_count[i] = 0;
-  __syncthreads();
+  // Route lane (half 0) and lane + 32 (half 1).  Validity is decided on the
+  // full-width id, before narrowing (an int64 id of 2^32 + 5 is invalid).
+  long long raw0 = -1, raw1 = -1;
+  if (lane < R) raw0 = (long long)ids[lane];
+  if (lane + 32 < R) raw1 = (long long)ids[lane + 32];
 
-  if (tid < 32) {
-    const int lane = tid;
-    const unsigned lt = (1u << lane) - 1u;
-    // Route lane (half 0) and lane + 32 (half 1).  Validity is decided on the
-    // full-width id, before narrowing (an int64 id of 2^32 + 5 is invalid).
-    int e0 = -1, e1 = -1;
-    if (lane < R) {
-      const long long raw = (long long)ids[lane];
-      if (raw >= 0 && raw < kMoeExperts) e0 = (int)raw;
-    }
-    if (lane + 32 < R) {
-      const long long raw = (long long)ids[lane + 32];
-      if (raw >= 0 && raw < kMoeExperts) e1 = (int)raw;
-    }
-    // Invalid routes get a key no valid expert uses; they never scatter.
-    const unsigned m0 = __match_any_sync(0xffffffffu, e0 >= 0 ? e0 : 0x7fffffff);
-    const int rank0 = __popc(m0 & lt);
-    if (e0 >= 0 && rank0 == 0) s_count[e0] = __popc(m0);
-    __syncwarp();
-    const int base1 = e1 >= 0 ? s_count[e1] : 0;  // routes of half 0 precede half 1
-    const unsigned m1 = __match_any_sync(0xffffffffu, e1 >= 0 ? e1 : 0x7fffffff);
-    const int rank1 = base1 + __popc(m1 & lt);
-    __syncwarp();
-    if (e1 >= 0 && __popc(m1 & lt) == 0) s_count[e1] = base1 + __popc(m1);
-    __syncwarp();
+  // Initialise while the loads are in flight: padding = R, unused blocks = -1.
+  const int4 pad4 = make_int4(R, R, R, R);
+  for (int i = lane; i < 2 * R; i += 32) reinterpret_cast<int4 *>(s_sorted)[i] = pad4;  // 8R ints
+  for (int i = lane; i < R; i += 32) s_experts[i] = -1;
+  for (int i = lane; i < kMoeExperts; i += 32) s_count[i] = 0;
+  __syncwarp();
 
-    // Exclusive prefix of padded counts: lane owns experts [9 lane, 9 lane + 9).
-    int local[kMoePerLane];
-    int sum = 0;
+  const int e0 = (raw0 >= 0 && raw0 < kMoeExperts) ? (int)raw0 : -1;
+  const int e1 = (raw1 >= 0 && raw1 < kMoeExperts) ? (int)raw1 : -1;
+  // Invalid routes get a key no valid expert uses; they never scatter.
+  const unsigned m0 = __match_any_sync(0xffffffffu, e0 >= 0 ? e0 : 0x7fffffff);
+  const int rank0 = __popc(m0 & lt);
+  if (e0 >= 0 && rank0 == 0) s_count[e0] = __popc(m0);
+  __syncwarp();
+  const int base1 = e1 >= 0 ? s_count[e1] : 0;  // routes of half 0 precede half 1
+  const unsigned m1 = __match_any_sync(0xffffffffu, e1 >= 0 ? e1 : 0x7fffffff);
+  const int rank1 = base1 + __popc(m1 & lt);
+  __syncwarp();
+  if (e1 >= 0 && __popc(m1 & lt) == 0) s_count[e1] = base1 + __popc(m1);
+  __syncwarp();
+
+  // Exclusive prefix of padded counts: lane owns experts [9 lane, 9 lane + 9).
+  int local[kMoePerLane], cnt[kMoePerLane];
+  int sum = 0;
 #pragma unroll
-    for (int k = 0; k < kMoePerLane; ++k) {
-      const int c = s_count[kMoePerLane * lane + k];
-      local[k] = sum;
-      sum += (c + 7) & ~7;
-    }
-    int incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    const int excl = incl - sum;
-#pragma unroll
-    for (int k = 0; k < kMoePerLane; ++k) {
-      const int e = kMoePerLane * lane + k;
-      const int off = excl + local[k];
-      s_offset[e] = off;
-      const int blocks = ((s_count[e] + 7) & ~7) >> 3;
-      for (int b = 0; b < blocks; ++b) s_experts[(off >> 3) + b] = e;
-    }
-    __syncwarp();
-    if (e0 >= 0) s_sorted[s_offset[e0] + rank0] = lane;
-    if (e1 >= 0) s_sorted[s_offset[e1] + rank1] = lane + 32;
-    if (lane == 31) s_total = incl;
+  for (int k = 0; k < kMoePerLane; ++k) {
+    cnt[k] = s_count[kMoePerLane * lane + k];
+    local[k] = sum;
+    sum += (cnt[k] + 7) & ~7;
   }
-  __syncthreads();
-  for (int i = tid; i < R * 8; i += nthr) sorted_ids[i] = s_sorted[i];
-  for (int i = tid; i < R; i += nthr) expert_ids[i] = s_experts[i];
-  if (tid == 0) postpad[0] = s_total;
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const int excl = incl - sum;
+#pragma unroll
+  for (int k = 0; k < kMoePerLane; ++k) {
+    const int e = kMoePerLane * lane + k;
+    const int off = excl + local[k];
+    s_offset[e] = off;
+    const int blocks = ((cnt[k] + 7) & ~7) >> 3;
+    for (int b = 0; b < blocks; ++b) s_experts[(off >> 3) + b] = e;
+  }
+  __syncwarp();
+  if (e0 >= 0) s_sorted[s_offset[e0] + rank0] = lane;
+  if (e1 >= 0) s_sorted[s_offset[e1] + rank1] = lane + 32;
+  __syncwarp();
+  if (vec_out) {
+    for (int i = lane; i < 2 * R; i += 32)
+      reinterpret_cast<int4 *>(sorted_ids)[i] = reinterpret_cast<const int4 *>(s_sorted)[i];
+    for (int i = lane; i < R / 4; i += 32)
+      reinterpret_cast<int4 *>(expert_ids)[i] = reinterpret_cast<const int4 *>(s_experts)[i];
+  } else {
+    for (int i = lane; i < 8 * R; i += 32) sorted_ids[i] = s_sorted[i];
+    for (int i = lane; i < R; i += 32) expert_ids[i] = s_experts[i];
+  }
+  if (lane == 31) postpad[0] = incl;
 }
 
 }  // namespace titan
@@ -117,11 +122,12 @@ extern "C" int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int
     return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_align_small: null pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int R = (int)num_routes;
+  const bool vec_out = (uintptr_t)sorted_ids % 16 == 0 && (uintptr_t)expert_ids % 16 == 0;
   if (ids_is_int64)
     moe_align_small_kernel<long long><<<1, 32 * num_warps, 0, s>>>(static_cast<const long long *>(topk_ids), R,
-                                                                  sorted_ids, expert_ids, postpad);
+                                                                  sorted_ids, expert_ids, postpad, vec_out);
   else
     moe_align_small_kernel<int32_t><<<1, 32 * num_warps, 0, s>>>(static_cast<const int32_t *>(topk_ids), R,
-                                                                 sorted_ids, expert_ids, postpad);
+                                                                 sorted_ids, expert_ids, postpad, vec_out);
   return check_launch("moe_align_small launch");
 }
