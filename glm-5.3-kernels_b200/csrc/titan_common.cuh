@@ -86,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 }
 
 // One bulk copy global -> this CTA's shared memory, completing on `bar`.
-// dst, src 16-byte aligned; bytes a multiple of 16.  No multicast.
+// dst, src 16-byte aligned; bytes a multiple of 16.  Single destination CTA.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
