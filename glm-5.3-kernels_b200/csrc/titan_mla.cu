@@ -85,7 +85,7 @@ __device__ __forceinline__ int pick4(const int (&v)[4], int i) {
 }
 
 template <bool kPartialOut>
-__global__ void __launch_bounds__(kThreads, 1) sparse_mla_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
 
@@ -584,10 +584,15 @@ static int prepare_device(size_t smem, const int **capacity) {
       if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: kernel attributes: %s", cudaGetErrorString(e));
     }
-    int sms = 0;
+    int sms = 0, per_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sparse_mla_kernel<false>, kThreads, smem) != cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
     for (int cs = 0; cs <= kMaxCluster; ++cs) g_cluster_capacity[dev][cs] = 0;
-    g_cluster_capacity[dev][1] = sms;
+    g_cluster_capacity[dev][1] = sms * per_sm;  // co-resident CTAs without clusters
     for (int cs = 2; cs <= kMaxCluster; cs <<= 1) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3((unsigned)cs, 1, 1);

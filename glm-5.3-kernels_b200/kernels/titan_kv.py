@@ -43,7 +43,7 @@ def store_int8(x, cache, slots):
         slots = slots.to(torch.int64)
     cache8 = cache.view(torch.int8)
     lib = _native.load()
-    with torch.cuda.device(x.device):
+    with _native.on_device(x.device):
         rc = lib.titan_store_int8(
             x.data_ptr(), x.stride(0), cache8.data_ptr(), cache8.shape[0], cache8.shape[1],
             cache8.stride(0), cache8.stride(1), slots.data_ptr(), 1 if slots.dtype == torch.int64 else 0,

@@ -41,6 +41,7 @@ _MIN_TOPK_PER_SPLIT = 128
 _SPLIT_MAX_OCCUPANCY = 4
 
 
+@functools.lru_cache(maxsize=64)
 def num_compute_units(device_index):
     return torch.cuda.get_device_properties(device_index).multi_processor_count
 
@@ -72,14 +73,16 @@ def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int
     return max(1, num_kv_splits)
 
 
-# Cost model of the B200 kernel, fitted to back-to-back B=1 / B=8 sweeps on
-# B200 (microseconds): one 32-row tile per CTA, the cluster merge, and the
-# combine launch (with a small per-partial term) when a token has >1 cluster.
+# Cost model of the B200 kernel, fitted to back-to-back B=1 / B=4 / B=8
+# sweeps on B200 (microseconds): one 32-row tile per CTA, the cluster merge,
+# and the combine launch (plus a per-partial term) when a token has more than
+# one cluster.  Decode grids are kept to one CTA per SM: two co-resident CTAs
+# slow each other's tiles more than the extra parallelism returns.
 _TILE_ROWS = 32
 _COST_TILE_US = 1.25
-_COST_CLUSTER_MERGE_US = 0.6
+_COST_CLUSTER_MERGE_US = 1.2
 _COST_COMBINE_US = 1.4
-_COST_COMBINE_PER_PARTIAL_US = 0.025
+_COST_COMBINE_PER_PARTIAL_US = 0.05
 _MAX_CLUSTER = 16
 _max_clusters_cache = {}
 
@@ -95,14 +98,21 @@ def _max_active_clusters(device_index):
 
 
 def _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count, max_clusters):
+    return _choose_kv_splits_b200_cached(num_tokens, num_head_groups, index_topk, sm_count,
+                                         tuple(sorted(max_clusters.items())))
+
+
+@functools.lru_cache(maxsize=1024)
+def _choose_kv_splits_b200_cached(num_tokens, num_head_groups, index_topk, sm_count, max_clusters_items):
     """Auto split count for the B200 kernel.
 
-    Candidates are split counts S whose whole grid (tokens x groups x S CTAs,
-    one per SM) and whose clusters (C = largest power of two <= 16 dividing S
+    Candidates are split counts S whose whole grid (tokens x groups x S CTAs)
+    fits one CTA per SM and whose clusters (C = largest power of two <= 16 dividing S
     that the device can co-schedule in one wave) fit at once; the cheapest
-    under the cost model above wins (ties: more splits).  The reference's
+    under the cost model above wins (ties: fewer splits).  The reference's
     `_choose_num_kv_splits` targets its own SM80 kernel and stays available.
     """
+    max_clusters = dict(max_clusters_items)
     units = num_tokens * num_head_groups
     if units == 0 or units >= sm_count:
         return 1
@@ -199,7 +209,7 @@ def triton_mla_sparse_attention(
     # Split partials live in a caching-allocator buffer, like the reference's
     # `mid_out` (kernels/titan_mla.py:533-537): graph-capture safe, no sync.
     workspace = torch.empty(max(ws_bytes, 0), dtype=torch.uint8, device=q.device) if ws_bytes > 0 else None
-    with torch.cuda.device(q.device):
+    with _native.on_device(q.device):
         rc = lib.titan_mla_sparse_attention(
             q.data_ptr(), q.stride(0), q.stride(1),
             kv.data_ptr(), kv_row_stride, seq_kv,

@@ -50,7 +50,7 @@ def titan_moe_align_small(
     if num_warps not in (1, 2, 4):
         raise ValueError('Candidate warp counts are 1, 2, or 4')
     lib = _native.load()
-    with torch.cuda.device(topk_ids.device):
+    with _native.on_device(topk_ids.device):
         rc = lib.titan_moe_align_small(
             topk_ids.data_ptr(), 1 if topk_ids.dtype == torch.int64 else 0, routes,
             sorted_ids.data_ptr(), expert_ids.data_ptr(), postpad.data_ptr(), num_warps,

@@ -82,7 +82,29 @@ def check(status, what):
 def stream_of(tensor):
     """Raw handle of torch's current stream on the tensor's device."""
     import torch
-    return torch.cuda.current_stream(tensor.device).cuda_stream
+    return torch._C._cuda_getCurrentRawStream(tensor.device.index)
+
+
+class on_device:
+    """Make `device` current for the launch (no-op when it already is)."""
+
+    __slots__ = ("index", "prev")
+
+    def __init__(self, device):
+        self.index = device.index
+
+    def __enter__(self):
+        import torch
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.index:
+            torch.cuda.set_device(self.index)
+        return self
+
+    def __exit__(self, *exc):
+        import torch
+        if self.prev != self.index:
+            torch.cuda.set_device(self.prev)
+        return False
 
 
 def device_error(tensor, clear=True):
