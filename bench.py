@@ -308,15 +308,14 @@ class DecodeBench:
 
 
 def splits_and_launches(batch, sms, device_index):
-    """Split count the B200 policy picks and kernel launches per call."""
-    from kernels.titan_mla import _choose_kv_splits_b200, _max_active_clusters
-    table = _max_active_clusters(device_index)
-    S = _choose_kv_splits_b200(batch, 1, TOPK, sms, table)
-    max_c = max([c for c, n in table.items() if n > 0] or [1])
-    C = 1
-    while C * 2 <= min(16, max_c) and S % (C * 2) == 0:
-        C *= 2
-    return S, C, (1 if S // C == 1 else 2)
+    """Split count the B200 policy picks, its cluster size and kernel launches
+    per call (the combine kernel runs only when the split kernel cannot merge
+    the cluster partials itself)."""
+    from kernels.titan_mla import _choose_kv_splits_b200, _cluster_tables, _launch_layout
+    tables = _cluster_tables(device_index)
+    S = _choose_kv_splits_b200(batch, 1, TOPK, sms, tables)
+    C, nc = _launch_layout(batch, S, tables)
+    return S, C, (1 if nc == 1 or (C >= 2 and nc <= C) else 2)
 
 
 def run_ours(args, dist):
@@ -523,7 +522,7 @@ def run_ours(args, dist):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "algorithmic_bytes_per_call": bytes_per_call,
-                         "kernel": "sparse_mla_kernel + combine (whole call, back to back)"},
+                         "kernel": ("sparse_mla_kernel<true> (split + cluster merge + last-arriver merge), whole call, back to back" if launches_per_call == 1 else "sparse_mla_kernel + combine (whole call, back to back)")},
             "e2e": {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": q_sets[0].numel() * 2 + idx_sets[0].numel() * 4,
                     "d2h_bytes_per_step": HEADS * 512 * 2},
             "gpu_launches": K * launches_per_call,

@@ -250,6 +250,18 @@ __device__ __forceinline__ T *dsmem_ptr(T *p, uint32_t rank) {
   return reinterpret_cast<T *>(r);
 }
 
+// Arrival ticket with release (prior writes of this thread and of those
+// ordered before it by a CTA barrier) and acquire semantics at GPU scope.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int *p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void st_relaxed_gpu(int *p, int v) {
+  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ float ld_global_nc_f32(const void *p) {
   float v;
   asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));

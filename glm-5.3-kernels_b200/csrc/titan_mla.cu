@@ -27,8 +27,10 @@
 //  * Split merge: the C <= 16 splits of a (token, head group) that form one
 //    thread-block cluster merge through distributed shared memory, each CTA
 //    reducing 512 / C dims; a single cluster writes the bf16 output directly.
-//    With more clusters than one, each cluster writes one partial (o, lse) and
-//    a combine kernel, launched as a programmatic dependent, merges them.
+//    With more clusters than one, each cluster writes one partial (o, lse);
+//    given arrival counters, the last CTA of each rank to finish merges that
+//    rank's slice over all partials (no second kernel), otherwise a combine
+//    kernel, launched as a programmatic dependent, merges them.
 #include "titan_common.cuh"
 
 namespace titan {
@@ -58,6 +60,7 @@ struct Smem {
   float cw[kMaxCluster][kHeads];           // cluster merge weights
   float cM[kHeads], cL[kHeads];
   alignas(8) uint64_t merge_bar;           // counts the bytes the cluster pushes here
+  int last;                                // this CTA arrived last at its cross-cluster counter
 };
 
 struct Params {
@@ -78,10 +81,62 @@ struct Params {
   int NC;           // clusters per (token, head group) = S / C = partials to combine
   int64_t split_topk;
   float scale_log2;  // sm_scale * log2(e)
+  int *sem;          // [T][groups][16] arrival counters (zero between calls) or null: combine kernel
 };
 
 __device__ __forceinline__ int pick4(const int (&v)[4], int i) {
   return i == 0 ? v[0] : i == 1 ? v[1] : i == 2 ? v[2] : v[3];
+}
+
+// Last-arriver merge of the NC <= C cluster partials of (token t, head group
+// hg) over the dims of cluster rank `rank` (D = 512 / C = 32 kPer dims), same
+// arithmetic as the combine kernel below.  16 lanes per head: lane j holds
+// partial j's LSE and owns pairs j + 16 k, k < kPer; every load is issued
+// before the first use.
+template <int kPer>
+__device__ __forceinline__ void merge_cluster_partials(const Params &p, int t, int hg, uint32_t rank, int tid) {
+  constexpr int kSlots = kMaxCluster / kPer;  // = C, upper bound of NC
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int h = tid >> 4, j = tid & 15;
+  const int hh = hg * kHeads + h;
+  const bool live = hh < p.H;
+  const int64_t split_stride = (int64_t)p.Hp * kD;
+  const int dim = (int)rank * (32 * kPer) + 2 * j;
+  const float *o_src = p.part_o + ((int64_t)t * p.NC * p.Hp + hh) * kD + dim;
+  const float lse = (live && j < p.NC) ? __ldcg(p.part_lse + ((int64_t)t * p.NC + j) * p.Hp + hh) : -INFINITY;
+  float2 ov[kSlots][kPer];
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s)
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      ov[s][k] = (live && s < p.NC) ? __ldcg(reinterpret_cast<const float2 *>(o_src + s * split_stride + 32 * k))
+                                    : make_float2(0.f, 0.f);
+  float m = fmaxf(kNegLarge, lse);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float w = ex2_approx((lse - m) * kLog2e);
+  float L = w;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  const float inv = L > 0.0f ? 1.0f / L : 1.0f;
+  float2 sum[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) sum[k] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) {
+    const float ws = __shfl_sync(0xffffffffu, w, s, 16);  // partial s's weight, from lane s of this head
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      sum[k].x += ws * ov[s][k].x;
+      sum[k].y += ws * ov[s][k].y;
+    }
+  }
+  if (live) {
+    __nv_bfloat16 *dst = p.out + (int64_t)t * p.out_st + (int64_t)hh * p.out_sh + dim;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      *reinterpret_cast<uint32_t *>(dst + 32 * k) = pack_bf16x2(sum[k].x * inv, sum[k].y * inv);
+  }
 }
 
 template <bool kPartialOut>
@@ -440,8 +495,34 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     }
   }
   if constexpr (kPartialOut) {
-    if (rank == 0 && tid < kHeads && hg * kHeads + tid < p.H)
+    // Every rank writes the (identical) LSE of its cluster, so the rank-r
+    // counter below orders everything the rank-r merge reads.
+    if (tid < kHeads && hg * kHeads + tid < p.H)
       p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (sm.cM[tid] + lg2_approx(sm.cL[tid])) * kLn2;
+    if (p.sem != nullptr) {
+      // Cross-cluster merge in this kernel: the CTAs of rank r in the NC
+      // clusters of (t, hg) take a ticket after publishing their slice; the
+      // last one merges dims [r D, r D + D) over all NC partials and resets
+      // the counter for the next call.  The launcher guarantees NC <= C.
+      __syncthreads();
+      if (tid == 0) {
+        // acq_rel ticket after the CTA barrier: releases this CTA's slice and
+        // LSE, and the last arriver acquires every other CTA's.
+        int *ctr = p.sem + ((int64_t)t * gridDim.y + hg) * kMaxCluster + rank;
+        const int last = atom_add_acq_rel_gpu(ctr, 1) == p.NC - 1;
+        if (last) st_relaxed_gpu(ctr, 0);
+        sm.last = last;
+      }
+      __syncthreads();
+      if (sm.last) {
+        switch (p.logC) {
+          case 1: merge_cluster_partials<8>(p, t, hg, rank, tid); break;
+          case 2: merge_cluster_partials<4>(p, t, hg, rank, tid); break;
+          case 3: merge_cluster_partials<2>(p, t, hg, rank, tid); break;
+          default: merge_cluster_partials<1>(p, t, hg, rank, tid); break;
+        }
+      }
+    }
   }
   if (tid < C) bulk_wait_read_all();  // the stage is read by the copy engine until here
 }
@@ -634,15 +715,40 @@ static int choose_cluster(int64_t units, int64_t S, const int *capacity) {
 }  // namespace mla
 }  // namespace titan
 
-extern "C" int titan_mla_max_active_clusters(int cluster_size) {
-  using namespace titan::mla;
+namespace titan {
+namespace mla {
+
+// Co-resident clusters of `cluster_size` MLA CTAs; with `exclusive`, counted
+// as if each CTA had an SM to itself (the query is made with enough dynamic
+// shared memory that a second CTA cannot fit on the SM).
+static int max_active_clusters(int cluster_size, bool exclusive) {
   if (cluster_size < 1 || cluster_size > kMaxCluster) return -1;
   const int *capacity = nullptr;
   if (prepare_device(sizeof(Smem), &capacity) != TITAN_OK) return -1;
+  size_t smem = sizeof(Smem);
+  if (exclusive) {
+    int dev = 0, per_sm = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+    smem = (size_t)per_sm / 2 + 1024;
+    if (smem < sizeof(Smem)) smem = sizeof(Smem);
+    if (smem > (size_t)optin) return -1;
+    // Raise the opt-in ceiling so the query is legal; launches still request
+    // sizeof(Smem).
+    if (cudaFuncSetAttribute(sparse_mla_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)cluster_size, 1, 1);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)cluster_size;
@@ -651,11 +757,25 @@ extern "C" int titan_mla_max_active_clusters(int cluster_size) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg) != cudaSuccess) {
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg);
+  if (exclusive)  // back to the launch setting
+    cudaFuncSetAttribute(sparse_mla_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+  if (e != cudaSuccess) {
     cudaGetLastError();
     return -1;
   }
   return n;
+}
+
+}  // namespace mla
+}  // namespace titan
+
+extern "C" int titan_mla_max_active_clusters(int cluster_size) {
+  return titan::mla::max_active_clusters(cluster_size, false);
+}
+
+extern "C" int titan_mla_max_exclusive_clusters(int cluster_size) {
+  return titan::mla::max_active_clusters(cluster_size, true);
 }
 
 extern "C" int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_heads, int64_t num_kv_splits) {
@@ -667,15 +787,23 @@ extern "C" int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_hea
   return o_bytes + ((lse_bytes + 255) / 256) * 256;
 }
 
-extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token, int64_t q_stride_head,
-                                          const void *kv, int64_t kv_row_stride, int64_t seq_kv,
-                                          const int32_t *indices, int64_t indices_stride_token, int64_t topk,
-                                          void *out, int64_t out_stride_token, int64_t out_stride_head,
-                                          int64_t num_tokens, int64_t num_heads, float sm_scale,
-                                          int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
-                                          titan_stream_t stream) {
-  using namespace titan;
+extern "C" int64_t titan_mla_semaphore_count(int64_t num_tokens, int64_t num_heads) {
   using namespace titan::mla;
+  if (num_tokens <= 0 || num_heads <= 0) return 0;
+  return num_tokens * ((num_heads + kHeads - 1) / kHeads) * kMaxCluster;
+}
+
+namespace titan {
+namespace mla {
+
+// Shared launcher of titan_mla_sparse_attention (sem == nullptr: partials of
+// several clusters are merged by the combine kernel) and
+// titan_mla_sparse_attention_sem (the split kernel merges them itself).
+static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_head, const void *kv,
+                      int64_t kv_row_stride, int64_t seq_kv, const int32_t *indices, int64_t indices_stride_token,
+                      int64_t topk, void *out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_tokens,
+                      int64_t num_heads, float sm_scale, int64_t num_kv_splits, void *workspace,
+                      int64_t workspace_bytes, int32_t *sem, int64_t sem_count, titan_stream_t stream) {
   if (num_tokens < 0 || num_heads <= 0 || topk < 0 || seq_kv < 0)
     return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: invalid sizes");
   if (num_tokens == 0) return TITAN_OK;
@@ -708,6 +836,12 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   // NC clusters (partials) of C splits per (token, head group).
   const int C = choose_cluster(num_tokens * groups, num_kv_splits, capacity);
   const int64_t NC = num_kv_splits / C;
+  // The split kernel merges only when every lane of the last CTA loads at
+  // most 16 partial values (NC <= C); larger merges go to the combine kernel.
+  const bool in_kernel_merge = sem != nullptr && C >= 2 && NC > 1 && NC <= C;
+  if (sem != nullptr && sem_count < titan_mla_semaphore_count(num_tokens, num_heads))
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: %lld semaphores given, %lld needed", (long long)sem_count,
+                (long long)titan_mla_semaphore_count(num_tokens, num_heads));
 
   Params prm;
   prm.q = static_cast<const __nv_bfloat16 *>(q);
@@ -734,6 +868,7 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
   prm.part_o = nullptr;
   prm.part_lse = nullptr;
+  prm.sem = in_kernel_merge ? sem : nullptr;
   if (NC > 1) {
     const int64_t o_bytes = num_tokens * NC * prm.Hp * kD * 4;
     prm.part_o = static_cast<float *>(workspace);
@@ -758,11 +893,41 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
   cudaError_t e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true>, prm)
                          : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false>, prm);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla launch (C=%d): %s", C, cudaGetErrorString(e));
-  if (NC == 1) return TITAN_OK;
+  if (NC == 1 || in_kernel_merge) return TITAN_OK;
   // Combine the NC cluster partials: 32 CTAs per (token, head group).
   e = launch_combine(prm, (int)groups, s);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla combine launch: %s", cudaGetErrorString(e));
   return TITAN_OK;
+}
+
+}  // namespace mla
+}  // namespace titan
+
+extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                                          const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                                          const int32_t *indices, int64_t indices_stride_token, int64_t topk,
+                                          void *out, int64_t out_stride_token, int64_t out_stride_head,
+                                          int64_t num_tokens, int64_t num_heads, float sm_scale,
+                                          int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
+                                          titan_stream_t stream) {
+  return titan::mla::launch_mla(q, q_stride_token, q_stride_head, kv, kv_row_stride, seq_kv, indices,
+                                indices_stride_token, topk, out, out_stride_token, out_stride_head, num_tokens,
+                                num_heads, sm_scale, num_kv_splits, workspace, workspace_bytes, nullptr, 0, stream);
+}
+
+extern "C" int titan_mla_sparse_attention_sem(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                                              const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                                              const int32_t *indices, int64_t indices_stride_token, int64_t topk,
+                                              void *out, int64_t out_stride_token, int64_t out_stride_head,
+                                              int64_t num_tokens, int64_t num_heads, float sm_scale,
+                                              int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
+                                              int32_t *semaphores, int64_t semaphore_count, titan_stream_t stream) {
+  if (semaphores == nullptr || (uintptr_t)semaphores % 4)
+    return titan::fail(TITAN_ERR_INVALID_ARGUMENT, "mla: semaphores must be a non-null int32 array");
+  return titan::mla::launch_mla(q, q_stride_token, q_stride_head, kv, kv_row_stride, seq_kv, indices,
+                                indices_stride_token, topk, out, out_stride_token, out_stride_head, num_tokens,
+                                num_heads, sm_scale, num_kv_splits, workspace, workspace_bytes, semaphores,
+                                semaphore_count, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -4,9 +4,10 @@
 Drop-in for the reference `triton_mla_sparse_attention`
 (kernels/titan_mla.py:452-581) with the same argument order, defaults,
 assertions and split heuristic (`_choose_num_kv_splits`, :432-449).  The
-compute runs in libtitan_b200.so (csrc/titan_mla.cu): a bulk-copy (TMA) row
-gather into shared memory, bf16 tensor-core MMAs with fp32 online softmax, and
-a combine kernel for split-KV launches.
+compute runs in libtitan_b200.so (csrc/titan_mla.cu): rows gathered straight
+into tensor-core fragments, bf16 MMAs with fp32 online softmax, and split
+partials merged inside thread-block clusters and, across clusters, by the
+last CTA to finish (arrival counters).
 
 528 bytes/token: 512 signed INT8 values followed by 1 FP32 scale + 12 zero bytes.
 """
@@ -73,69 +74,136 @@ def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int
     return max(1, num_kv_splits)
 
 
-# Cost model of the B200 kernel, fitted to back-to-back B=1 / B=4 / B=8
-# sweeps on B200 (microseconds): one 32-row tile per CTA, the cluster merge,
-# and the combine launch (plus a per-partial term) when a token has more than
-# one cluster.  Decode grids are kept to one CTA per SM: two co-resident CTAs
-# slow each other's tiles more than the extra parallelism returns.
+# Cost model of the B200 kernel, fitted to back-to-back B=1/2/4/8 sweeps of
+# every split count on B200 (microseconds): 32-row tiles per CTA, the merge
+# inside a thread-block cluster, the merge across clusters (done by the last
+# CTA to finish when NC <= C, else by the combine kernel plus a per-partial
+# term), and a penalty when more clusters are launched than fit with one CTA
+# per SM (they then share SMs and slow each other's gathers).
 _TILE_ROWS = 32
 _COST_TILE_US = 1.25
 _COST_CLUSTER_MERGE_US = 1.2
+_COST_SPLIT_MERGE_US = 1.2
 _COST_COMBINE_US = 1.4
 _COST_COMBINE_PER_PARTIAL_US = 0.05
+_COST_SHARED_SM_US = 2.0
 _MAX_CLUSTER = 16
-_max_clusters_cache = {}
+_CLUSTER_SIZES = (1, 2, 4, 8, 16)
+_cluster_tables_cache = {}
 
 
-def _max_active_clusters(device_index):
-    """{cluster size: co-resident clusters} of the MLA kernel on this device."""
-    if device_index not in _max_clusters_cache:
+def _cluster_tables(device_index):
+    """((C, co-resident clusters, clusters with an SM per CTA), ...) for C in
+    1, 2, 4, 8, 16: the MLA kernel's cluster capacity on this device."""
+    tables = _cluster_tables_cache.get(device_index)
+    if tables is None:
         lib = _native.load()
         with torch.cuda.device(device_index):
-            table = {c: lib.titan_mla_max_active_clusters(c) for c in (1, 2, 4, 8, 16)}
-        _max_clusters_cache[device_index] = table
-    return _max_clusters_cache[device_index]
+            tables = tuple((c, lib.titan_mla_max_active_clusters(c), lib.titan_mla_max_exclusive_clusters(c))
+                           for c in _CLUSTER_SIZES)
+        _cluster_tables_cache[device_index] = tables
+    return tables
 
 
-def _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count, max_clusters):
-    return _choose_kv_splits_b200_cached(num_tokens, num_head_groups, index_topk, sm_count,
-                                         tuple(sorted(max_clusters.items())))
+def _launch_layout(units, S, tables):
+    """(C, NC) as the launcher picks them: C = the largest power of two <= 16
+    dividing S whose units * S / C clusters are all co-resident."""
+    C = 1
+    for c, capacity, _ in tables:
+        if c == 1:
+            continue
+        if S % c:
+            break
+        if units * (S // c) <= max(0, capacity):
+            C = c
+    return C, S // C
 
 
 @functools.lru_cache(maxsize=1024)
-def _choose_kv_splits_b200_cached(num_tokens, num_head_groups, index_topk, sm_count, max_clusters_items):
+def _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count, tables):
     """Auto split count for the B200 kernel.
 
-    Candidates are split counts S whose whole grid (tokens x groups x S CTAs)
-    fits one CTA per SM and whose clusters (C = largest power of two <= 16 dividing S
-    that the device can co-schedule in one wave) fit at once; the cheapest
-    under the cost model above wins (ties: fewer splits).  The reference's
-    `_choose_num_kv_splits` targets its own SM80 kernel and stays available.
+    Candidates keep the whole grid (tokens x groups x S CTAs) within one CTA
+    per SM; the cheapest under the cost model above wins (ties: fewer
+    splits).  The reference's `_choose_num_kv_splits` targets its own SM80
+    kernel and stays available through an explicit num_kv_splits.
     """
-    max_clusters = dict(max_clusters_items)
     units = num_tokens * num_head_groups
     if units == 0 or units >= sm_count:
         return 1
+    exclusive = {c: e for c, _, e in tables}
     best, best_cost = 1, None
     for S in range(1, sm_count // units + 1):
-        C = 1  # same rule as the launcher: largest power of two dividing S whose clusters all fit
-        cs = 2
-        while cs <= _MAX_CLUSTER and S % cs == 0:
-            if units * (S // cs) <= max(0, max_clusters.get(cs, 0)):
-                C = cs
-            cs *= 2
-        nc = S // C
+        C, nc = _launch_layout(units, S, tables)
         rows = -(-index_topk // S)
         cost = max(1, -(-rows // _TILE_ROWS)) * _COST_TILE_US
         cost += _COST_CLUSTER_MERGE_US if C > 1 else 0.0
-        cost += (_COST_COMBINE_US + _COST_COMBINE_PER_PARTIAL_US * nc) if nc > 1 else 0.0
+        if nc > 1:
+            if C >= 2 and nc <= C:
+                cost += _COST_SPLIT_MERGE_US
+            else:
+                cost += _COST_COMBINE_US + _COST_COMBINE_PER_PARTIAL_US * nc
+        if units * nc > max(0, exclusive.get(C, 0)):
+            cost += _COST_SHARED_SM_US
         if best_cost is None or cost < best_cost - 1e-9:
             best, best_cost = S, cost
     return best
 
 
-def _aligned16(t):
-    return t.data_ptr() % 16 == 0 and all((s * t.element_size()) % 16 == 0 for s in t.stride()[:-1])
+# Per-(device, stream) scratch of split launches: int32 arrival counters (zero
+# between calls: every call leaves them at zero) and the fp32 partials
+# workspace.  Calls on one stream are ordered, so they can share it; other
+# streams get their own.  Buffers are kept for the life of the process, since
+# a CUDA graph captured on a stream keeps using that stream's buffers: such a
+# graph must not be replayed concurrently with other calls issued on the
+# stream it was captured on.  Workspaces above _MAX_CACHED_WORKSPACE are taken
+# from the caching allocator per call, like the reference's `mid_out`
+# (kernels/titan_mla.py:533-537).
+_MAX_CACHED_WORKSPACE = 8 << 20
+_scratch = {}
+_retired = []
+_plans = {}
+
+
+def _split_scratch(q, dev, stream, ws_bytes, sem_count):
+    entry = _scratch.get((dev, stream))
+    if entry is not None and entry[0].numel() >= sem_count and entry[1].numel() >= ws_bytes:
+        return entry
+    if ws_bytes > _MAX_CACHED_WORKSPACE or torch.cuda.is_current_stream_capturing():
+        # Not cached: a graph being captured zeroes its own counters on
+        # every replay and keeps both buffers in its private pool.
+        sem = torch.zeros(sem_count, dtype=torch.int32, device=q.device)
+        if entry is not None and entry[0].numel() >= sem_count:
+            sem = entry[0]
+        return sem, torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    if entry is not None:
+        _retired.append(entry)
+        sem_count = max(sem_count, entry[0].numel())
+        ws_bytes = max(ws_bytes, entry[1].numel())
+    entry = (torch.zeros(max(sem_count, 4096), dtype=torch.int32, device=q.device),
+             torch.empty(max(ws_bytes, 1 << 20), dtype=torch.uint8, device=q.device))
+    _scratch[(dev, stream)] = entry
+    return entry
+
+
+def _plan(dev, num_tokens, num_heads_q, index_topk, num_kv_splits, sm_count):
+    """(splits, workspace bytes, counter count) of one call shape, cached."""
+    key = (dev, num_tokens, num_heads_q, index_topk, num_kv_splits, sm_count)
+    plan = _plans.get(key)
+    if plan is None:
+        S = num_kv_splits
+        if S is None or S == 0:
+            groups = _cdiv(num_heads_q, min(_BLOCK_H, num_heads_q))
+            S = _choose_kv_splits_b200(num_tokens, groups, index_topk,
+                                       num_compute_units(dev) if sm_count is None else sm_count,
+                                       _cluster_tables(dev))
+        lib = _native.load()
+        ws_bytes = lib.titan_mla_workspace_bytes(num_tokens, num_heads_q, S) if num_tokens > 0 else 0
+        sem_count = lib.titan_mla_semaphore_count(num_tokens, num_heads_q) if ws_bytes > 0 else 0
+        plan = (int(S), ws_bytes, sem_count)
+        if len(_plans) < 4096:
+            _plans[key] = plan
+    return plan
 
 
 def triton_mla_sparse_attention(
@@ -166,57 +234,65 @@ def triton_mla_sparse_attention(
         f"sparse MLA kernel requires dim_qk={_BLOCK_DMODEL} (NoPE) or "
         f"{_DIM_QK} (RoPE), got {dim_qk}"
     )
-    block_dpe = dim_qk - _BLOCK_DMODEL
-    assert kv.shape[1] == 1 and kv.shape[2] == (_ROW_BYTES if kv.dtype == torch.int8 else dim_qk)
+    kv_dtype = kv.dtype
+    kv_shape = kv.shape
+    assert kv_shape[1] == 1 and kv_shape[2] == (_ROW_BYTES if kv_dtype == torch.int8 else dim_qk)
     index_topk = indices.shape[2]
     assert index_topk % _MIN_BLOCK_N == 0, (
         f"topk ({index_topk}) must be a multiple of the smallest autotune "
         f"BLOCK_N ({_MIN_BLOCK_N})"
     )
     # This build carries the INT8 NoPE path (GLM-5.3, qk_rope_head_dim = 0).
-    assert block_dpe == 0 and kv.dtype == torch.int8, (
+    assert dim_qk == _BLOCK_DMODEL and kv_dtype == torch.int8, (
         "the B200 kernel implements the INT8 NoPE path: dim_qk=512 with a [seq_kv, 1, 528] int8 cache")
     assert q.dtype == torch.bfloat16, "q must be bf16"
-    assert q.is_cuda and kv.is_cuda and indices.is_cuda, "sparse MLA runs on CUDA tensors only"
-    assert q.device == kv.device == indices.device, "q, kv and indices must share a device"
+    dev = q.get_device()
+    assert dev >= 0 and kv.get_device() >= 0 and indices.get_device() >= 0, \
+        "sparse MLA runs on CUDA tensors only"
+    assert kv.get_device() == dev and indices.get_device() == dev, "q, kv and indices must share a device"
 
-    kv_group_num = num_heads_q
-    num_head_groups = _cdiv(num_heads_q, min(_BLOCK_H, kv_group_num))
-
-    if num_kv_splits is None or num_kv_splits == 0:
-        if sm_count is None:
-            sm_count = num_compute_units(q.device.index)
-        num_kv_splits = _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count,
-                                               _max_active_clusters(q.device.index))
-
-    out = torch.empty((num_tokens, num_heads_q, _BLOCK_DV), dtype=torch.bfloat16, device=q.device)
+    num_kv_splits, ws_bytes, sem_count = _plan(dev, num_tokens, num_heads_q, index_topk, num_kv_splits,
+                                               sm_count)
+    out = q.new_empty((num_tokens, num_heads_q, _BLOCK_DV))
     if num_tokens == 0:
         return out
 
-    seq_kv = kv.shape[0]
-    if q.stride(-1) != 1 or not _aligned16(q):
+    seq_kv = kv_shape[0]
+    q_st = q.stride()
+    if q_st[2] != 1 or q.data_ptr() % 16 or (q_st[0] * 2) % 16 or (q_st[1] * 2) % 16:
         q = q.contiguous()
-    idx = indices[:, 0, :]
+        q_st = q.stride()
+    idx = indices
     if idx.dtype != torch.int32:
         # Out-of-range wide indices must stay masked after narrowing.
         idx = torch.where((idx >= 0) & (idx < seq_kv), idx, -1).to(torch.int32)
-    if idx.stride(-1) != 1:
+    idx_st = idx.stride()
+    if idx_st[2] != 1:
         idx = idx.contiguous()
-    kv_row_stride = kv.stride(0)  # bytes (int8)
+        idx_st = idx.stride()
+    out_st = out.stride()
 
     lib = _native.load()
-    ws_bytes = lib.titan_mla_workspace_bytes(num_tokens, num_heads_q, num_kv_splits)
-    # Split partials live in a caching-allocator buffer, like the reference's
-    # `mid_out` (kernels/titan_mla.py:533-537): graph-capture safe, no sync.
-    workspace = torch.empty(max(ws_bytes, 0), dtype=torch.uint8, device=q.device) if ws_bytes > 0 else None
-    with _native.on_device(q.device):
-        rc = lib.titan_mla_sparse_attention(
-            q.data_ptr(), q.stride(0), q.stride(1),
-            kv.data_ptr(), kv_row_stride, seq_kv,
-            idx.data_ptr(), idx.stride(0), index_topk,
-            out.data_ptr(), out.stride(0), out.stride(1),
-            num_tokens, num_heads_q, float(sm_scale), int(num_kv_splits),
-            workspace.data_ptr() if workspace is not None else None, ws_bytes,
-            _native.stream_of(q))
-    _native.check(rc, "triton_mla_sparse_attention")
+    stream = torch._C._cuda_getCurrentRawStream(dev)
+    prev = torch.cuda.current_device()
+    if prev != dev:
+        torch.cuda.set_device(dev)
+    try:
+        # indices[:, 0, :] is row t at idx + t * stride(0): no view is needed.
+        args = (q.data_ptr(), q_st[0], q_st[1], kv.data_ptr(), kv.stride(0), seq_kv,
+                idx.data_ptr(), idx_st[0], index_topk, out.data_ptr(), out_st[0], out_st[1],
+                num_tokens, num_heads_q, float(sm_scale), num_kv_splits)
+        if ws_bytes > 0:
+            # Split launch: partials of a token's clusters are merged by the
+            # last CTA to finish (arrival counters), or by a combine kernel.
+            sem, ws = _split_scratch(q, dev, stream, ws_bytes, sem_count)
+            rc = lib.titan_mla_sparse_attention_sem(*args, ws.data_ptr(), ws.numel(), sem.data_ptr(),
+                                                    sem.numel(), stream)
+        else:
+            rc = lib.titan_mla_sparse_attention(*args, None, 0, stream)
+    finally:
+        if prev != dev:
+            torch.cuda.set_device(prev)
+    if rc:
+        _native.check(rc, "triton_mla_sparse_attention")
     return out

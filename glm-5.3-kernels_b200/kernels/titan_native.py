@@ -28,10 +28,17 @@ SIGNATURES = {
     "titan_store_int8": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _int, _i64, _vp]),
     "titan_mla_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "titan_mla_max_active_clusters": (_int, [_int]),
+    "titan_mla_max_exclusive_clusters": (_int, [_int]),
     "titan_mla_sparse_attention": (
         _int,
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
          ctypes.c_float, _i64, _vp, _i64, _vp],
+    ),
+    "titan_mla_semaphore_count": (_i64, [_i64, _i64]),
+    "titan_mla_sparse_attention_sem": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+         ctypes.c_float, _i64, _vp, _i64, _vp, _i64, _vp],
     ),
     "titan_mla_noalloc_scratch_bytes": (_i64, []),
     "titan_mla_sparse_attention_noalloc": (

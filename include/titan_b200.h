@@ -89,6 +89,14 @@ int64_t titan_mla_workspace_bytes(int64_t num_tokens, int64_t num_heads,
 int titan_mla_max_active_clusters(int cluster_size);
 
 /*
+ * Diagnostic: like titan_mla_max_active_clusters, but counting clusters whose
+ * CTAs each have an SM to themselves (-1 on error).  Clusters beyond this
+ * count share SMs with other MLA CTAs; the automatic split policy of the
+ * Python layer avoids that.
+ */
+int titan_mla_max_exclusive_clusters(int cluster_size);
+
+/*
  * Sparse NoPE MLA attention over an INT8 528-byte-row cache.  Replaces
  * `triton_mla_sparse_attention(q, kv, indices, sm_scale, num_kv_splits,
  * sm_count)`, kernels/titan_mla.py:452-581 (kernels :59-429).
@@ -112,6 +120,37 @@ int titan_mla_sparse_attention(const void *q, int64_t q_stride_token, int64_t q_
                                int64_t num_tokens, int64_t num_heads, float sm_scale,
                                int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
                                titan_stream_t stream);
+
+/*
+ * Arrival counters for titan_mla_sparse_attention_sem: the number of int32
+ * entries (num_tokens * ceil(num_heads / 16) * 16).
+ */
+int64_t titan_mla_semaphore_count(int64_t num_tokens, int64_t num_heads);
+
+/*
+ * titan_mla_sparse_attention with the split merge done inside the split
+ * kernel.  Same arguments and results (within the fp32 summation-order
+ * tolerance) as titan_mla_sparse_attention, which this also replaces
+ * (kernels/titan_mla.py:452-581: the split kernel :258-354 and the combine
+ * kernel :357-429 become one launch).  When the splits of a token form several
+ * thread-block clusters, each cluster CTA publishes its partial slice and
+ * takes a ticket from an arrival counter; the last CTA of each cluster rank
+ * merges that rank's slice over all clusters and writes the bf16 output, then
+ * resets its counter to zero.
+ *
+ *   semaphores       int32 [semaphore_count] device array, all zero before the
+ *                    first call; every call leaves it zero again.  Calls that
+ *                    share one array must be ordered on the GPU (same stream,
+ *                    or event-ordered): overlapping calls race on the counters.
+ *   semaphore_count  >= titan_mla_semaphore_count(num_tokens, num_heads)
+ */
+int titan_mla_sparse_attention_sem(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                                   const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                                   const int32_t *indices, int64_t indices_stride_token, int64_t topk,
+                                   void *out, int64_t out_stride_token, int64_t out_stride_head,
+                                   int64_t num_tokens, int64_t num_heads, float sm_scale,
+                                   int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
+                                   int32_t *semaphores, int64_t semaphore_count, titan_stream_t stream);
 
 /*
  * Allocation-free variant of titan_mla_sparse_attention (no counterpart in the

@@ -175,3 +175,52 @@ def test_empty_tokens_and_topk(native_lib, cuda_device):
     out = attn(torch.ones(2, 16, 512, dtype=torch.bfloat16, device=cuda_device), kv,
                torch.zeros(2, 1, 0, dtype=torch.int32, device=cuda_device), 0.1)
     assert out.shape == (2, 16, 512) and not out.any()
+
+
+@pytest.mark.parametrize("tokens,heads", [(1, 16), (2, 20), (3, 32)])
+def test_in_kernel_merge_matches_combine_kernel(big_cache, native_lib, cuda_device, tokens, heads):
+    """titan_mla_sparse_attention_sem (last-arriving CTA merges the cluster
+    partials) against titan_mla_sparse_attention (combine kernel) and the
+    oracle, for split counts that give several clusters per token; the
+    arrival counters are zero again after every call."""
+    import ctypes
+    lib = native_lib
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(11 + tokens)
+    q = torch.randn(tokens, heads, 512, generator=g).to(torch.bfloat16)
+    idx = torch.randint(-8, n + 8, (tokens, 2176), generator=g, dtype=torch.int32)
+    ref = O.mla_sparse_attention(q, rows, idx.view(tokens, 1, 2176), 512 ** -0.5)
+    qd, idxd, kv = q.to(cuda_device), idx.to(cuda_device), cache.view(n, 528)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    need = lib.titan_mla_semaphore_count(tokens, heads)
+    assert need == tokens * -(-heads // 16) * 16
+    sem = torch.zeros(need, dtype=torch.int32, device=cuda_device)
+    for splits in (12, 24, 32, 40, 48, 56, 64, 80, 96, 136):
+        ws = torch.empty(lib.titan_mla_workspace_bytes(tokens, heads, splits), dtype=torch.uint8,
+                         device=cuda_device)
+        args = (qd.data_ptr(), qd.stride(0), qd.stride(1), kv.data_ptr(), kv.stride(0), n,
+                idxd.data_ptr(), idxd.stride(0), 2176)
+        tail = (tokens, heads, ctypes.c_float(512 ** -0.5), splits, ws.data_ptr(), ws.numel())
+        outs = []
+        for use_sem in (False, True, True):
+            out = torch.full((tokens, heads, 512), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+            o = (out.data_ptr(), out.stride(0), out.stride(1))
+            if use_sem:
+                rc = lib.titan_mla_sparse_attention_sem(*args, *o, *tail, sem.data_ptr(), sem.numel(), stream)
+            else:
+                rc = lib.titan_mla_sparse_attention(*args, *o, *tail, stream)
+            assert rc == 0, lib.titan_last_error()
+            outs.append(out)
+            torch.cuda.synchronize()
+            assert not sem.any(), (splits, "arrival counters not reset")
+        combine, merged, again = outs
+        assert torch.equal(merged, again), splits         # deterministic
+        ok, err = within(merged, ref)
+        assert ok, (splits, err)
+        d = (merged.float() - combine.float()).abs()
+        assert bool((d <= ATOL + RTOL * combine.float().abs()).all()), (splits, d.max().item())
+    rc = lib.titan_mla_sparse_attention_sem(*args, *o, *tail, sem.data_ptr(), need - 1, stream)
+    assert rc == 1 and b"semaphores" in lib.titan_last_error()
+    from kernels import titan_native
+    assert titan_native.device_error(qd) == 0

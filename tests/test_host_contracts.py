@@ -61,6 +61,30 @@ def test_split_heuristic_matches_restatement():
         assert _choose_num_kv_splits(T, G, topk, sms) == O.choose_num_kv_splits(T, G, topk, sms), (T, G, topk, sms)
 
 
+# (cluster size, co-resident clusters, clusters with one CTA per SM) of the MLA
+# kernel on a 148-SM B200, as titan_mla_max_active_clusters /
+# titan_mla_max_exclusive_clusters report them.
+B200_CLUSTER_TABLES = ((1, 296, 148), (2, 148, 74), (4, 71, 33), (8, 33, 15), (16, 14, 7))
+
+
+def test_b200_split_policy_picks():
+    """The automatic split counts for the decode batch sizes, and the launch
+    layout (cluster size C, clusters per token NC) the launcher derives."""
+    from kernels.titan_mla import _choose_kv_splits_b200, _launch_layout
+    picks = {B: _choose_kv_splits_b200(B, 1, 2176, 148, B200_CLUSTER_TABLES) for B in (1, 2, 4, 8)}
+    assert picks == {1: 80, 2: 40, 4: 35, 8: 17}, picks
+    assert _launch_layout(1, 80, B200_CLUSTER_TABLES) == (16, 5)   # last-arriver merge (NC <= C)
+    assert _launch_layout(2, 40, B200_CLUSTER_TABLES) == (8, 5)
+    assert _launch_layout(8, 17, B200_CLUSTER_TABLES) == (1, 17)   # combine kernel
+    assert _launch_layout(8, 16, B200_CLUSTER_TABLES) == (16, 1)
+    for T in (148, 149, 4096):
+        assert _choose_kv_splits_b200(T, 1, 2176, 148, B200_CLUSTER_TABLES) == 1
+    assert _choose_kv_splits_b200(0, 1, 2176, 148, B200_CLUSTER_TABLES) == 1
+    for B in range(1, 148):
+        S = _choose_kv_splits_b200(B, 1, 2176, 148, B200_CLUSTER_TABLES)
+        assert 1 <= S and B * S <= 148, (B, S)
+
+
 def test_moe_argument_errors_are_value_errors():
     from kernels.titan_moe_align import titan_moe_align_small
     ok = torch.zeros(2, 8, dtype=torch.int32)
