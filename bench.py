@@ -376,18 +376,23 @@ def run_ours(args, dist):
     iso_us = statistics.fmean(timed_cold(lambda k: g1.replay(), max(10, min(K, 100)), flush, load1)) * 1000
     g1.reset()
 
-    # ---- e2e: public API, pinned host inputs and output copy inside the timed region
+    # ---- e2e: public API, pinned host inputs and output copy inside the timed
+    # region.  Each step's q and indices sit back to back in one pinned
+    # staging row and cross to the device in ONE copy (small pinned copies
+    # cost ~5-8 us of copy-engine latency each on this platform); the API is
+    # called on device views of that buffer and the output is read back.
     sets = 64
     q_sets, idx_sets = decode_sets(1, sets, 199 + rank)
-    q_host = q_sets.pin_memory()
-    idx_host = idx_sets.pin_memory()
+    q_bytes = q_sets[0].numel() * 2
+    staging = torch.cat([q_sets.reshape(sets, -1).view(torch.uint8),
+                         idx_sets.reshape(sets, -1).view(torch.uint8)], 1).pin_memory()
     out_host = torch.empty((sets, 1, HEADS, 512), dtype=torch.bfloat16).pin_memory()
-    qd = torch.empty(1, HEADS, 512, dtype=torch.bfloat16, device=dev)
-    idd = torch.empty(1, 1, TOPK, dtype=torch.int32, device=dev)
+    landing = torch.empty(staging.shape[1], dtype=torch.uint8, device=dev)
+    qd = landing[:q_bytes].view(torch.bfloat16).view(1, HEADS, 512)
+    idd = landing[q_bytes:].view(torch.int32).view(1, 1, TOPK)
 
     def e2e_step(k):
-        qd.copy_(q_host[k % sets], non_blocking=True)
-        idd.copy_(idx_host[k % sets], non_blocking=True)
+        landing.copy_(staging[k % sets], non_blocking=True)
         o = attn(qd, kvs[k % REPLICAS], idd, SM_SCALE, sm_count=sms)
         out_host[k % sets].copy_(o, non_blocking=True)
 
@@ -523,8 +528,9 @@ def run_ours(args, dist):
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "algorithmic_bytes_per_call": bytes_per_call,
                          "kernel": ("sparse_mla_kernel<true> (split + cluster merge + last-arriver merge), whole call, back to back" if launches_per_call == 1 else "sparse_mla_kernel + combine (whole call, back to back)")},
-            "e2e": {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": q_sets[0].numel() * 2 + idx_sets[0].numel() * 4,
-                    "d2h_bytes_per_step": HEADS * 512 * 2},
+            "e2e": {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": staging.shape[1],
+                    "d2h_bytes_per_step": HEADS * 512 * 2,
+                    "copies_per_step": "1 H2D (q + indices, one pinned staging row), 1 D2H (output)"},
             "gpu_launches": K * launches_per_call,
             "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"],
                        "samples": clocks["samples"]},
