@@ -44,6 +44,7 @@ constexpr int kBN = 32;                     // rows per tile (four 8-row n-tiles
 constexpr int kRedStride = 40;              // floats per head row of a warp's partial scores
 constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (bf16, 32 rows + pad)
 constexpr int kMaxCluster = 16;
+constexpr int kRing = 3;                    // row-gather ring: tiles in flight ahead of the math + 1
 constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -51,10 +52,15 @@ struct Smem {
   float red[kWarps][kHeads * kRedStride];  // partial scores of each warp
   uint32_t p[kHeads * kPStrideWords];      // bf16(p * scale), n-order
   float rcv[kHeads * kD];                  // cluster merge: [C][16][512/C] slices pushed by the peers
-  float stage[kHeads * kD];                // cluster merge: this CTA's acc as [owner][16][512/C]
+  union {
+    float stage[kHeads * kD];              // cluster merge: this CTA's acc as [owner][16][512/C]
+    struct {
+      uint4 rows[kRing][kWarps][4][32];    // tile loop: lane's four 16-byte row pieces per stage
+      float scale[kRing][kBN];             // row scales of the stage's tile, n-order
+    } ring;                                // (dead before the merge stages its accumulator)
+  } u;
   float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
-  float scale[kBN];                        // row scales of the tile, n-order
-  uint32_t vword[4];                       // per n-tile: bit 4n = row n valid
+  uint32_t vword[kRing][4];                // per stage and n-tile: bit 4n = row n valid
   float alpha[kHeads];
   float2 ml[kHeads];                       // final (m, l) of this CTA
   float cw[kMaxCluster][kHeads];           // cluster merge weights
@@ -175,7 +181,6 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   const int32_t *idx_row = p.idx + (int64_t)t * p.idx_st;
   const uint8_t *kv_lane = p.kv + warp * 64 + c * 16;  // this lane's 16-byte column of a row
   const int64_t seq_kv = p.seq_kv;
-  const bool scale_loader = warp < 4 && c == 0;          // loads scales of n-tile `warp`
 
   // Row indices of tile j for this lane: n-tile nt, n-order row g.
   auto load_idx = [&](int j, int (&r)[4]) {
@@ -186,23 +191,45 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     }
   };
   auto row_ok = [&](int r) { return r >= 0 && (int64_t)r < seq_kv; };
-  auto load_rows = [&](const int (&r)[4], uint4 (&kb)[4], float &sc) {
+  // Gather of tile j into ring stage st, asynchronously (cp.async): each lane
+  // copies its own four 16-byte row pieces (its MMA B fragments), zero-filled
+  // for masked rows, which are never read; the scale loaders fetch the row
+  // scales; warps 0-3 record which rows are valid.  One commit group per
+  // tile, empty past the last tile.
+  auto issue = [&](int j, int st, const int (&r)[4]) {
+    if (j < n_tiles) {
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-      kb[nt] = row_ok(r[nt]) ? ld_global_nc_v4(kv_lane + (int64_t)r[nt] * p.kv_rs) : make_uint4(0, 0, 0, 0);
-    sc = 0.0f;
-    if (scale_loader) {
-      const int rs = pick4(r, warp);
-      if (row_ok(rs)) sc = ld_global_nc_f32(p.kv + (int64_t)rs * p.kv_rs + 512);
+      for (int nt = 0; nt < 4; ++nt) {
+        const bool ok = row_ok(r[nt]);
+        cp_async_16_zfill(&sm.u.ring.rows[st][warp][nt][lane],
+                          ok ? static_cast<const void *>(kv_lane + (int64_t)r[nt] * p.kv_rs) : p.q, ok ? 16u : 0u);
+      }
+      if (warp < 4) {
+        const int rs = pick4(r, warp);
+        const bool ok = row_ok(rs);
+        if (c == 0)
+          cp_async_4_zfill(&sm.u.ring.scale[st][warp * 8 + g],
+                           ok ? static_cast<const void *>(p.kv + (int64_t)rs * p.kv_rs + 512) : p.q, ok ? 4u : 0u);
+        const uint32_t vb = __ballot_sync(0xffffffffu, c == 0 && ok);
+        if (lane == 0) sm.vword[st][warp] = vb;
+      }
     }
+    cp_async_commit();
   };
 
-  int r_cur[4], r_next[4];
-  uint4 kb_cur[4];
-  float sc_cur;
-  load_idx(0, r_cur);
-  load_idx(1, r_next);
-  load_rows(r_cur, kb_cur, sc_cur);
+  // Tiles 0 and 1 in flight; r_a / r_b hold the indices of tiles 2 and 3.
+  int r_a[4], r_b[4];
+  {
+    int r0[4];
+    load_idx(0, r0);
+    load_idx(1, r_a);
+    load_idx(2, r_b);
+    issue(0, 0, r0);
+    issue(1, 1, r_a);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
+    load_idx(3, r_b);
+  }
 
   // q fragments for this warp's 64 dims (A operand of QK), 4 k-steps.
   uint32_t qa[4][4];
@@ -243,13 +270,18 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   const int red_nt = red_j >> 3;
   const int red_n = red_j & 7;
 
+  int st = 0, st_issue = 2;  // ring stage of tile i and of tile i + 2
   for (int i = 0; i < n_tiles; ++i) {
-    // Next tile's rows are in flight while this tile computes.
-    uint4 kb_nxt[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-    float sc_nxt = 0.0f;
-    int r_nn[4];
-    if (i + 1 < n_tiles) load_rows(r_next, kb_nxt, sc_nxt);
-    load_idx(i + 2, r_nn);
+    // Tile i + 2 goes in flight, tile i + 4's indices are fetched, and tile
+    // i's pieces (this lane's own copies) are waited for.
+    issue(i + 2, st_issue, r_a);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
+    load_idx(i + 4, r_b);
+    cp_async_wait<2>();
+    uint4 kb_cur[4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) kb_cur[nt] = sm.u.ring.rows[st][warp][nt][lane];
 
     // ---- QK^T over this warp's 64 dims; keep the bf16 B fragments for PV.
     uint32_t kf[4][4][2];
@@ -275,12 +307,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
         *reinterpret_cast<float2 *>(&red[(g + 8) * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[nt][2], sacc[nt][3]);
       }
     }
-    if (warp < 4) {
-      const uint32_t vb = __ballot_sync(0xffffffffu, c == 0 && row_ok(pick4(r_cur, warp)));
-      if (lane == 0) sm.vword[warp] = vb;
-      if (c == 0) sm.scale[warp * 8 + g] = sc_cur;
-    }
-    __syncthreads();
+    __syncthreads();  // partial scores, and this tile's scales (waited for by their loaders)
 
     // ---- Reduce the 8 partial scores, scale, mask, online softmax, P.
     {
@@ -291,9 +318,9 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
         s0 += v.x;
         s1 += v.y;
       }
-      const uint32_t vw = sm.vword[red_nt];
+      const uint32_t vw = sm.vword[st][red_nt];
       const bool v0 = (vw >> (4 * red_n)) & 1u, v1 = (vw >> (4 * red_n + 4)) & 1u;
-      const float sc0 = sm.scale[red_j], sc1 = sm.scale[red_j + 1];
+      const float sc0 = sm.u.ring.scale[st][red_j], sc1 = sm.u.ring.scale[st][red_j + 1];
       const float x0 = v0 ? (s0 * sc0) * p.scale_log2 : kNegLarge;
       const float x1 = v1 ? (s1 * sc1) * p.scale_log2 : kNegLarge;
       float mx = fmaxf(x0, x1);
@@ -341,14 +368,10 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
         }
       }
     }
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      kb_cur[nt] = kb_nxt[nt];
-      r_cur[nt] = r_next[nt];
-      r_next[nt] = r_nn[nt];
-    }
-    sc_cur = sc_nxt;
+    st = st == kRing - 1 ? 0 : st + 1;
+    st_issue = st_issue == kRing - 1 ? 0 : st_issue + 1;
   }
+  cp_async_wait<0>();  // only empty groups can remain; the ring is dead from here
 
   // ---- Epilogue.  Lane (g, c) of warp w holds, for heads g and g + 8,
   // dims 64 w + 16 c + j at acc[2 s + x][2 half + e] with j = 4 s + 2 x + e.
@@ -427,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int hl = g + 8 * half;
-      float4 *dst = reinterpret_cast<float4 *>(&sm.stage[(owner * kHeads + hl) * D + dd]);
+      float4 *dst = reinterpret_cast<float4 *>(&sm.u.stage[(owner * kHeads + hl) * D + dd]);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
         dst[s] = make_float4(acc[2 * s][2 * half], acc[2 * s][2 * half + 1], acc[2 * s + 1][2 * half],
@@ -438,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   __syncthreads();
   if (tid < C) {
     const uint32_t bytes = (uint32_t)(kHeads * D * 4);
-    bulk_s2cluster(dsmem_addr(&sm.rcv[(int)rank * kHeads * D], (uint32_t)tid), &sm.stage[tid * kHeads * D], bytes,
+    bulk_s2cluster(dsmem_addr(&sm.rcv[(int)rank * kHeads * D], (uint32_t)tid), &sm.u.stage[tid * kHeads * D], bytes,
                    dsmem_addr(&sm.merge_bar, (uint32_t)tid));
     bulk_commit();
   }
