@@ -73,8 +73,19 @@ __device__ __forceinline__ float warp_amax(float a) {
   return a;
 }
 
-// scale = max(max|x| / 127, 1e-12) with the IEEE quotient (kernels/titan_kv.py:16).
-__device__ __forceinline__ float row_scale(float amax) { return fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-12f); }
+// scale = max(max|x| / 127, 1e-12) with the IEEE quotient (kernels/titan_kv.py:16),
+// without a division: y0 = fl(amax * c), c = fl(1/127), corrected once with
+// the exact FMA residual (Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990).  amax is
+// the magnitude of a bf16 value, so every possible input can be and is checked
+// exhaustively (tests/test_kv_scale_exact.py): the result after the 1e-12
+// floor equals the IEEE quotient for all 32,640 non-negative finite bf16.
+constexpr float kInv127 = 0.007874015718698502f;  // fl(1/127)
+__device__ __forceinline__ float row_scale(float amax) {
+  const float y0 = __fmul_rn(amax, kInv127);
+  const float r = __fmaf_rn(-y0, 127.0f, amax);
+  return fmaxf(__fmaf_rn(r, kInv127, y0), 1.0e-12f);
+}
 
 // Each warp quantises kKvRowsPerWarp rows; every row's two 16-byte loads per
 // lane are issued before any arithmetic so ~4 KB per warp is in flight.
@@ -147,10 +158,16 @@ __device__ __forceinline__ uint32_t umax16x2(uint32_t a, uint32_t b) {
 
 // 32 values (16 bf16x2 words) of one row held by one lane -> 8 packed int8
 // words, four values at a time (same arithmetic and fallback as quant16).
+// y = v * rcp and the rounding residual d = y - rint(y) (exact) are packed
+// f32x2 operations.  The window test stays per group of four values: a warp
+// executes the exact path whenever any of its lanes needs it, so a wider
+// group would multiply the divisions executed (one lane in a 32-value group
+// hits the window for ~12 % of warp steps).
 __device__ __forceinline__ void quant32(const uint32_t (&w)[16], float scale, float rcp, uint32_t (&out)[8]) {
   const float2 rcp2 = make_float2(rcp, rcp);
   const float2 mag2 = make_float2(kRoundMagic, kRoundMagic);
   const float2 nmag2 = make_float2(-kRoundMagic, -kRoundMagic);
+  const float2 neg1 = make_float2(-1.0f, -1.0f);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     float2 m[2];
@@ -160,8 +177,8 @@ __device__ __forceinline__ void quant32(const uint32_t (&w)[16], float scale, fl
       const uint32_t wd = w[2 * k + e];
       const float2 y = __fmul2_rn(make_float2(__uint_as_float(wd << 16), __uint_as_float(wd & 0xFFFF0000u)), rcp2);
       m[e] = __fadd2_rn(y, mag2);
-      const float2 r = __fadd2_rn(m[e], nmag2);
-      dmax = fmaxf(dmax, fmaxf(fabsf(y.x - r.x), fabsf(y.y - r.y)));
+      const float2 d = __ffma2_rn(__fadd2_rn(m[e], nmag2), neg1, y);
+      dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
     }
     if (dmax > 0.49993896484375f) {  // a value within 2^-14 of a half-integer: exact quotient
 #pragma unroll

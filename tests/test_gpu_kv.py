@@ -133,3 +133,21 @@ def test_graph_capture_replay(native_lib, cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(cache, want)
     graph.reset()
+
+
+def test_every_bf16_magnitude_as_row_max(native_lib, cuda_device):
+    """One row per non-negative finite bf16 amax (32,640 rows, all scales the
+    writer can produce, subnormal to near-max), other values uniform in
+    [-amax, amax]: bytes bit-exact against the C oracle (IEEE division)."""
+    from kernels.titan_kv import store_int8
+    g = torch.Generator().manual_seed(17)
+    amax = torch.arange(0x7F80, dtype=torch.int32).mul(1 << 16).view(torch.float32)
+    x = (torch.rand(amax.numel(), 512, generator=g, dtype=torch.float64) * 2 - 1) * amax[:, None].double()
+    x = x.to(torch.float32).to(torch.bfloat16)
+    x[:, 7] = amax.to(torch.bfloat16)                       # exact bf16: amax itself
+    x[1::2, 7] = -x[1::2, 7]
+    n = x.shape[0]
+    cache = torch.zeros((n + 255) // 256, 256, 528, dtype=torch.int8, device=cuda_device)
+    store_int8(x.to(cuda_device), cache, torch.arange(n, device=cuda_device))
+    got = cache.view(-1, 528)[:n].cpu().numpy().view(np.uint8)
+    assert np.array_equal(got, _c_rows(x))
