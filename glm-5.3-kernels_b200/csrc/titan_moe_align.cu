@@ -68,13 +68,12 @@ __global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restr
   __syncwarp();
 
   // Exclusive prefix of padded counts: lane owns experts [9 lane, 9 lane + 9).
-  int local[kMoePerLane], cnt[kMoePerLane];
+  int local[kMoePerLane];
   int sum = 0;
 #pragma unroll
   for (int k = 0; k < kMoePerLane; ++k) {
-    cnt[k] = s_count[kMoePerLane * lane + k];
     local[k] = sum;
-    sum += (cnt[k] + 7) & ~7;
+    sum += (s_count[kMoePerLane * lane + k] + 7) & ~7;
   }
   int incl = sum;
 #pragma unroll
@@ -84,16 +83,21 @@ __global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restr
   }
   const int excl = incl - sum;
 #pragma unroll
-  for (int k = 0; k < kMoePerLane; ++k) {
-    const int e = kMoePerLane * lane + k;
-    const int off = excl + local[k];
-    s_offset[e] = off;
-    const int blocks = ((cnt[k] + 7) & ~7) >> 3;
-    for (int b = 0; b < blocks; ++b) s_experts[(off >> 3) + b] = e;
-  }
+  for (int k = 0; k < kMoePerLane; ++k) s_offset[kMoePerLane * lane + k] = excl + local[k];
   __syncwarp();
-  if (e0 >= 0) s_sorted[s_offset[e0] + rank0] = lane;
-  if (e1 >= 0) s_sorted[s_offset[e1] + rank1] = lane + 32;
+  // Scatter: route j goes to off_e + rank_j.  Offsets are multiples of 8, so
+  // the route whose rank is a multiple of 8 opens block (off_e + rank_j) / 8
+  // of its expert: exactly ceil(count_e / 8) blocks per expert, no loop.
+  if (e0 >= 0) {
+    const int pos = s_offset[e0] + rank0;
+    s_sorted[pos] = lane;
+    if ((rank0 & 7) == 0) s_experts[pos >> 3] = e0;
+  }
+  if (e1 >= 0) {
+    const int pos = s_offset[e1] + rank1;
+    s_sorted[pos] = lane + 32;
+    if ((rank1 & 7) == 0) s_experts[pos >> 3] = e1;
+  }
   __syncwarp();
   if (vec_out) {
     for (int i = lane; i < 2 * R; i += 32)
