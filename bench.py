@@ -307,6 +307,50 @@ class DecodeBench:
         self.graph.reset()
 
 
+class PagedBench:
+    """Config 2 on a paged layout: the 262,144-row cache as 4096 blocks of 64
+    rows, one request per call with its own block table (a random block
+    permutation) and its own 2048 distinct request-local positions + 128 x -1.
+    `fused` times triton_mla_sparse_attention_paged (the gather translates);
+    otherwise the conversion kernel runs first and the reader reads its
+    output, as the reference's backend does (integration/titan_backend.py:
+    49-54).  Calls back to back in one CUDA graph over the cache replicas."""
+
+    BLOCK = 64
+
+    def __init__(self, kvs, calls, seed, sms, fused):
+        from kernels.titan_index import triton_convert_req_index_to_global_index as conv
+        from kernels.titan_mla import triton_mla_sparse_attention as attn
+        from kernels.titan_mla import triton_mla_sparse_attention_paged as attn_paged
+        dev = kvs[0].device
+        g = torch.Generator().manual_seed(seed)
+        nb = KV_ROWS // self.BLOCK
+        self.bt = torch.stack([torch.randperm(nb, generator=g) for _ in range(calls)]).to(torch.int32).to(dev)
+        tok = torch.full((calls, 1, TOPK), -1, dtype=torch.int32)
+        for j in range(calls):
+            tok[j, 0, :VALID] = torch.randperm(KV_ROWS, generator=g)[:VALID].to(torch.int32)
+        self.tok = tok.to(dev)
+        self.q = torch.randn(calls, 1, HEADS, 512, generator=g).to(torch.bfloat16).to(dev)
+        self.req = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def run():
+            for j in range(calls):
+                kv = kvs[j % len(kvs)]
+                bt = self.bt[j:j + 1]
+                if fused:
+                    attn_paged(self.q[j], kv, self.tok[j], self.req, bt, self.BLOCK, SM_SCALE, sm_count=sms)
+                else:
+                    glob = conv(self.req, bt, self.tok[j, :, :], BLOCK_SIZE=self.BLOCK, NUM_TOPK_TOKENS=TOPK)
+                    attn(self.q[j], kv, glob.view(1, 1, TOPK), SM_SCALE, sm_count=sms)
+        self.graph, _ = capture(run)
+
+    def time(self, replays, flush):
+        return timed_cold(lambda k: self.graph.replay(), replays, flush)
+
+    def close(self):
+        self.graph.reset()
+
+
 def splits_and_launches(batch, sms, device_index):
     """Split count the B200 policy picks, its cluster size and kernel launches
     per call (the combine kernel runs only when the split kernel cannot merge
@@ -343,6 +387,12 @@ def run_ours(args, dist):
         store_int8(latents(KV_ROWS, 1234 + r, dev) if r else lat, c, slots)
         caches.append(c)
     kvs = [c.view(KV_ROWS, 1, ROW_BYTES) for c in caches]
+    # Every rank builds the same replicas: compare a checksum of each replica's
+    # bytes across ranks (four 16-bit lanes of a wrapping int64 word sum, so
+    # the float64 reduction is exact).
+    sums = [int(c.view(torch.int64).sum()) for c in caches]
+    lanes = [float((x >> (16 * k)) & 0xFFFF) for x in sums for k in range(4)]
+    cache_identical = all(dist.max(v) == -dist.max(-v) for v in lanes)
     torch.cuda.synchronize()
 
     sampler.start()
@@ -435,6 +485,17 @@ def run_ours(args, dist):
     store_int8(lat, caches[0], slots)
     store_int8(latents(KV_ROWS, 1235, dev), caches[1], slots)
 
+    # ---- config 2 on a paged cache: fused translation vs conversion + reader
+    paged = {}
+    for name, fused in (("fused_us_per_call", True), ("convert_then_reader_us_per_call", False)):
+        pb = PagedBench(kvs, 64, 77 + rank, sms, fused)
+        pb.time(2, flush)
+        ms = pb.time(8, flush)
+        pb.close()
+        paged[name] = dist.max(statistics.median(ms) * 1000.0 / 64)
+    paged["block_size"] = PagedBench.BLOCK
+    secondary["paged_decode_b1"] = paged
+
     # ---- config 3: B=8 decode, tokens sharded contiguously over ranks
     lo, hi = token_block(8, world, rank)
     per = max(1, hi - lo)
@@ -496,6 +557,22 @@ def run_ours(args, dist):
             samples.append(a.elapsed_time(b) * 1000 / 100)
         moe[f"B{B}_in_graph_us"] = statistics.median(samples)
         g100.reset()
+        # config 5's second distribution: Zipf(s=1.1) over the 288 experts, no
+        # duplicate within a token
+        zw = (torch.arange(1, 289, dtype=torch.float64) ** -1.1)
+        zids = torch.stack([torch.multinomial(zw, 8, replacement=False, generator=gm) for _ in range(B)])
+        zids = zids.to(torch.int32).to(dev)
+        gz, _ = capture(lambda: [titan_moe_align_small(zids) for _ in range(100)])
+        gz.replay()
+        samples = []
+        for _ in range(5):
+            a.record()
+            gz.replay()
+            b.record()
+            torch.cuda.synchronize()
+            samples.append(a.elapsed_time(b) * 1000 / 100)
+        moe[f"B{B}_zipf_in_graph_us"] = statistics.median(samples)
+        gz.reset()
     secondary["moe_align_graph_replay"] = moe
     clocks = sampler.stop()
     dist.barrier()
@@ -532,6 +609,7 @@ def run_ours(args, dist):
                     "d2h_bytes_per_step": HEADS * 512 * 2,
                     "copies_per_step": "1 H2D (q + indices, one pinned staging row), 1 D2H (output)"},
             "gpu_launches": K * launches_per_call,
+            "cache_replicas_identical_across_ranks": cache_identical,
             "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"],
                        "samples": clocks["samples"]},
             "secondary": secondary,

@@ -4,3 +4,4 @@
 #include "titan_kv.cu"
 #include "titan_moe_align.cu"
 #include "titan_mla.cu"
+#include "titan_index.cu"

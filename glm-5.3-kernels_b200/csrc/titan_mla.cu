@@ -88,6 +88,13 @@ struct Params {
   int64_t split_topk;
   float scale_log2;  // sm_scale * log2(e)
   int *sem;          // [T][groups][16] arrival counters (zero between calls) or null: combine kernel
+  // Paged launches (kPaged): idx holds request-local token positions; row =
+  // block_table[req_id[t], tok / block_size] * block_stride_rows + tok % block_size.
+  const int32_t *req_id;
+  const int32_t *block_table;
+  int64_t bt_st0, bt_st1;
+  int num_reqs, max_blocks, block_size, block_shift;  // block_shift >= 0: block_size is 2^block_shift
+  int64_t block_stride_rows;
 };
 
 __device__ __forceinline__ int pick4(const int (&v)[4], int i) {
@@ -145,7 +152,7 @@ __device__ __forceinline__ void merge_cluster_partials(const Params &p, int t, i
   }
 }
 
-template <bool kPartialOut>
+template <bool kPartialOut, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
@@ -191,6 +198,27 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     }
   };
   auto row_ok = [&](int r) { return r >= 0 && (int64_t)r < seq_kv; };
+  // Paged: the request's block-table row, and the translation of a tile's
+  // request-local positions to cache rows (a negative position, a block past
+  // the table or a row outside int32 gives -1; the gather masks rows outside
+  // [0, seq_kv) as for any index).  Same mapping as the standalone
+  // titan_convert_req_index_to_global.
+  // The request id is only consumed inside translate (a select, no branch),
+  // so its load and the first position loads are in flight together.
+  const int req = kPaged ? __ldg(p.req_id + t) : 0;
+  auto translate = [&](const int (&tok)[4], int (&r)[4]) {
+    const bool req_ok = req >= 0 && req < p.num_reqs;
+    const int32_t *bt_row = p.block_table + (int64_t)(req_ok ? req : 0) * p.bt_st0;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int x = tok[nt];
+      const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
+      const bool ok = req_ok && x >= 0 && blk < p.max_blocks;
+      const int64_t base = ok ? (int64_t)__ldg(bt_row + (int64_t)blk * p.bt_st1) : 0;
+      const int64_t row = base * p.block_stride_rows + (x - blk * p.block_size);
+      r[nt] = (ok && row >= 0 && row <= 0x7fffffffLL) ? (int)row : -1;
+    }
+  };
   // Gather of tile j into ring stage st, asynchronously (cp.async): each lane
   // copies its own four 16-byte row pieces (its MMA B fragments), zero-filled
   // for masked rows, which are never read; the scale loaders fetch the row
@@ -217,18 +245,36 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     cp_async_commit();
   };
 
-  // Tiles 0 and 1 in flight; r_a / r_b hold the indices of tiles 2 and 3.
+  // Tiles 0 and 1 in flight; r_a / r_b hold the rows of tiles 2 and 3 and,
+  // when paged, t_c the request-local positions of tile 4 (positions are
+  // fetched three tiles ahead and translated two tiles ahead).
   int r_a[4], r_b[4];
+  int t_c[4];
   {
     int r0[4];
-    load_idx(0, r0);
-    load_idx(1, r_a);
-    load_idx(2, r_b);
-    issue(0, 0, r0);
-    issue(1, 1, r_a);
+    if constexpr (kPaged) {
+      int x0[4], x1[4], x2[4], x3[4];
+      load_idx(0, x0);
+      load_idx(1, x1);
+      load_idx(2, x2);
+      load_idx(3, x3);
+      load_idx(4, t_c);
+      translate(x0, r0);
+      translate(x1, r_a);
+      issue(0, 0, r0);
+      issue(1, 1, r_a);
+      translate(x2, r_a);
+      translate(x3, r_b);
+    } else {
+      load_idx(0, r0);
+      load_idx(1, r_a);
+      load_idx(2, r_b);
+      issue(0, 0, r0);
+      issue(1, 1, r_a);
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
-    load_idx(3, r_b);
+      for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
+      load_idx(3, r_b);
+    }
   }
 
   // q fragments for this warp's 64 dims (A operand of QK), 4 k-steps.
@@ -277,7 +323,12 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     issue(i + 2, st_issue, r_a);
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
-    load_idx(i + 4, r_b);
+    if constexpr (kPaged) {
+      translate(t_c, r_b);
+      load_idx(i + 5, t_c);
+    } else {
+      load_idx(i + 4, r_b);
+    }
     cp_async_wait<2>();
     uint4 kb_cur[4];
 #pragma unroll
@@ -682,7 +733,8 @@ static int prepare_device(size_t smem, const int **capacity) {
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "mla: device ordinal %d out of range", dev);
   if (!g_dev_ready[dev]) {
-    void (*kernels[2])(const Params) = {sparse_mla_kernel<false>, sparse_mla_kernel<true>};
+    void (*kernels[4])(const Params) = {sparse_mla_kernel<false, false>, sparse_mla_kernel<true, false>,
+                                        sparse_mla_kernel<false, true>, sparse_mla_kernel<true, true>};
     for (auto k : kernels) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -690,7 +742,7 @@ static int prepare_device(size_t smem, const int **capacity) {
     }
     int sms = 0, per_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sparse_mla_kernel<false>, kThreads, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sparse_mla_kernel<false, false>, kThreads, smem) != cudaSuccess ||
         per_sm < 1) {
       cudaGetLastError();
       per_sm = 1;
@@ -710,7 +762,7 @@ static int prepare_device(size_t smem, const int **capacity) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false, false>, &cfg) != cudaSuccess) {
         cudaGetLastError();  // clear a rejected query: that size is not schedulable
         n = 0;
       }
@@ -762,7 +814,7 @@ static int max_active_clusters(int cluster_size, bool exclusive) {
     if (smem > (size_t)optin) return -1;
     // Raise the opt-in ceiling so the query is legal; launches still request
     // sizeof(Smem).
-    if (cudaFuncSetAttribute(sparse_mla_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(sparse_mla_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess) {
       cudaGetLastError();
       return -1;
@@ -780,9 +832,9 @@ static int max_active_clusters(int cluster_size, bool exclusive) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false>, &cfg);
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false, false>, &cfg);
   if (exclusive)  // back to the launch setting
-    cudaFuncSetAttribute(sparse_mla_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+    cudaFuncSetAttribute(sparse_mla_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
   if (e != cudaSuccess) {
     cudaGetLastError();
     return -1;
@@ -819,14 +871,25 @@ extern "C" int64_t titan_mla_semaphore_count(int64_t num_tokens, int64_t num_hea
 namespace titan {
 namespace mla {
 
+// Request-local indices of a paged launch (see Params).
+struct PagedIndex {
+  const int32_t *req_id;
+  int64_t num_reqs;
+  const int32_t *block_table;
+  int64_t bt_st0, bt_st1, max_blocks, block_size, block_stride_rows;
+};
+
 // Shared launcher of titan_mla_sparse_attention (sem == nullptr: partials of
-// several clusters are merged by the combine kernel) and
-// titan_mla_sparse_attention_sem (the split kernel merges them itself).
+// several clusters are merged by the combine kernel),
+// titan_mla_sparse_attention_sem (the split kernel merges them itself) and
+// titan_mla_sparse_attention_paged (paged != nullptr: indices are
+// request-local positions translated in the gather).
 static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_head, const void *kv,
                       int64_t kv_row_stride, int64_t seq_kv, const int32_t *indices, int64_t indices_stride_token,
                       int64_t topk, void *out, int64_t out_stride_token, int64_t out_stride_head, int64_t num_tokens,
                       int64_t num_heads, float sm_scale, int64_t num_kv_splits, void *workspace,
-                      int64_t workspace_bytes, int32_t *sem, int64_t sem_count, titan_stream_t stream) {
+                      int64_t workspace_bytes, int32_t *sem, int64_t sem_count, const PagedIndex *paged,
+                      titan_stream_t stream) {
   if (num_tokens < 0 || num_heads <= 0 || topk < 0 || seq_kv < 0)
     return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: invalid sizes");
   if (num_tokens == 0) return TITAN_OK;
@@ -892,6 +955,26 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   prm.part_o = nullptr;
   prm.part_lse = nullptr;
   prm.sem = in_kernel_merge ? sem : nullptr;
+  prm.req_id = nullptr;
+  prm.block_table = nullptr;
+  prm.bt_st0 = prm.bt_st1 = 0;
+  prm.num_reqs = prm.max_blocks = 0;
+  prm.block_size = 1;
+  prm.block_shift = 0;
+  prm.block_stride_rows = 0;
+  if (paged != nullptr) {
+    prm.req_id = paged->req_id;
+    prm.block_table = paged->block_table;
+    prm.bt_st0 = paged->bt_st0;
+    prm.bt_st1 = paged->bt_st1;
+    prm.num_reqs = (int)paged->num_reqs;
+    prm.max_blocks = (int)paged->max_blocks;
+    prm.block_size = (int)paged->block_size;
+    prm.block_shift = -1;
+    for (int sh = 0; sh < 31; ++sh)
+      if ((1ll << sh) == paged->block_size) prm.block_shift = sh;
+    prm.block_stride_rows = paged->block_stride_rows;
+  }
   if (NC > 1) {
     const int64_t o_bytes = num_tokens * NC * prm.Hp * kD * 4;
     prm.part_o = static_cast<float *>(workspace);
@@ -913,8 +996,13 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = C > 1 ? 2 : 1;
-  cudaError_t e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true>, prm)
-                         : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false>, prm);
+  cudaError_t e;
+  if (paged != nullptr)
+    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true>, prm)
+               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true>, prm);
+  else
+    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, false>, prm)
+               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false>, prm);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla launch (C=%d): %s", C, cudaGetErrorString(e));
   if (NC == 1 || in_kernel_merge) return TITAN_OK;
   // Combine the NC cluster partials: 32 CTAs per (token, head group).
@@ -935,7 +1023,8 @@ extern "C" int titan_mla_sparse_attention(const void *q, int64_t q_stride_token,
                                           titan_stream_t stream) {
   return titan::mla::launch_mla(q, q_stride_token, q_stride_head, kv, kv_row_stride, seq_kv, indices,
                                 indices_stride_token, topk, out, out_stride_token, out_stride_head, num_tokens,
-                                num_heads, sm_scale, num_kv_splits, workspace, workspace_bytes, nullptr, 0, stream);
+                                num_heads, sm_scale, num_kv_splits, workspace, workspace_bytes, nullptr, 0, nullptr,
+                                stream);
 }
 
 extern "C" int titan_mla_sparse_attention_sem(const void *q, int64_t q_stride_token, int64_t q_stride_head,
@@ -950,7 +1039,30 @@ extern "C" int titan_mla_sparse_attention_sem(const void *q, int64_t q_stride_to
   return titan::mla::launch_mla(q, q_stride_token, q_stride_head, kv, kv_row_stride, seq_kv, indices,
                                 indices_stride_token, topk, out, out_stride_token, out_stride_head, num_tokens,
                                 num_heads, sm_scale, num_kv_splits, workspace, workspace_bytes, semaphores,
-                                semaphore_count, stream);
+                                semaphore_count, nullptr, stream);
+}
+
+extern "C" int titan_mla_sparse_attention_paged(
+    const void *q, int64_t q_stride_token, int64_t q_stride_head, const void *kv, int64_t kv_row_stride,
+    int64_t seq_kv, const int32_t *token_indices, int64_t indices_stride_token, int64_t topk, const int32_t *req_id,
+    int64_t num_reqs, const int32_t *block_table, int64_t block_table_stride_req, int64_t block_table_stride_block,
+    int64_t max_blocks_per_req, int64_t block_size, int64_t block_stride_rows, void *out, int64_t out_stride_token,
+    int64_t out_stride_head, int64_t num_tokens, int64_t num_heads, float sm_scale, int64_t num_kv_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *semaphores, int64_t semaphore_count, titan_stream_t stream) {
+  using namespace titan;
+  if (num_tokens > 0 && topk > 0 && (req_id == nullptr || (block_table == nullptr && num_reqs > 0 && max_blocks_per_req > 0)))
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla paged: null req_id or block_table");
+  if (block_size <= 0 || block_size > 0x40000000LL || num_reqs < 0 || max_blocks_per_req < 0 ||
+      max_blocks_per_req > 0x7fffffffLL || num_reqs > 0x7fffffffLL || block_stride_rows < 0)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla paged: invalid block geometry");
+  if (semaphores != nullptr && (uintptr_t)semaphores % 4)
+    return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: semaphores must be an int32 array");
+  const mla::PagedIndex paged = {req_id, num_reqs, block_table, block_table_stride_req, block_table_stride_block,
+                                 max_blocks_per_req, block_size, block_stride_rows};
+  return mla::launch_mla(q, q_stride_token, q_stride_head, kv, kv_row_stride, seq_kv, token_indices,
+                         indices_stride_token, topk, out, out_stride_token, out_stride_head, num_tokens, num_heads,
+                         sm_scale, num_kv_splits, workspace, workspace_bytes, semaphores, semaphore_count, &paged,
+                         stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -296,3 +296,87 @@ def triton_mla_sparse_attention(
     if rc:
         _native.check(rc, "triton_mla_sparse_attention")
     return out
+
+
+def triton_mla_sparse_attention_paged(
+    q: torch.Tensor,
+    kv: torch.Tensor,
+    token_indices: torch.Tensor,
+    req_id_per_token: torch.Tensor,
+    block_table: torch.Tensor,
+    block_size: int,
+    sm_scale: float,
+    block_stride_rows: int | None = None,
+    num_kv_splits: int | None = None,
+    sm_count: int | None = None,
+) -> torch.Tensor:
+    """Sparse MLA over request-local top-k positions of a paged INT8 cache.
+
+    The reference's backend converts the indexer's request-local positions to
+    cache rows and then calls the reader (integration/titan_backend.py:48-54).
+    Here the gather does the conversion (one launch, no global-index round
+    trip); the result is bit-identical to
+
+        triton_mla_sparse_attention(q, kv, titan_index.triton_convert_req_index_to_global_index(
+            req_id_per_token, block_table, token_indices, BLOCK_SIZE=block_size,
+            NUM_TOPK_TOKENS=topk, BLOCK_STRIDE_ROWS=block_stride_rows).view(T, 1, -1), ...)
+
+    Args:
+        q:             [num_tokens, num_heads_q, 512] bf16
+        kv:            [rows, 1, 528] int8: the paged cache viewed as rows
+        token_indices: [num_tokens, topk] or [num_tokens, 1, topk] int32 request-local
+                       positions (negative = none)
+        req_id_per_token: [num_tokens] int32 request of each token
+        block_table:   [num_requests, max_blocks] int32 cache block of each request block
+        block_size:    positions per block
+        block_stride_rows: cache rows from one block to the next (default block_size)
+        num_kv_splits, sm_count: as triton_mla_sparse_attention
+    """
+    num_tokens, num_heads_q, dim_qk = q.shape
+    assert dim_qk == _BLOCK_DMODEL and kv.dtype == torch.int8 and kv.shape[1] == 1 and kv.shape[2] == _ROW_BYTES, (
+        "the B200 kernel implements the INT8 NoPE path: dim_qk=512 with a [rows, 1, 528] int8 cache")
+    assert q.dtype == torch.bfloat16, "q must be bf16"
+    ti = token_indices if token_indices.dim() == 2 else token_indices[:, 0, :]
+    assert ti.dim() == 2 and ti.shape[0] == num_tokens and ti.dtype == torch.int32, \
+        "token_indices must be int32 [num_tokens, topk]"
+    index_topk = ti.shape[1]
+    assert index_topk % _MIN_BLOCK_N == 0, (
+        f"topk ({index_topk}) must be a multiple of the smallest autotune BLOCK_N ({_MIN_BLOCK_N})")
+    assert req_id_per_token.dtype == torch.int32 and req_id_per_token.numel() >= num_tokens, \
+        "req_id_per_token must be int32 [num_tokens]"
+    assert block_table.dtype == torch.int32 and block_table.dim() == 2, "block_table must be int32 [requests, blocks]"
+    assert block_size > 0, "block_size must be positive"
+    if block_stride_rows is None:
+        block_stride_rows = block_size
+    dev = q.get_device()
+    assert dev >= 0 and all(t.get_device() == dev for t in (kv, ti, req_id_per_token, block_table)), \
+        "all tensors must be CUDA tensors on one device"
+
+    num_kv_splits, ws_bytes, sem_count = _plan(dev, num_tokens, num_heads_q, index_topk, num_kv_splits, sm_count)
+    out = q.new_empty((num_tokens, num_heads_q, _BLOCK_DV))
+    if num_tokens == 0:
+        return out
+    q_st = q.stride()
+    if q_st[2] != 1 or q.data_ptr() % 16 or (q_st[0] * 2) % 16 or (q_st[1] * 2) % 16:
+        q = q.contiguous()
+        q_st = q.stride()
+    if ti.stride(1) != 1:
+        ti = ti.contiguous()
+    req = req_id_per_token if req_id_per_token.is_contiguous() else req_id_per_token.contiguous()
+    bt_st = block_table.stride()
+    out_st = out.stride()
+
+    lib = _native.load()
+    stream = torch._C._cuda_getCurrentRawStream(dev)
+    with _native.on_device(q.device):
+        sem, ws = _split_scratch(q, dev, stream, ws_bytes, sem_count) if ws_bytes > 0 else (None, None)
+        rc = lib.titan_mla_sparse_attention_paged(
+            q.data_ptr(), q_st[0], q_st[1], kv.data_ptr(), kv.stride(0), kv.shape[0],
+            ti.data_ptr(), ti.stride(0), index_topk,
+            req.data_ptr(), block_table.shape[0], block_table.data_ptr(), bt_st[0], bt_st[1], block_table.shape[1],
+            int(block_size), int(block_stride_rows),
+            out.data_ptr(), out_st[0], out_st[1], num_tokens, num_heads_q, float(sm_scale), num_kv_splits,
+            ws.data_ptr() if ws is not None else None, ws_bytes,
+            sem.data_ptr() if sem is not None else None, sem.numel() if sem is not None else 0, stream)
+    _native.check(rc, "triton_mla_sparse_attention_paged")
+    return out

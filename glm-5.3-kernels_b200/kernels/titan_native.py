@@ -40,6 +40,13 @@ SIGNATURES = {
         [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
          ctypes.c_float, _i64, _vp, _i64, _vp, _i64, _vp],
     ),
+    "titan_convert_req_index_to_global": (
+        _int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "titan_mla_sparse_attention_paged": (
+        _int,
+        [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
+         _vp, _i64, _i64, _i64, _i64, ctypes.c_float, _i64, _vp, _i64, _vp, _i64, _vp],
+    ),
     "titan_mla_noalloc_scratch_bytes": (_i64, []),
     "titan_mla_sparse_attention_noalloc": (
         _int,

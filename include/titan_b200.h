@@ -8,6 +8,9 @@
  *   titan_store_int8              replaces kernels/titan_kv.py:23-28
  *   titan_mla_sparse_attention    replaces kernels/titan_mla.py:452-581
  *   titan_moe_align_small         replaces kernels/titan_moe_align.py:49-81
+ *   titan_convert_req_index_to_global / titan_mla_sparse_attention_paged
+ *                                 replace the index conversion before the
+ *                                 reader, integration/titan_backend.py:48-54
  *
  * The Python modules titan_kv / titan_mla / titan_moe_align keep the
  * reference's names, argument meaning and exception types and call these
@@ -151,6 +154,49 @@ int titan_mla_sparse_attention_sem(const void *q, int64_t q_stride_token, int64_
                                    int64_t num_tokens, int64_t num_heads, float sm_scale,
                                    int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
                                    int32_t *semaphores, int64_t semaphore_count, titan_stream_t stream);
+
+/*
+ * Request-local top-k positions -> global cache rows (paged KV cache).
+ * Replaces the conversion the reference's backend runs before the sparse MLA
+ * reader (integration/titan_backend.py:48-54), vLLM's
+ * `triton_convert_req_index_to_global_index` (v1/attention/backends/mla/
+ * sparse_utils.py, a third-party dependency of the reference):
+ *   out[t, j] = block_table[req_id[t], tok / block_size] * block_stride_rows
+ *               + tok % block_size,   tok = token_indices[t, j]
+ *   out[t, j] = -1 if tok < 0, tok / block_size >= max_blocks_per_req, or
+ *               req_id[t] outside [0, num_reqs) (the last one is a widening:
+ *               vLLM reads out of bounds there).
+ * block_stride_rows = block_size for a contiguous cache.  All arrays int32;
+ * strides in elements; block_table_stride_block is the stride between the
+ * blocks of one request (1 when contiguous).
+ */
+int titan_convert_req_index_to_global(const int32_t *req_id, int64_t num_reqs, const int32_t *block_table,
+                                      int64_t block_table_stride_req, int64_t block_table_stride_block,
+                                      int64_t max_blocks_per_req, const int32_t *token_indices,
+                                      int64_t indices_stride_token, int64_t topk, int32_t *out,
+                                      int64_t out_stride_token, int64_t num_tokens, int64_t block_size,
+                                      int64_t block_stride_rows, titan_stream_t stream);
+
+/*
+ * titan_mla_sparse_attention_sem on request-local positions: the gather
+ * translates each position with the mapping of
+ * titan_convert_req_index_to_global (a translated row outside [0, seq_kv) is
+ * masked, like any index), so the conversion kernel, its launch and its
+ * global-index round trip disappear (the reference runs the conversion and
+ * the reader back to back, integration/titan_backend.py:49-54).  Results are
+ * bit-identical to the conversion followed by the sem/combine entry point.
+ * semaphores may be null (combine kernel for multi-cluster splits).
+ */
+int titan_mla_sparse_attention_paged(const void *q, int64_t q_stride_token, int64_t q_stride_head,
+                                     const void *kv, int64_t kv_row_stride, int64_t seq_kv,
+                                     const int32_t *token_indices, int64_t indices_stride_token, int64_t topk,
+                                     const int32_t *req_id, int64_t num_reqs, const int32_t *block_table,
+                                     int64_t block_table_stride_req, int64_t block_table_stride_block,
+                                     int64_t max_blocks_per_req, int64_t block_size, int64_t block_stride_rows,
+                                     void *out, int64_t out_stride_token, int64_t out_stride_head,
+                                     int64_t num_tokens, int64_t num_heads, float sm_scale,
+                                     int64_t num_kv_splits, void *workspace, int64_t workspace_bytes,
+                                     int32_t *semaphores, int64_t semaphore_count, titan_stream_t stream);
 
 /*
  * Allocation-free variant of titan_mla_sparse_attention (no counterpart in the

@@ -12,6 +12,9 @@ golden vectors produced by the reference's own code (tests/golden/make_golden.py
 runs kernels/titan_kv.py, kernels/titan_moe_align.py and the
 benchmarks/moe_align.py oracles); mla_sparse_attention is checked against the
 reference MLA kernels' outputs within the path's tolerance.
+convert_req_index_to_global is checked bit-exactly against golden vectors
+from vLLM's own conversion kernel (the third-party function the reference's
+backend calls, run by the Triton interpreter).
 """
 import numpy as np
 import torch
@@ -198,3 +201,30 @@ def moe_align_small_loops(flat):
     postpad = len(output)
     return (output + [count] * (count * 8 - len(output)),
             experts + [-1] * (count - len(experts)), [postpad])
+
+
+# ------------------------------------------------------ paged index conversion
+def convert_req_index_to_global(req_id, block_table, token_indices, block_size, block_stride_rows=None):
+    """Request-local top-k positions -> global cache rows (int32 [T, topk]).
+
+    Restates vLLM 0.22 v1/attention/backends/mla/sparse_utils.py:11-83
+    (`_convert_req_index_to_global_index_kernel`, called by the reference's
+    backend at integration/titan_backend.py:49-52 with BLOCK_STRIDE_ROWS):
+      blk = tok // block_size, off = tok % block_size
+      out = block_table[req, blk] * block_stride_rows + off   (int32 arithmetic)
+      out = -1 where tok < 0 or blk >= max_blocks
+    plus -1 where req_id[t] is not a row of block_table (vLLM reads out of
+    bounds there).  block_stride_rows defaults to block_size (vLLM 0.22).
+    """
+    req = np.asarray(req_id, dtype=np.int64)
+    bt = np.asarray(block_table, dtype=np.int64)
+    tok = np.asarray(token_indices, dtype=np.int64)
+    stride_rows = block_size if block_stride_rows is None else block_stride_rows
+    num_reqs, max_blocks = bt.shape
+    blk = np.where(tok >= 0, tok // block_size, -1)
+    ok = (tok >= 0) & (blk < max_blocks) & ((req >= 0) & (req < num_reqs))[:, None]
+    rr = np.clip(req, 0, max(num_reqs - 1, 0))[:, None]
+    base = bt[rr, np.clip(blk, 0, max(max_blocks - 1, 0))] if num_reqs and max_blocks else np.zeros_like(tok)
+    val = base * stride_rows + (tok - blk * block_size)
+    val = ((val + 2 ** 31) % 2 ** 32) - 2 ** 31          # two's-complement int32 wrap
+    return np.where(ok, val, -1).astype(np.int32)

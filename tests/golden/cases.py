@@ -114,3 +114,33 @@ def mla_input_digest(inp):
         h.update(inp[key].contiguous().view(torch.int16).numpy().tobytes())
     h.update(inp["indices"].contiguous().numpy().astype(np.int32).tobytes())
     return h.hexdigest()
+
+
+@dataclasses.dataclass(frozen=True)
+class IndexCase:
+    """Paged index conversion: T tokens of R requests, block tables of
+    max_blocks entries, positions uniform in [-3, max_blocks * block_size + 40)."""
+    name: str
+    seed: int
+    tokens: int
+    reqs: int
+    max_blocks: int
+    block_size: int
+    topk: int
+
+
+INDEX_CASES = (
+    IndexCase("bs64", 31, 6, 3, 5, 64, 256),
+    IndexCase("bs16", 32, 4, 2, 20, 16, 128),
+    IndexCase("bs48", 33, 3, 3, 8, 48, 128),
+    IndexCase("bs64_topk2176", 34, 2, 2, 40, 64, 2176),
+)
+
+
+def index_inputs(case):
+    g = torch.Generator().manual_seed(case.seed)
+    req = torch.randint(0, case.reqs, (case.tokens,), generator=g, dtype=torch.int32)
+    bt = torch.randint(0, 4096, (case.reqs, case.max_blocks), generator=g, dtype=torch.int32)
+    hi = case.max_blocks * case.block_size + 40
+    tok = torch.randint(-3, hi, (case.tokens, case.topk), generator=g, dtype=torch.int32)
+    return {"req_id": req, "block_table": bt, "token_indices": tok}

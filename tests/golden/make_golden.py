@@ -16,6 +16,10 @@ the tests read the committed .npz files).  Sources of truth:
   Triton interpreter on seeded bf16 latents with edge rows.
 * Sparse MLA (mla_golden.npz): kernels/titan_mla.py `triton_mla_sparse_attention`
   executed by the Triton interpreter (final, split and merge kernels).
+* Paged index conversion (index_golden.npz): vLLM's
+  `triton_convert_req_index_to_global_index`, which the reference's backend
+  calls before the reader (integration/titan_backend.py:49-52), executed by the
+  Triton interpreter (vLLM version recorded in the file).
 
 The interpreter needs three shims, all inside this script and none in the
 reference's code: libdevice `nearbyint` (absent from the interpreter) is
@@ -218,14 +222,33 @@ def gen_mla(ref):
     return out
 
 
+def gen_index():
+    # vLLM's conversion kernel (the third-party function the reference's
+    # backend calls, integration/titan_backend.py:49-52), run by the Triton
+    # interpreter; installed vLLM 0.22 has no BLOCK_STRIDE_ROWS, so these
+    # vectors pin the block_stride_rows == block_size mapping.
+    import vllm
+    from vllm.v1.attention.backends.mla.sparse_utils import triton_convert_req_index_to_global_index as conv
+    out = {"vllm_version": np.frombuffer(vllm.__version__.encode(), dtype=np.uint8)}
+    for case in C.INDEX_CASES:
+        inp = C.index_inputs(case)
+        res = conv(inp["req_id"], inp["block_table"], inp["token_indices"], BLOCK_SIZE=case.block_size,
+                   NUM_TOPK_TOKENS=case.topk)
+        for k, v in inp.items():
+            out[f"{case.name}__{k}"] = v.numpy()
+        out[f"{case.name}__out"] = res.numpy()
+        print(f"  index case {case.name}", flush=True)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--reference", type=Path, required=True)
     ap.add_argument("--out", type=Path, default=HERE)
-    ap.add_argument("--only", choices=("moe", "kv", "mla"), nargs="*")
+    ap.add_argument("--only", choices=("moe", "kv", "mla", "index"), nargs="*")
     args = ap.parse_args()
     install_interpreter_shims()
-    only = set(args.only or ("moe", "kv", "mla"))
+    only = set(args.only or ("moe", "kv", "mla", "index"))
     if "moe" in only:
         np.savez_compressed(args.out / "moe_golden.npz", **gen_moe(args.reference))
         print("wrote moe_golden.npz")
@@ -235,6 +258,9 @@ def main():
     if "mla" in only:
         np.savez_compressed(args.out / "mla_golden.npz", **gen_mla(args.reference))
         print("wrote mla_golden.npz")
+    if "index" in only:
+        np.savez_compressed(args.out / "index_golden.npz", **gen_index())
+        print("wrote index_golden.npz")
 
 
 if __name__ == "__main__":

@@ -122,3 +122,19 @@ def test_split_heuristic_restatement_table():
     assert O.choose_num_kv_splits(8, 1, 2176, 148) == 16
     assert O.choose_num_kv_splits(37, 1, 2176, 148) == 1
     assert O.choose_num_kv_splits(0, 1, 2176, 148) == 1
+
+
+def test_index_conversion_oracle_matches_vllm_goldens():
+    """oracle.convert_req_index_to_global vs vLLM's own conversion kernel
+    (Triton interpreter, tests/golden/make_golden.py), bit-exact."""
+    gold = np.load(f"{GOLDEN}/index_golden.npz")
+    assert bytes(gold["vllm_version"]).decode().startswith("0.")
+    for case in C.INDEX_CASES:
+        inp = C.index_inputs(case)
+        for k, v in inp.items():
+            assert np.array_equal(gold[f"{case.name}__{k}"], v.numpy()), (case.name, k)
+        got = O.convert_req_index_to_global(inp["req_id"].numpy(), inp["block_table"].numpy(),
+                                            inp["token_indices"].numpy(), case.block_size)
+        want = gold[f"{case.name}__out"]
+        assert np.array_equal(got, want), case.name
+        assert (want == -1).any() and (want >= 0).any()
