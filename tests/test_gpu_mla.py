@@ -224,3 +224,26 @@ def test_in_kernel_merge_matches_combine_kernel(big_cache, native_lib, cuda_devi
     assert rc == 1 and b"semaphores" in lib.titan_last_error()
     from kernels import titan_native
     assert titan_native.device_error(qd) == 0
+
+
+@pytest.mark.parametrize("tokens,heads,topk", [(160, 16, 2176), (150, 20, 96), (148, 16, 2208)])
+def test_large_single_pass(big_cache, native_lib, cuda_device, tokens, heads, topk):
+    """Single-pass launches that fill the device (prefill shapes): against the
+    FP32 oracle, with masked and out-of-range indices, an all-masked token,
+    duplicates, a top-k that is not a multiple of 128 and a head count that is
+    not a multiple of 16."""
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(tokens + heads + topk)
+    q = torch.randn(tokens, heads, 512, generator=g).to(torch.bfloat16)
+    idx = torch.randint(-40, n + 40, (tokens, 1, topk), generator=g, dtype=torch.int32)
+    idx[3] = -1                                     # a token with no valid index
+    idx[5, 0, : topk // 2] = idx[5, 0, 0]           # duplicates
+    ref = O.mla_sparse_attention(q, rows, idx, 512 ** -0.5)
+    out = attn(q.to(cuda_device), cache.view(n, 1, 528), idx.to(cuda_device), 512 ** -0.5, num_kv_splits=1)
+    ok, err = within(out, ref)
+    assert ok, err
+    assert not out[3].any()
+    from kernels import titan_native
+    assert titan_native.device_error(out) == 0
