@@ -185,20 +185,19 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   const int64_t end = min(start + p.split_topk, p.topk);
   const int n_rows = end > start ? (int)(end - start) : 0;
   const int n_tiles = (n_rows + kBN - 1) / kBN;
-  const int32_t *idx_row = p.idx + (int64_t)t * p.idx_st + start;  // this split's positions
+  const int32_t *idx_row = p.idx + (int64_t)t * p.idx_st;
   const uint8_t *kv_lane = p.kv + warp * 64 + c * 16;  // this lane's 16-byte column of a row
-  // Rows are int32: a row is valid iff 0 <= r < seq_kv, one unsigned compare.
-  const uint32_t seq_rows = (uint32_t)min(p.seq_kv, (int64_t)0x7fffffff);
+  const int64_t seq_kv = p.seq_kv;
 
   // Row indices of tile j for this lane: n-tile nt, n-order row g.
   auto load_idx = [&](int j, int (&r)[4]) {
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
-      const int pos = j * kBN + nt * 8 + g;
-      r[nt] = pos < n_rows ? __ldg(idx_row + pos) : -1;
+      const int64_t pos = start + (int64_t)j * kBN + nt * 8 + g;
+      r[nt] = (j < n_tiles && pos < end) ? __ldg(idx_row + pos) : -1;
     }
   };
-  auto row_ok = [&](int r) { return (uint32_t)r < seq_rows; };
+  auto row_ok = [&](int r) { return r >= 0 && (int64_t)r < seq_kv; };
   // Paged: the request's block-table row, and the translation of a tile's
   // request-local positions to cache rows (a negative position, a block past
   // the table or a row outside int32 gives -1; the gather masks rows outside
