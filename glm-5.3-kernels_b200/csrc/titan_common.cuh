@@ -85,32 +85,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
 }
 
-// One bulk copy global -> this CTA's shared memory, completing on `bar`.
-// dst, src 16-byte aligned; bytes a multiple of 16.  Single destination CTA.
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Same, with an L2 eviction-priority hint (createpolicy result).
-__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
-                                              uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
-      "%4;" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
-__device__ __forceinline__ uint64_t policy_evict_first() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
 // PDL (programmatic dependent launch) controls.
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -203,12 +177,6 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
-// Cluster-wide barrier with release/acquire semantics: every thread of every
-// CTA in the cluster must reach it (all CTAs of a cluster are co-scheduled).
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 // Split cluster barrier: arrive early (non-blocking), wait later.
 __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
@@ -224,11 +192,6 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void *p, uint32_t rank) {
 
 // Asynchronous remote stores into a peer CTA's shared memory that complete
 // (in bytes) on the peer's mbarrier; the sender never waits.
-__device__ __forceinline__ void st_async_f32x4(uint32_t addr, float4 v, uint32_t mbar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
-               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(mbar)
-               : "memory");
-}
 __device__ __forceinline__ void st_async_f32x2(uint32_t addr, float2 v, uint32_t mbar) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
                "f"(v.x), "f"(v.y), "r"(mbar)
@@ -250,16 +213,6 @@ __device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, const void 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
-// Generic pointer to the same shared-memory variable in CTA `rank` of this
-// cluster.  Loads through it are ordinary loads (the compiler may batch them);
-// cluster_sync()'s memory clobber keeps them after the barrier.
-template <typename T>
-__device__ __forceinline__ T *dsmem_ptr(T *p, uint32_t rank) {
-  uint64_t r;
-  asm("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
-  return reinterpret_cast<T *>(r);
-}
-
 // Arrival ticket with release (prior writes of this thread and of those
 // ordered before it by a CTA barrier) and acquire semantics at GPU scope.
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int *p, int v) {
@@ -270,12 +223,6 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int *p, int v) {
 
 __device__ __forceinline__ void st_relaxed_gpu(int *p, int v) {
   asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ float ld_global_nc_f32(const void *p) {
-  float v;
-  asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
-  return v;
 }
 
 __device__ __forceinline__ uint4 ld_global_nc_v4(const void *p) {
