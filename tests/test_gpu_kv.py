@@ -151,3 +151,21 @@ def test_every_bf16_magnitude_as_row_max(native_lib, cuda_device):
     store_int8(x.to(cuda_device), cache, torch.arange(n, device=cuda_device))
     got = cache.view(-1, 528)[:n].cpu().numpy().view(np.uint8)
     assert np.array_equal(got, _c_rows(x))
+
+
+@pytest.mark.parametrize("n", [100, 3000])
+def test_non_power_of_two_block_size(native_lib, cuda_device, n):
+    """Blocks of 48 rows (the writer divides instead of shifting), on the
+    small-batch (n < 1024) and the streaming (n >= 1024) kernels, with skipped
+    slots: bytes bit-exact against the oracle, untouched rows stay zero."""
+    from kernels.titan_kv import store_int8
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(n, 512, generator=g).to(torch.bfloat16)
+    blocks = (n + 200) // 48 + 1
+    slots = torch.randperm(blocks * 48, generator=g)[:n]
+    slots[::17] = -1
+    cache = torch.zeros(blocks, 48, 528, dtype=torch.int8, device=cuda_device)
+    store_int8(x.to(cuda_device), cache, slots.to(cuda_device))
+    want = np.zeros((blocks, 48, 528), np.uint8)
+    O.store_int8(O.tensor_bf16_bits(x), want, slots.numpy())
+    assert np.array_equal(cache.cpu().numpy().view(np.uint8), want)
