@@ -702,6 +702,20 @@ def run_profile(args):
         q, idx = q.to(dev), idx.to(dev)
         for k in range(n):
             attn(q[k % 8], kv, idx[k % 8], SM_SCALE)
+    elif args.profile == "paged_b1":
+        from kernels.titan_index import triton_convert_req_index_to_global_index as conv
+        from kernels.titan_mla import triton_mla_sparse_attention_paged as attn_paged
+        g = torch.Generator().manual_seed(77)
+        bt = torch.randperm(KV_ROWS // 64, generator=g).to(torch.int32).view(1, -1).to(dev)
+        tok = torch.full((1, TOPK), -1, dtype=torch.int32)
+        tok[0, :VALID] = torch.randperm(KV_ROWS, generator=g)[:VALID].to(torch.int32)
+        tok = tok.to(dev)
+        req = torch.zeros(1, dtype=torch.int32, device=dev)
+        q1 = torch.randn(1, HEADS, 512, generator=g).to(torch.bfloat16).to(dev)
+        for _ in range(n):  # fused call, then conversion + reader
+            attn_paged(q1, kv, tok, req, bt, 64, SM_SCALE)
+            glob = conv(req, bt, tok, BLOCK_SIZE=64, NUM_TOPK_TOKENS=TOPK)
+            attn(q1, kv, glob.view(1, 1, TOPK), SM_SCALE)
     elif args.profile == "prefill":
         tp = 512
         ip = prefill_indices(tp, 4242, t0=1024).to(dev)
@@ -721,7 +735,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill"), default=None,
+    ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1"), default=None,
                     help="run only this workload (warmup + steps calls) as an ncu target; prints nothing")
     args = ap.parse_args()
     rank, world, local_rank = env_rank()
