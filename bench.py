@@ -309,8 +309,10 @@ class DecodeBench:
 
 class PagedBench:
     """Config 2 on a paged layout: the 262,144-row cache as 4096 blocks of 64
-    rows, one request per call with its own block table (a random block
-    permutation) and its own 2048 distinct request-local positions + 128 x -1.
+    rows and one request whose block table (a random block permutation) is
+    shared by all calls, as the layers of one decode step share it, while each
+    call has its own 2048 distinct request-local positions + 128 x -1 (the
+    per-layer indexer output).
     `fused` times triton_mla_sparse_attention_paged (the gather translates);
     otherwise the conversion kernel runs first and the reader reads its
     output, as the reference's backend does (integration/titan_backend.py:
@@ -325,7 +327,7 @@ class PagedBench:
         dev = kvs[0].device
         g = torch.Generator().manual_seed(seed)
         nb = KV_ROWS // self.BLOCK
-        self.bt = torch.stack([torch.randperm(nb, generator=g) for _ in range(calls)]).to(torch.int32).to(dev)
+        self.bt = torch.randperm(nb, generator=g).to(torch.int32).view(1, nb).to(dev)
         tok = torch.full((calls, 1, TOPK), -1, dtype=torch.int32)
         for j in range(calls):
             tok[j, 0, :VALID] = torch.randperm(KV_ROWS, generator=g)[:VALID].to(torch.int32)
@@ -336,7 +338,7 @@ class PagedBench:
         def run():
             for j in range(calls):
                 kv = kvs[j % len(kvs)]
-                bt = self.bt[j:j + 1]
+                bt = self.bt
                 if fused:
                     attn_paged(self.q[j], kv, self.tok[j], self.req, bt, self.BLOCK, SM_SCALE, sm_count=sms)
                 else:
