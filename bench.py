@@ -4,7 +4,11 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Headline (one JSON line on rank 0): BASELINE config 2 — B=1 decode, 16 heads,
+Workloads, numbered as in the benchmark configuration list of this path:
+1 = the CPU-sized B=1 case (4096-row cache), 2 = production B=1 decode,
+3 = B=8 decode, 4 = prefill-shaped T=4096, 5 = MoE route alignment B1..8.
+
+Headline (one JSON line on rank 0): config 2 — B=1 decode, 16 heads,
 262,144-row INT8 cache (1024 blocks x 256 x 528 B) filled by store_int8,
 2176 indices per token (2048 distinct valid + 128 x -1), sm_scale 512^-0.5.
 A step is one call of triton_mla_sparse_attention on one token's index set.
