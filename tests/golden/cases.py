@@ -66,7 +66,7 @@ class MlaCase:
 
 
 MLA_CASES = (
-    # seed 0, [4096, 512] latents, q [1, 16, 512],
+    # The CPU-sized B=1 case: seed 0, [4096, 512] latents, q [1, 16, 512],
     # 2176 indices uniform in [0, 4096) with the last 128 set to -1.
     MlaCase("c1", 0, 4096, 1, 16, 2176, "tail128", (1, 4, 8, 16, 32)),
     # tests/verify_mla.py:72-78 masking: tail 2048.. = -1, token 1 2000.. = -1,

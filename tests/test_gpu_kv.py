@@ -72,8 +72,9 @@ def test_block_strided_cache(native_lib, cuda_device):
 
 @pytest.mark.parametrize("order", ["arange", "permutation"])
 def test_full_cache_fill_bit_exact(native_lib, cuda_device, order):
-    """BASELINE config 2 fill (262,144 rows) and config 4's random-permutation
-    store, byte for byte against the C oracle, plus the reference test's
+    """The production cache fill (262,144 rows, slots in order) and the same
+    fill with a random slot permutation, byte for byte against the C oracle,
+    plus the reference test's
     quantisation criteria (tests/verify_mla.py:50-66)."""
     from kernels.titan_kv import store_int8
     n = 262144

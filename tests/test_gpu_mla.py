@@ -1,7 +1,7 @@
 # SPDX-License-Identifier: Apache-2.0
 """Sparse MLA on the GPU vs the CPU oracle and the reference-generated goldens.
 
-Tolerance: |out - ref| <= 2e-2 + 1e-2 |ref| elementwise,
+Tolerance of this path: |out - ref| <= 2e-2 + 1e-2 |ref| elementwise,
 ref = FP32 attention over the dequantised cache.  Plus the reference test's own
 criteria vs the original bf16 latents: NMSE < 1e-3, cosine > 0.999
 (tests/verify_mla.py:79-90), and exact zeros for a token with no valid index.
@@ -58,7 +58,7 @@ def test_golden_cases(case, native_lib, cuda_device):
 
 @pytest.fixture(scope="module")
 def big_cache(cuda_device):
-    """BASELINE config 2 cache: 262,144 rows written by store_int8."""
+    """The production B=1 cache: 262,144 rows written by store_int8."""
     n = 262144
     g = torch.Generator().manual_seed(1234)
     latent = torch.randn(n, 512, generator=g).to(torch.bfloat16)
@@ -104,7 +104,8 @@ def test_config3_b8(big_cache, native_lib, cuda_device):
 
 
 def test_prefill_shaped_slice(big_cache, native_lib, cuda_device):
-    """BASELINE config 4 index construction for a 192-token slice
+    """Prefill-shaped index construction (token t draws from min(t+1, 2176) +
+    65536 (t // 1024) candidates) for a 192-token slice
     (tokens t = 0..63, 1000..1063, 3000..3063), single pass."""
     from kernels.titan_mla import triton_mla_sparse_attention as attn
     latent, cache, rows = big_cache

@@ -109,7 +109,7 @@ def test_mla_oracle_vs_reference_golden(case, mla_golden):
     ref = O.mla_sparse_attention(inp["q"], rows, inp["indices"], case.sm_scale)
     for s in case.splits:
         gold = torch.from_numpy(O.bf16_bits_to_f32(mla_golden[f"{case.name}__s{s}"]).reshape(ref.shape))
-        # Path tolerance (BASELINE north star): |a - b| <= 2e-2 + 1e-2 |b|.
+        # Path tolerance: |a - b| <= 2e-2 + 1e-2 |b|.
         assert bool(((gold - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()), (case.name, s)
         if case.pattern == "all_neg":
             assert not gold.any()
