@@ -248,3 +248,33 @@ def test_large_single_pass(big_cache, native_lib, cuda_device, tokens, heads, to
     assert not out[3].any()
     from kernels import titan_native
     assert titan_native.device_error(out) == 0
+
+
+def test_concurrent_streams_use_separate_split_scratch(big_cache, native_lib, cuda_device):
+    """Split launches issued on two streams at once (no ordering between
+    them) each use their own stream's partials workspace and arrival
+    counters: results equal the same calls issued one after another."""
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    kv = cache.view(n, 1, 528)
+    g = torch.Generator().manual_seed(21)
+    qs = [torch.randn(1, 16, 512, generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(8)]
+    ids = [torch.randint(0, n, (1, 1, 2176), generator=g, dtype=torch.int32).to(cuda_device) for _ in range(8)]
+    want = [attn(qs[k], kv, ids[k], 512 ** -0.5, num_kv_splits=80) for k in range(8)]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for s in streams:
+        s.wait_stream(torch.cuda.current_stream())
+    got = [None] * 8
+    for rep in range(4):
+        for k in range(8):
+            with torch.cuda.stream(streams[k % 2]):
+                got[k] = attn(qs[k], kv, ids[k], 512 ** -0.5, num_kv_splits=80)
+        for s in streams:
+            torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        for k in range(8):
+            assert torch.equal(got[k], want[k]), (rep, k)
+    from kernels import titan_native
+    assert titan_native.device_error(qs[0]) == 0
