@@ -74,19 +74,22 @@ def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int
     return max(1, num_kv_splits)
 
 
-# Cost model of the B200 kernel, fitted to back-to-back B=1/2/4/8 sweeps of
-# every split count on B200 (microseconds): 32-row tiles per CTA, the merge
-# inside a thread-block cluster, the merge across clusters (done by the last
-# CTA to finish when NC <= C, else by the combine kernel plus a per-partial
-# term), and a penalty when more clusters are launched than fit with one CTA
-# per SM (they then share SMs and slow each other's gathers).
+# Cost model of the B200 kernel (microseconds): 32-row tiles per CTA, the
+# merge inside a thread-block cluster, the merge across clusters (done by the
+# last CTA to finish when NC <= C, else by the combine kernel plus a
+# per-partial term), and a penalty when more clusters are launched than fit
+# with one CTA per SM (they then share SMs and slow each other's gathers).
+# Fitted to a B200 sweep of every split count with at most one CTA per SM for
+# B = 1..8 (calls back to back in CUDA graphs, cold L2): the median of the
+# parameter sets whose picks lose the least against the best measured split
+# count (0.25 us summed over the eight batch sizes).
 _TILE_ROWS = 32
-_COST_TILE_US = 1.25
-_COST_CLUSTER_MERGE_US = 1.2
-_COST_SPLIT_MERGE_US = 1.2
-_COST_COMBINE_US = 1.4
+_COST_TILE_US = 0.75
+_COST_CLUSTER_MERGE_US = 0.8
+_COST_SPLIT_MERGE_US = 0.6
+_COST_COMBINE_US = 1.0
 _COST_COMBINE_PER_PARTIAL_US = 0.05
-_COST_SHARED_SM_US = 2.0
+_COST_SHARED_SM_US = 1.5
 _MAX_CLUSTER = 16
 _CLUSTER_SIZES = (1, 2, 4, 8, 16)
 _cluster_tables_cache = {}
