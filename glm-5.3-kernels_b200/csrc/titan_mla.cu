@@ -45,6 +45,7 @@ constexpr int kRedStride = 40;              // floats per head row of a warp's p
 constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (bf16, 32 rows + pad)
 constexpr int kMaxCluster = 16;
 constexpr int kRing = 3;                    // row-gather ring: tiles in flight ahead of the math + 1
+constexpr int kIdxRing = 8;                 // index ring: indices are staged five tiles ahead
 constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -57,6 +58,7 @@ struct Smem {
     struct {
       uint4 rows[kRing][kWarps][4][32];    // tile loop: lane's four 16-byte row pieces per stage
       float scale[kRing][kBN];             // row scales of the stage's tile, n-order
+      int32_t idx[kIdxRing][kBN];          // row indices of tile j in slot j % kIdxRing (non-paged)
     } ring;                                // (dead before the merge stages its accumulator)
   } u;
   float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
@@ -245,9 +247,29 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     cp_async_commit();
   };
 
-  // Tiles 0 and 1 in flight; r_a / r_b hold the rows of tiles 2 and 3 and,
-  // when paged, t_c the request-local positions of tile 4 (positions are
-  // fetched three tiles ahead and translated two tiles ahead).
+  // Non-paged: warp 0 stages the 32 indices of tile j into slot j % 8 with
+  // 4-byte cp.async five tiles ahead of the row gather (they ride in that
+  // iteration's commit group, so the per-tile wait and barriers publish them);
+  // every thread reads its four from shared memory when it issues the tile's
+  // rows: no register hand-over of a pending load.
+  auto copy_idx = [&](int j) {
+    if (warp == 0 && j < n_tiles) {
+      const int64_t pos = start + (int64_t)j * kBN + lane;
+      int32_t *dst = &sm.u.ring.idx[j % kIdxRing][lane];
+      if (pos < end)
+        cp_async_4_zfill(dst, idx_row + pos, 4u);
+      else
+        *dst = -1;
+    }
+  };
+  auto read_idx = [&](int j, int (&r)[4]) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) r[nt] = j < n_tiles ? sm.u.ring.idx[j % kIdxRing][nt * 8 + g] : -1;
+  };
+
+  // Tiles 0 and 1 in flight.  Paged: r_a / r_b hold the rows of tiles 2 and
+  // 3 and t_c the request-local positions of tile 4 (positions are fetched
+  // three tiles ahead and translated two tiles ahead).
   int r_a[4], r_b[4];
   int t_c[4];
   {
@@ -266,14 +288,15 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
       translate(x2, r_a);
       translate(x3, r_b);
     } else {
-      load_idx(0, r0);
-      load_idx(1, r_a);
-      load_idx(2, r_b);
+#pragma unroll 1
+      for (int j = 0; j < 5; ++j) copy_idx(j);
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+      read_idx(0, r0);
       issue(0, 0, r0);
-      issue(1, 1, r_a);
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
-      load_idx(3, r_b);
+      read_idx(1, r0);
+      issue(1, 1, r0);
     }
   }
 
@@ -320,14 +343,17 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   for (int i = 0; i < n_tiles; ++i) {
     // Tile i + 2 goes in flight, tile i + 4's indices are fetched, and tile
     // i's pieces (this lane's own copies) are waited for.
-    issue(i + 2, st_issue, r_a);
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
     if constexpr (kPaged) {
+      issue(i + 2, st_issue, r_a);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
       translate(t_c, r_b);
       load_idx(i + 5, t_c);
     } else {
-      load_idx(i + 4, r_b);
+      copy_idx(i + 5);  // committed with tile i + 2's rows; read at iteration i + 3
+      int r2[4];
+      read_idx(i + 2, r2);
+      issue(i + 2, st_issue, r2);
     }
     cp_async_wait<2>();
     uint4 kb_cur[4];
