@@ -45,7 +45,7 @@ constexpr int kRedStride = 40;              // floats per head row of a warp's p
 constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (bf16, 32 rows + pad)
 constexpr int kMaxCluster = 16;
 constexpr int kRing = 3;                    // row-gather ring: tiles in flight ahead of the math + 1
-constexpr int kIdxRing = 8;                 // index ring: indices are staged five tiles ahead
+constexpr int kIdxRing = 8;                 // index ring: indices are staged up to eight tiles ahead
 constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -58,7 +58,8 @@ struct Smem {
     struct {
       uint4 rows[kRing][kWarps][4][32];    // tile loop: lane's four 16-byte row pieces per stage
       float scale[kRing][kBN];             // row scales of the stage's tile, n-order
-      int32_t idx[kIdxRing][kBN];          // row indices of tile j in slot j % kIdxRing (non-paged)
+      int32_t idx[kIdxRing][kBN];          // row indices (paged: request-local positions) of tile j, slot j % kIdxRing
+      int32_t base[kIdxRing][kBN];         // paged: block-table entry of each position of tile j
     } ring;                                // (dead before the merge stages its accumulator)
   } u;
   float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
@@ -191,36 +192,12 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   const uint8_t *kv_lane = p.kv + warp * 64 + c * 16;  // this lane's 16-byte column of a row
   const int64_t seq_kv = p.seq_kv;
 
-  // Row indices of tile j for this lane: n-tile nt, n-order row g.
-  auto load_idx = [&](int j, int (&r)[4]) {
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int64_t pos = start + (int64_t)j * kBN + nt * 8 + g;
-      r[nt] = (j < n_tiles && pos < end) ? __ldg(idx_row + pos) : -1;
-    }
-  };
   auto row_ok = [&](int r) { return r >= 0 && (int64_t)r < seq_kv; };
-  // Paged: the request's block-table row, and the translation of a tile's
-  // request-local positions to cache rows (a negative position, a block past
-  // the table or a row outside int32 gives -1; the gather masks rows outside
-  // [0, seq_kv) as for any index).  Same mapping as the standalone
-  // titan_convert_req_index_to_global.
-  // The request id is only consumed inside translate (a select, no branch),
-  // so its load and the first position loads are in flight together.
+  // Paged: the request of this token (positions of an unknown request, a
+  // negative position or a block past the table give row -1; the gather masks
+  // rows outside [0, seq_kv) as for any index).  Same mapping as the
+  // standalone titan_convert_req_index_to_global.
   const int req = kPaged ? __ldg(p.req_id + t) : 0;
-  auto translate = [&](const int (&tok)[4], int (&r)[4]) {
-    const bool req_ok = req >= 0 && req < p.num_reqs;
-    const int32_t *bt_row = p.block_table + (int64_t)(req_ok ? req : 0) * p.bt_st0;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int x = tok[nt];
-      const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
-      const bool ok = req_ok && x >= 0 && blk < p.max_blocks;
-      const int64_t base = ok ? (int64_t)__ldg(bt_row + (int64_t)blk * p.bt_st1) : 0;
-      const int64_t row = base * p.block_stride_rows + (x - blk * p.block_size);
-      r[nt] = (ok && row >= 0 && row <= 0x7fffffffLL) ? (int)row : -1;
-    }
-  };
   // Gather of tile j into ring stage st, asynchronously (cp.async): each lane
   // copies its own four 16-byte row pieces (its MMA B fragments), zero-filled
   // for masked rows, which are never read; the scale loaders fetch the row
@@ -247,9 +224,41 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     cp_async_commit();
   };
 
-  // Non-paged: warp 0 stages the 32 indices of tile j into slot j % 8 with
-  // 4-byte cp.async five tiles ahead of the row gather (they ride in that
-  // iteration's commit group, so the per-tile wait and barriers publish them);
+  // Paged: warp 0 also stages the block-table entries of tile j's positions
+  // (4-byte cp.async, reading the positions from the index ring), three
+  // tiles after the positions and three before the rows; rows are formed
+  // from both rings when the tile is issued.
+  const bool req_ok = req >= 0 && req < p.num_reqs;
+  const int32_t *bt_req = p.block_table + (int64_t)(req_ok ? req : 0) * p.bt_st0;
+  auto copy_base = [&](int j) {
+    if (warp == 0 && j < n_tiles) {
+      const int x = sm.u.ring.idx[j % kIdxRing][lane];
+      const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
+      if (req_ok && x >= 0 && blk < p.max_blocks)
+        cp_async_4_zfill(&sm.u.ring.base[j % kIdxRing][lane], bt_req + (int64_t)blk * p.bt_st1, 4u);
+    }
+  };
+  auto read_rows_paged = [&](int j, int (&r)[4]) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      int row = -1;
+      if (j < n_tiles) {
+        const int x = sm.u.ring.idx[j % kIdxRing][nt * 8 + g];
+        const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
+        if (req_ok && x >= 0 && blk < p.max_blocks) {
+          const int64_t v =
+              (int64_t)sm.u.ring.base[j % kIdxRing][nt * 8 + g] * p.block_stride_rows + (x - blk * p.block_size);
+          row = (v >= 0 && v <= 0x7fffffffLL) ? (int)v : -1;
+        }
+      }
+      r[nt] = row;
+    }
+  };
+
+  // Warp 0 stages the 32 indices (paged: positions) of tile j into slot j % 8
+  // with 4-byte cp.async five (paged: eight) tiles ahead of the row gather
+  // (they ride in that iteration's commit group, so the per-tile wait and
+  // barriers publish them; a slot is read three iterations after its copy);
   // every thread reads its four from shared memory when it issues the tile's
   // rows: no register hand-over of a pending load.
   auto copy_idx = [&](int j) {
@@ -267,26 +276,26 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     for (int nt = 0; nt < 4; ++nt) r[nt] = j < n_tiles ? sm.u.ring.idx[j % kIdxRing][nt * 8 + g] : -1;
   };
 
-  // Tiles 0 and 1 in flight.  Paged: r_a / r_b hold the rows of tiles 2 and
-  // 3 and t_c the request-local positions of tile 4 (positions are fetched
-  // three tiles ahead and translated two tiles ahead).
-  int r_a[4], r_b[4];
-  int t_c[4];
+  // Tiles 0 and 1 in flight; the index ring holds tiles 2..4 (paged:
+  // positions of tiles 2..7 and block-table entries of tiles 2..4).
   {
     int r0[4];
     if constexpr (kPaged) {
-      int x0[4], x1[4], x2[4], x3[4];
-      load_idx(0, x0);
-      load_idx(1, x1);
-      load_idx(2, x2);
-      load_idx(3, x3);
-      load_idx(4, t_c);
-      translate(x0, r0);
-      translate(x1, r_a);
+#pragma unroll 1
+      for (int j = 0; j < 8; ++j) copy_idx(j);  // positions of tiles 0..7
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+#pragma unroll 1
+      for (int j = 0; j < 5; ++j) copy_base(j);  // their block-table entries, tiles 0..4
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+      read_rows_paged(0, r0);
       issue(0, 0, r0);
-      issue(1, 1, r_a);
-      translate(x2, r_a);
-      translate(x3, r_b);
+      read_rows_paged(1, r0);
+      issue(1, 1, r0);
+      __syncthreads();  // slots 0 and 1 are refilled from the first iteration on
     } else {
 #pragma unroll 1
       for (int j = 0; j < 5; ++j) copy_idx(j);
@@ -341,14 +350,14 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
 
   int st = 0, st_issue = 2;  // ring stage of tile i and of tile i + 2
   for (int i = 0; i < n_tiles; ++i) {
-    // Tile i + 2 goes in flight, tile i + 4's indices are fetched, and tile
+    // Tile i + 2 goes in flight, later tiles' indices are staged, and tile
     // i's pieces (this lane's own copies) are waited for.
     if constexpr (kPaged) {
-      issue(i + 2, st_issue, r_a);
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) r_a[nt] = r_b[nt];
-      translate(t_c, r_b);
-      load_idx(i + 5, t_c);
+      copy_idx(i + 8);   // positions, eight tiles ahead
+      copy_base(i + 5);  // block-table entries, five tiles ahead
+      int r2[4];
+      read_rows_paged(i + 2, r2);
+      issue(i + 2, st_issue, r2);
     } else {
       copy_idx(i + 5);  // committed with tile i + 2's rows; read at iteration i + 3
       int r2[4];
