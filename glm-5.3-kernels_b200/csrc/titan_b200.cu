@@ -5,3 +5,4 @@
 #include "titan_moe_align.cu"
 #include "titan_mla.cu"
 #include "titan_index.cu"
+#include "titan_io.cu"

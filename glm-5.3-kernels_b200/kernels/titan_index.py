@@ -55,9 +55,9 @@ def triton_convert_req_index_to_global_index(
     ti = token_indices if token_indices.stride(1) == 1 else token_indices.contiguous()
     req = req_id if req_id.is_contiguous() else req_id.contiguous()
     out = torch.empty((num_tokens, NUM_TOPK_TOKENS), dtype=torch.int32, device=token_indices.device)
-    lib = _native.load()
+    lib = _native.entry()
     with _native.on_device(token_indices.device):
-        rc = lib.titan_convert_req_index_to_global(
+        rc = lib.convert(
             req.data_ptr(), block_table.shape[0], block_table.data_ptr(), block_table.stride(0),
             block_table.stride(1), block_table.shape[1], ti.data_ptr(), ti.stride(0), NUM_TOPK_TOKENS,
             out.data_ptr(), out.stride(0), num_tokens, int(BLOCK_SIZE), int(stride_rows),

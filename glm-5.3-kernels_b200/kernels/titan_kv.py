@@ -42,9 +42,9 @@ def store_int8(x, cache, slots):
     if slots.dtype not in (torch.int32, torch.int64):
         slots = slots.to(torch.int64)
     cache8 = cache.view(torch.int8)
-    lib = _native.load()
+    lib = _native.entry()
     with _native.on_device(x.device):
-        rc = lib.titan_store_int8(
+        rc = lib.store_int8(
             x.data_ptr(), x.stride(0), cache8.data_ptr(), cache8.shape[0], cache8.shape[1],
             cache8.stride(0), cache8.stride(1), slots.data_ptr(), 1 if slots.dtype == torch.int64 else 0,
             n, _native.stream_of(x))

@@ -12,6 +12,7 @@ last CTA to finish (arrival counters).
 528 bytes/token: 512 signed INT8 values followed by 1 FP32 scale + 12 zero bytes.
 """
 
+import ctypes
 import functools
 
 import torch
@@ -209,6 +210,24 @@ def _plan(dev, num_tokens, num_heads_q, index_topk, num_kv_splits, sm_count):
     return plan
 
 
+def _destination(out, dev, shape):
+    """Device-accessible address of a caller-provided output: a CUDA tensor on
+    `dev`, or pinned host memory through its device mapping."""
+    assert tuple(out.shape) == shape and out.dtype == torch.bfloat16, \
+        f"out must be bf16 {list(shape)}, got {out.dtype} {list(out.shape)}"
+    st = out.stride()
+    assert st[2] == 1 and out.data_ptr() % 16 == 0 and (st[0] * 2) % 16 == 0 and (st[1] * 2) % 16 == 0, \
+        "out needs a contiguous last dim and 16-byte aligned rows"
+    if out.is_cuda:
+        assert out.get_device() == dev, "out must be on q's device"
+        return out.data_ptr()
+    assert out.is_pinned(), "a host `out` must be pinned memory (tensor.pin_memory())"
+    ptr = ctypes.c_void_p()
+    _native.check(_native.load().titan_device_pointer(out.data_ptr(), ctypes.byref(ptr)),
+                  "triton_mla_sparse_attention(out=)")
+    return ptr.value
+
+
 def triton_mla_sparse_attention(
     q: torch.Tensor,
     kv: torch.Tensor,
@@ -216,6 +235,8 @@ def triton_mla_sparse_attention(
     sm_scale: float,
     num_kv_splits: int | None = None,
     sm_count: int | None = None,
+    *,
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Sparse MLA attention over top-k indices.
 
@@ -227,9 +248,15 @@ def triton_mla_sparse_attention(
         num_kv_splits: override the auto-heuristic; None/0 = auto (the B200 policy,
                    `_choose_kv_splits_b200`), 1 = single pass.
         sm_count:  cached device SM count for the split heuristic.
+        out:       optional (keyword only; not in the reference signature)
+                   [num_tokens, num_heads_q, 512] bf16 destination: a CUDA
+                   tensor on q's device or a PINNED host tensor, which the
+                   kernel writes through its device mapping (no separate
+                   device -> host copy).  Last dim contiguous, 16-byte aligned
+                   rows.
 
     Returns:
-        out:   [num_tokens, num_heads_q, 512] bf16 (a new tensor)
+        out:   [num_tokens, num_heads_q, 512] bf16 (a new tensor unless `out` is given)
     """
     num_tokens, num_heads_q, dim_qk = q.shape
     # Shape contract of kernels/titan_mla.py:478-488.
@@ -256,7 +283,11 @@ def triton_mla_sparse_attention(
 
     num_kv_splits, ws_bytes, sem_count = _plan(dev, num_tokens, num_heads_q, index_topk, num_kv_splits,
                                                sm_count)
-    out = q.new_empty((num_tokens, num_heads_q, _BLOCK_DV))
+    if out is None:
+        out = q.new_empty((num_tokens, num_heads_q, _BLOCK_DV))
+        out_ptr = out.data_ptr()
+    else:
+        out_ptr = _destination(out, dev, (num_tokens, num_heads_q, _BLOCK_DV))
     if num_tokens == 0:
         return out
 
@@ -275,7 +306,7 @@ def triton_mla_sparse_attention(
         idx_st = idx.stride()
     out_st = out.stride()
 
-    lib = _native.load()
+    lib = _native.entry()
     stream = torch._C._cuda_getCurrentRawStream(dev)
     prev = torch.cuda.current_device()
     if prev != dev:
@@ -283,16 +314,15 @@ def triton_mla_sparse_attention(
     try:
         # indices[:, 0, :] is row t at idx + t * stride(0): no view is needed.
         args = (q.data_ptr(), q_st[0], q_st[1], kv.data_ptr(), kv.stride(0), seq_kv,
-                idx.data_ptr(), idx_st[0], index_topk, out.data_ptr(), out_st[0], out_st[1],
+                idx.data_ptr(), idx_st[0], index_topk, out_ptr, out_st[0], out_st[1],
                 num_tokens, num_heads_q, float(sm_scale), num_kv_splits)
         if ws_bytes > 0:
             # Split launch: partials of a token's clusters are merged by the
             # last CTA to finish (arrival counters), or by a combine kernel.
             sem, ws = _split_scratch(q, dev, stream, ws_bytes, sem_count)
-            rc = lib.titan_mla_sparse_attention_sem(*args, ws.data_ptr(), ws.numel(), sem.data_ptr(),
-                                                    sem.numel(), stream)
+            rc = lib.mla_sem(*args, ws.data_ptr(), ws.numel(), sem.data_ptr(), sem.numel(), stream)
         else:
-            rc = lib.titan_mla_sparse_attention(*args, None, 0, stream)
+            rc = lib.mla(*args, None, 0, stream)
     finally:
         if prev != dev:
             torch.cuda.set_device(prev)
@@ -369,11 +399,11 @@ def triton_mla_sparse_attention_paged(
     bt_st = block_table.stride()
     out_st = out.stride()
 
-    lib = _native.load()
+    lib = _native.entry()
     stream = torch._C._cuda_getCurrentRawStream(dev)
     with _native.on_device(q.device):
         sem, ws = _split_scratch(q, dev, stream, ws_bytes, sem_count) if ws_bytes > 0 else (None, None)
-        rc = lib.titan_mla_sparse_attention_paged(
+        rc = lib.mla_paged(
             q.data_ptr(), q_st[0], q_st[1], kv.data_ptr(), kv.stride(0), kv.shape[0],
             ti.data_ptr(), ti.stride(0), index_topk,
             req.data_ptr(), block_table.shape[0], block_table.data_ptr(), bt_st[0], bt_st[1], block_table.shape[1],

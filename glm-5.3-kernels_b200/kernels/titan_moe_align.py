@@ -49,9 +49,9 @@ def titan_moe_align_small(
         num_warps = 1 if routes <= 16 else 4
     if num_warps not in (1, 2, 4):
         raise ValueError('Candidate warp counts are 1, 2, or 4')
-    lib = _native.load()
+    lib = _native.entry()
     with _native.on_device(topk_ids.device):
-        rc = lib.titan_moe_align_small(
+        rc = lib.moe_align(
             topk_ids.data_ptr(), 1 if topk_ids.dtype == torch.int64 else 0, routes,
             sorted_ids.data_ptr(), expert_ids.data_ptr(), postpad.data_ptr(), num_warps,
             _native.stream_of(topk_ids))

@@ -1,14 +1,23 @@
 # SPDX-License-Identifier: Apache-2.0
-"""ctypes binding of libtitan_b200.so, the C ABI declared in include/titan_b200.h.
+"""Binding of libtitan_b200.so, the C ABI declared in include/titan_b200.h.
 
-The library is loaded lazily on the first kernel call, so importing the
-titan_* modules touches neither the library nor CUDA (the reference's import
-contract, tests/test_cpu_contracts.py:33-53).  There is no fallback: a missing
-library or a failed launch raises.
+The library is loaded lazily (ctypes) on the first kernel call, so importing
+the titan_* modules touches neither the library nor CUDA (the reference's
+import contract, tests/test_cpu_contracts.py:33-53).  The hot launchers are
+then called through `entry()`: the CPython fast-call module _titan_pybind
+(lib/, built with the library) bound to the entry points of the loaded
+library — ctypes' per-argument conversion costs ~3.7 us for the MLA launcher,
+more than the decode kernel's own host launch.  When that module is absent the
+same entry points are called through ctypes.  There is no compute fallback: a
+missing library or a failed launch raises.
 """
 import ctypes
+import importlib.machinery
+import importlib.util
 import os
+import sysconfig
 import threading
+import types
 from pathlib import Path
 
 _PKG_ROOT = Path(__file__).resolve().parent.parent
@@ -16,6 +25,18 @@ _DEFAULT_LIB = _PKG_ROOT / "lib" / "libtitan_b200.so"
 
 _lock = threading.Lock()
 _lib = None
+_entry = None
+
+# entry() name -> C entry point
+_HOT = {
+    "mla": "titan_mla_sparse_attention",
+    "mla_sem": "titan_mla_sparse_attention_sem",
+    "mla_paged": "titan_mla_sparse_attention_paged",
+    "copy": "titan_copy",
+    "store_int8": "titan_store_int8",
+    "moe_align": "titan_moe_align_small",
+    "convert": "titan_convert_req_index_to_global",
+}
 
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -55,6 +76,8 @@ SIGNATURES = {
     ),
     "titan_moe_align_small": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _int, _vp]),
     "titan_device_error": (_int, [ctypes.POINTER(_int), _int, _vp]),
+    "titan_copy": (_int, [_vp, _vp, _i64, _vp]),
+    "titan_device_pointer": (_int, [_vp, ctypes.POINTER(_vp)]),
 }
 
 
@@ -85,6 +108,35 @@ def load():
                 fn.argtypes = argtypes
             _lib = lib
     return _lib
+
+
+def _load_pybind(lib):
+    """_titan_pybind from the library's directory, bound to `lib`, or None."""
+    path = library_path().parent / ("_titan_pybind" + sysconfig.get_config_var("EXT_SUFFIX"))
+    if not path.exists():
+        return None
+    loader = importlib.machinery.ExtensionFileLoader("_titan_pybind", str(path))
+    spec = importlib.util.spec_from_file_location("_titan_pybind", str(path), loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    mod.bind(*(ctypes.cast(getattr(lib, c_name), ctypes.c_void_p).value for c_name in _HOT.values()))
+    return mod
+
+
+def entry():
+    """The hot launchers (`mla`, `mla_sem`, `mla_paged`, `copy`, `store_int8`,
+    `moe_align`, `convert`), positional arguments as in include/titan_b200.h,
+    returning the status: the fast-call module, else the ctypes functions."""
+    global _entry
+    if _entry is not None:
+        return _entry
+    lib = load()
+    with _lock:
+        if _entry is None:
+            fast = None if os.environ.get("TITAN_B200_CTYPES_ONLY") else _load_pybind(lib)
+            _entry = fast if fast is not None else types.SimpleNamespace(
+                **{name: getattr(lib, c_name) for name, c_name in _HOT.items()})
+    return _entry
 
 
 def check(status, what):

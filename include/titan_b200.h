@@ -238,6 +238,25 @@ int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int64_t num_ro
                           int num_warps, titan_stream_t stream);
 
 /*
+ * Host <-> device staging (no counterpart in the reference, whose callers keep
+ * every operand on the GPU).  titan_copy moves `bytes` from src to dst with a
+ * kernel launched on `stream` (ordered after the stream's previous kernel, as
+ * a programmatic dependent); either side may be device memory or PINNED host
+ * memory (cudaHostAlloc / cudaMallocHost / torch pin_memory), which the kernel
+ * reads or writes through its device mapping: one PCIe round trip instead of
+ * a copy engine's fixed latency, for the small per-call transfers of decode.
+ * Pageable host memory and overlapping buffers are rejected
+ * (TITAN_ERR_INVALID_ARGUMENT).
+ *
+ * titan_device_pointer returns the device-accessible address of `ptr` (the
+ * device mapping of pinned host memory; device memory unchanged), e.g. to
+ * hand a pinned host buffer to titan_mla_sparse_attention as `out` so the
+ * reader stores its result straight into host memory.
+ */
+int titan_copy(void *dst, const void *src, int64_t bytes, titan_stream_t stream);
+int titan_device_pointer(const void *ptr, void **device_ptr_out);
+
+/*
  * Device-side error word: kernels set it instead of trapping when a bounded
  * wait gives up.  Reads (and, if clear_after is non-zero, resets) the word of
  * the current device; synchronises the stream first.  0 = no error.

@@ -49,3 +49,27 @@ def test_invalid_arguments_rejected_on_host(native_lib):
     rc = native_lib.titan_store_int8(None, 512, None, 1, 256, 0, 0, None, 1, -1, None)
     assert rc == 1
     assert native_lib.titan_store_int8(None, 512, None, 1, 256, 0, 0, None, 1, 0, None) == 0  # nothing to do
+
+
+def test_fast_call_binding_is_built_and_bound(native_lib):
+    """The hot launchers go through the CPython fast-call module (bound to the
+    loaded library), which validates argument count and types before calling."""
+    import pytest
+    from kernels import titan_native
+    e = titan_native.entry()
+    assert type(e).__name__ == "module" and e.__name__ == "_titan_pybind"
+    for name in titan_native._HOT:
+        assert callable(getattr(e, name))
+    # Same host-side validation as through ctypes: status 1, nothing launched.
+    assert e.moe_align(None, 0, 7, None, None, None, 1, None) == 1
+    assert b"num_routes" in native_lib.titan_last_error()
+    assert e.mla(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, 1, 16, 0.1, 0, None, 0, None) == 1
+    assert e.store_int8(None, 512, None, 1, 256, 0, 0, None, 1, 0, None) == 0
+    assert e.copy(None, None, 0, None) == 0
+    assert e.copy(None, None, 16, None) == 1 and b"null" in native_lib.titan_last_error()
+    with pytest.raises(TypeError):
+        e.mla_sem(*([0] * 20))                   # one argument short
+    with pytest.raises(TypeError):
+        e.copy(0, 0, 1.5, 0)                     # float where an int64 belongs
+    with pytest.raises(TypeError):
+        e.store_int8("x", 512, None, 1, 256, 0, 0, None, 1, 0, None)
