@@ -210,6 +210,19 @@ __device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, const void 
       "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
       : "memory");
 }
+// TMA gather of four rows of a 2-D tensor map (box one row high): rows r0..r3
+// at column x land back to back at dst (128-byte aligned), completing in bytes
+// on `bar`.  Rows outside the map read as zeros.  x * element size must be a
+// multiple of 16 bytes.
+__device__ __forceinline__ void tma_gather4(void *dst, const void *tmap, int x, int r0, int r1, int r2, int r3,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 

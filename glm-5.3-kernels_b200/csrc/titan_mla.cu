@@ -11,12 +11,18 @@
 //   :357-429 combine: sum_s exp(lse_s - M) o_s / sum_s exp(lse_s - M), bf16
 //
 // B200 design: one CTA (8 warps) per (token, split, 16-head group).
-//  * Gather straight into registers: every 528-byte row is read once, so it is
-//    not staged in shared memory.  Warp w owns latent dims [64 w, 64 w + 64);
-//    lane (g, c) of the warp loads 16 bytes of row (8 nt + g) at byte
-//    64 w + 16 c for each of the tile's four 8-row n-tiles: exactly its MMA
-//    B fragments.  Loads run one tile ahead of the math (indices two tiles
-//    ahead); masked rows are never read.
+//  * Row gather by the tensor memory accelerator: per 32-row tile, warp 0
+//    issues eight `cp.async.bulk.tensor ... tile::gather4` loads (four rows
+//    each, by row index, 544-byte boxes) into a three-stage shared-memory
+//    ring, two tiles ahead of the math, completing on the stage's mbarrier.
+//    Rows outside [0, seq_kv) read as zeros (TMA bounds fill); a group whose
+//    four rows are all masked is not issued.  The row scale arrives with the
+//    row (bytes 512..515).  Warp w owns latent dims [64 w, 64 w + 64); lane
+//    (g, c) reads 16 bytes of each of its four rows at byte 64 w + 16 c:
+//    exactly its MMA B fragments, bank-conflict free in the 544-byte pitch.
+//    The indices reach shared memory through warp 0's 4-byte cp.async ring
+//    five tiles ahead (paged: positions eight and block-table entries five
+//    tiles ahead), so no thread waits on a load issued one tile earlier.
 //  * QK: mma.sync m16n8k16 bf16 (A = 16 heads x 16 dims of q in registers).
 //    The k dimension is permuted identically for q and k so that each lane's
 //    16 contiguous bytes feed four k-steps.  The 8 warps' partial scores meet
@@ -31,6 +37,8 @@
 //    given arrival counters, the last CTA of each rank to finish merges that
 //    rank's slice over all partials (no second kernel), otherwise a combine
 //    kernel, launched as a programmatic dependent, merges them.
+#include <cuda.h>  // CUtensorMap
+
 #include "titan_common.cuh"
 
 namespace titan {
@@ -46,6 +54,9 @@ constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (b
 constexpr int kMaxCluster = 16;
 constexpr int kRing = 3;                    // row-gather ring: tiles in flight ahead of the math + 1
 constexpr int kIdxRing = 8;                 // index ring: indices are staged up to eight tiles ahead
+constexpr int kRowPitch = 544;              // gathered row in shared memory: 528 B + 16 B of bounds fill
+constexpr int kGroupBytes = 4 * kRowPitch;  // one gather4 load: 2176 B, a multiple of 128
+constexpr int kGroups = kBN / 4;            // gather4 loads per tile
 constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -53,24 +64,29 @@ struct Smem {
   float red[kWarps][kHeads * kRedStride];  // partial scores of each warp
   uint32_t p[kHeads * kPStrideWords];      // bf16(p * scale), n-order
   float rcv[kHeads * kD];                  // cluster merge: [C][16][512/C] slices pushed by the peers
-  union {
+  union alignas(128) {
     float stage[kHeads * kD];              // cluster merge: this CTA's acc as [owner][16][512/C]
     struct {
-      uint4 rows[kRing][kWarps][4][32];    // tile loop: lane's four 16-byte row pieces per stage
-      float scale[kRing][kBN];             // row scales of the stage's tile, n-order
+      uint8_t rows[kRing][kGroups][kGroupBytes];  // tile loop: stage = 8 gather4 groups of 4 rows
       int32_t idx[kIdxRing][kBN];          // row indices (paged: request-local positions) of tile j, slot j % kIdxRing
       int32_t base[kIdxRing][kBN];         // paged: block-table entry of each position of tile j
     } ring;                                // (dead before the merge stages its accumulator)
   } u;
   float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
-  uint32_t vword[kRing][4];                // per stage and n-tile: bit 4n = row n valid
+  alignas(8) uint8_t vbits[kRing][kGroups];  // per stage and gather4 group: bit k = slot k valid
   float alpha[kHeads];
   float2 ml[kHeads];                       // final (m, l) of this CTA
   float cw[kMaxCluster][kHeads];           // cluster merge weights
   float cM[kHeads], cL[kHeads];
   alignas(8) uint64_t merge_bar;           // counts the bytes the cluster pushes here
+  uint64_t row_bar[kRing];                 // per ring stage: one arrival per warp + its gather4 bytes
   int last;                                // this CTA arrived last at its cross-cluster counter
 };
+
+// Two CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
+static_assert(2 * (sizeof(Smem) + 1024) <= 228 * 1024, "the reader must fit twice per SM");
+static_assert(kGroups == kWarps, "warp w issues gather4 group w");
+static_assert(offsetof(Smem, u) % 128 == 0 && kGroupBytes % 128 == 0, "gather4 destinations are 128-byte aligned");
 
 struct Params {
   const __nv_bfloat16 *q;
@@ -99,10 +115,6 @@ struct Params {
   int num_reqs, max_blocks, block_size, block_shift;  // block_shift >= 0: block_size is 2^block_shift
   int64_t block_stride_rows;
 };
-
-__device__ __forceinline__ int pick4(const int (&v)[4], int i) {
-  return i == 0 ? v[0] : i == 1 ? v[1] : i == 2 ? v[2] : v[3];
-}
 
 // Last-arriver merge of the NC <= C cluster partials of (token t, head group
 // hg) over the dims of cluster rank `rank` (D = 512 / C = 32 kPer dims), same
@@ -156,7 +168,8 @@ __device__ __forceinline__ void merge_cluster_partials(const Params &p, int t, i
 }
 
 template <bool kPartialOut, bool kPaged>
-__global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, 2)
+    sparse_mla_kernel(const Params p, const __grid_constant__ CUtensorMap rows_map) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
 
@@ -172,24 +185,24 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   // has completed and flushed.
   pdl_wait_primary();
   pdl_launch_dependents();  // the combine (or the next call) may become resident now
-  // Cluster peers must be running, with their merge barrier initialised,
-  // before anyone writes into their shared memory: initialise, publish to the
-  // cluster, arrive now, wait right before the first remote store.
-  if (p.C > 1) {
-    if (tid == 0) {
-      mbar_init(&sm.merge_bar, 1);
-      fence_mbar_init();
-    }
-    __syncthreads();
-    cluster_arrive_relaxed();
+  // Ring-stage barriers (one arrival per warp, plus the gather bytes, per
+  // use) and, for clusters, the merge barrier.  Cluster peers must be
+  // running, with their merge barrier initialised, before anyone writes into
+  // their shared memory: initialise, publish to the cluster, arrive now, wait
+  // right before the first remote store.
+  if (tid == 0) {
+    for (int s = 0; s < kRing; ++s) mbar_init(&sm.row_bar[s], kWarps);
+    if (p.C > 1) mbar_init(&sm.merge_bar, 1);
+    fence_mbar_init();
   }
+  __syncthreads();
+  if (p.C > 1) cluster_arrive_relaxed();
 
   const int64_t start = (int64_t)split * p.split_topk;
   const int64_t end = min(start + p.split_topk, p.topk);
   const int n_rows = end > start ? (int)(end - start) : 0;
   const int n_tiles = (n_rows + kBN - 1) / kBN;
   const int32_t *idx_row = p.idx + (int64_t)t * p.idx_st;
-  const uint8_t *kv_lane = p.kv + warp * 64 + c * 16;  // this lane's 16-byte column of a row
   const int64_t seq_kv = p.seq_kv;
 
   auto row_ok = [&](int r) { return r >= 0 && (int64_t)r < seq_kv; };
@@ -198,71 +211,33 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   // rows outside [0, seq_kv) as for any index).  Same mapping as the
   // standalone titan_convert_req_index_to_global.
   const int req = kPaged ? __ldg(p.req_id + t) : 0;
-  // Gather of tile j into ring stage st, asynchronously (cp.async): each lane
-  // copies its own four 16-byte row pieces (its MMA B fragments), zero-filled
-  // for masked rows, which are never read; the scale loaders fetch the row
-  // scales; warps 0-3 record which rows are valid.  One commit group per
-  // tile, empty past the last tile.
-  auto issue = [&](int j, int st, const int (&r)[4]) {
-    if (j < n_tiles) {
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const bool ok = row_ok(r[nt]);
-        cp_async_16_zfill(&sm.u.ring.rows[st][warp][nt][lane],
-                          ok ? static_cast<const void *>(kv_lane + (int64_t)r[nt] * p.kv_rs) : p.q, ok ? 16u : 0u);
-      }
-      if (warp < 4) {
-        const int rs = pick4(r, warp);
-        const bool ok = row_ok(rs);
-        if (c == 0)
-          cp_async_4_zfill(&sm.u.ring.scale[st][warp * 8 + g],
-                           ok ? static_cast<const void *>(p.kv + (int64_t)rs * p.kv_rs + 512) : p.q, ok ? 4u : 0u);
-        const uint32_t vb = __ballot_sync(0xffffffffu, c == 0 && ok);
-        if (lane == 0) sm.vword[st][warp] = vb;
-      }
-    }
-    cp_async_commit();
-  };
-
-  // Paged: warp 0 also stages the block-table entries of tile j's positions
-  // (4-byte cp.async, reading the positions from the index ring), three
-  // tiles after the positions and three before the rows; rows are formed
-  // from both rings when the tile is issued.
   const bool req_ok = req >= 0 && req < p.num_reqs;
   const int32_t *bt_req = p.block_table + (int64_t)(req_ok ? req : 0) * p.bt_st0;
-  auto copy_base = [&](int j) {
-    if (warp == 0 && j < n_tiles) {
-      const int x = sm.u.ring.idx[j % kIdxRing][lane];
-      const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
-      if (req_ok && x >= 0 && blk < p.max_blocks)
-        cp_async_4_zfill(&sm.u.ring.base[j % kIdxRing][lane], bt_req + (int64_t)blk * p.bt_st1, 4u);
-    }
+
+  // Tile layout in a ring stage: the row at n-order position 8 nt + g (n-tile
+  // nt, row g of the MMA B fragment) sits in gather4 group (g >> 1) + 4 (nt >> 1)
+  // at slot 2 (g & 1) + (nt & 1).  With the 544-byte pitch (= 32 mod 128) the
+  // two rows a quarter-warp reads are 64 bytes apart in the banks: the
+  // lanes' 16-byte loads are conflict free.  Group w therefore holds the
+  // positions b, b + 8, b + 1, b + 9 with b = 16 (w >> 2) + 2 (w & 3).
+  auto row_offset = [](int nt, int gg) {
+    return ((gg >> 1) + 4 * (nt >> 1)) * kGroupBytes + (2 * (gg & 1) + (nt & 1)) * kRowPitch;
   };
-  auto read_rows_paged = [&](int j, int (&r)[4]) {
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      int row = -1;
-      if (j < n_tiles) {
-        const int x = sm.u.ring.idx[j % kIdxRing][nt * 8 + g];
-        const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
-        if (req_ok && x >= 0 && blk < p.max_blocks) {
-          const int64_t v =
-              (int64_t)sm.u.ring.base[j % kIdxRing][nt * 8 + g] * p.block_stride_rows + (x - blk * p.block_size);
-          row = (v >= 0 && v <= 0x7fffffffLL) ? (int)v : -1;
-        }
-      }
-      r[nt] = row;
-    }
+  auto row_valid = [](uint64_t vb, int nt, int gg) {
+    return (uint32_t)(vb >> (8 * ((gg >> 1) + 4 * (nt >> 1)) + 2 * (gg & 1) + (nt & 1))) & 1u;
   };
+  const int grp_b = 16 * (warp >> 2) + 2 * (warp & 3);  // first position of this warp's group
 
   // Warp 0 stages the 32 indices (paged: positions) of tile j into slot j % 8
-  // with 4-byte cp.async five (paged: eight) tiles ahead of the row gather
-  // (they ride in that iteration's commit group, so the per-tile wait and
-  // barriers publish them; a slot is read three iterations after its copy);
-  // every thread reads its four from shared memory when it issues the tile's
-  // rows: no register hand-over of a pending load.
+  // with 4-byte cp.async five (paged: eight) tiles ahead of the row gather,
+  // one commit group per iteration; paged, it also stages the block-table
+  // entry of each position five tiles ahead (reading the position from the
+  // ring).  Warp 0 waits for a slot two iterations after its copy
+  // (cp.async.wait_group 1) and the CTA barriers of that iteration publish it
+  // to every warp, which reads it one iteration later: no thread waits on a
+  // load issued one tile earlier.
   auto copy_idx = [&](int j) {
-    if (warp == 0 && j < n_tiles) {
+    if (j < n_tiles) {
       const int64_t pos = start + (int64_t)j * kBN + lane;
       int32_t *dst = &sm.u.ring.idx[j % kIdxRing][lane];
       if (pos < end)
@@ -271,43 +246,63 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
         *dst = -1;
     }
   };
-  auto read_idx = [&](int j, int (&r)[4]) {
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) r[nt] = j < n_tiles ? sm.u.ring.idx[j % kIdxRing][nt * 8 + g] : -1;
+  auto copy_base = [&](int j) {
+    if (j < n_tiles) {
+      const int x = sm.u.ring.idx[j % kIdxRing][lane];
+      const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
+      if (req_ok && x >= 0 && blk < p.max_blocks)
+        cp_async_4_zfill(&sm.u.ring.base[j % kIdxRing][lane], bt_req + (int64_t)blk * p.bt_st1, 4u);
+    }
+  };
+  // Row of tile-j position `pos` (paged: translated; -1 when masked).
+  auto row_at = [&](int j, int pos) {
+    const int x = sm.u.ring.idx[j % kIdxRing][pos];
+    if constexpr (!kPaged) {
+      return x;
+    } else {
+      const int blk = p.block_shift >= 0 ? (x >> p.block_shift) : x / p.block_size;
+      int row = -1;
+      if (req_ok && x >= 0 && blk < p.max_blocks) {
+        const int64_t v = (int64_t)sm.u.ring.base[j % kIdxRing][pos] * p.block_stride_rows + (x - blk * p.block_size);
+        row = (v >= 0 && v <= 0x7fffffffLL) ? (int)v : -1;
+      }
+      return row;
+    }
+  };
+  // Gather of tile j (< n_tiles) into stage st: lane 0 of warp w issues
+  // group w (one gather4; none when its four rows are all masked), arrives on
+  // the stage barrier with the bytes it issued and records the group's
+  // validity (bit k = slot k) in vbits[st][w].
+  auto issue = [&](int j, int st) {
+    if (lane == 0) {
+      const int r0 = row_at(j, grp_b), r1 = row_at(j, grp_b + 8);
+      const int r2 = row_at(j, grp_b + 1), r3 = row_at(j, grp_b + 9);
+      const uint32_t v = (uint32_t)row_ok(r0) | (uint32_t)row_ok(r1) << 1 | (uint32_t)row_ok(r2) << 2 |
+                         (uint32_t)row_ok(r3) << 3;
+      mbar_arrive_expect_tx(&sm.row_bar[st], v ? (uint32_t)kGroupBytes : 0u);
+      if (v) tma_gather4(&sm.u.ring.rows[st][warp][0], &rows_map, 0, r0, r1, r2, r3, &sm.row_bar[st]);
+      sm.vbits[st][warp] = (uint8_t)v;
+    }
   };
 
   // Tiles 0 and 1 in flight; the index ring holds tiles 2..4 (paged:
   // positions of tiles 2..7 and block-table entries of tiles 2..4).
-  {
-    int r0[4];
+  if (warp == 0) {
+#pragma unroll 1
+    for (int j = 0; j < (kPaged ? 8 : 5); ++j) copy_idx(j);
+    cp_async_commit();
+    cp_async_wait<0>();
     if constexpr (kPaged) {
+      __syncwarp();
 #pragma unroll 1
-      for (int j = 0; j < 8; ++j) copy_idx(j);  // positions of tiles 0..7
+      for (int j = 0; j < 5; ++j) copy_base(j);
       cp_async_commit();
       cp_async_wait<0>();
-      __syncthreads();
-#pragma unroll 1
-      for (int j = 0; j < 5; ++j) copy_base(j);  // their block-table entries, tiles 0..4
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
-      read_rows_paged(0, r0);
-      issue(0, 0, r0);
-      read_rows_paged(1, r0);
-      issue(1, 1, r0);
-      __syncthreads();  // slots 0 and 1 are refilled from the first iteration on
-    } else {
-#pragma unroll 1
-      for (int j = 0; j < 5; ++j) copy_idx(j);
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
-      read_idx(0, r0);
-      issue(0, 0, r0);
-      read_idx(1, r0);
-      issue(1, 1, r0);
     }
   }
+  __syncthreads();
+  if (n_tiles > 0) issue(0, 0);
+  if (n_tiles > 1) issue(1, 1);
 
   // q fragments for this warp's 64 dims (A operand of QK), 4 k-steps.
   uint32_t qa[4][4];
@@ -349,25 +344,28 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
   const int red_n = red_j & 7;
 
   int st = 0, st_issue = 2;  // ring stage of tile i and of tile i + 2
+  long long wait_limit = kLongWaitCycles;
   for (int i = 0; i < n_tiles; ++i) {
-    // Tile i + 2 goes in flight, later tiles' indices are staged, and tile
-    // i's pieces (this lane's own copies) are waited for.
-    if constexpr (kPaged) {
-      copy_idx(i + 8);   // positions, eight tiles ahead
-      copy_base(i + 5);  // block-table entries, five tiles ahead
-      int r2[4];
-      read_rows_paged(i + 2, r2);
-      issue(i + 2, st_issue, r2);
-    } else {
-      copy_idx(i + 5);  // committed with tile i + 2's rows; read at iteration i + 3
-      int r2[4];
-      read_idx(i + 2, r2);
-      issue(i + 2, st_issue, r2);
+    // Tile i + 2 goes in flight (its indices were published by the last
+    // iteration's barriers); warp 0 stages later tiles' indices.
+    if (i + 2 < n_tiles) issue(i + 2, st_issue);
+    if (warp == 0) {
+      cp_async_wait<1>();  // copies of two iterations back have landed; this iteration's barriers publish them
+      if constexpr (kPaged) {
+        copy_base(i + 5);  // block-table entries, five tiles ahead
+        copy_idx(i + 8);   // positions, eight tiles ahead
+      } else {
+        copy_idx(i + 5);
+      }
+      cp_async_commit();
     }
-    cp_async_wait<2>();
+    // Tile i's rows (this stage's k-th use has parity k & 1).
+    if (!mbar_wait_bounded(&sm.row_bar[st], (uint32_t)(i / kRing) & 1u, wait_limit)) wait_limit = kShortWaitCycles;
+    const uint8_t *stage = sm.u.ring.rows[st][0];
     uint4 kb_cur[4];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) kb_cur[nt] = sm.u.ring.rows[st][warp][nt][lane];
+    for (int nt = 0; nt < 4; ++nt)
+      kb_cur[nt] = *reinterpret_cast<const uint4 *>(stage + row_offset(nt, g) + warp * 64 + c * 16);
 
     // ---- QK^T over this warp's 64 dims; keep the bf16 B fragments for PV.
     uint32_t kf[4][4][2];
@@ -393,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
         *reinterpret_cast<float2 *>(&red[(g + 8) * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[nt][2], sacc[nt][3]);
       }
     }
-    __syncthreads();  // partial scores, and this tile's scales (waited for by their loaders)
+    __syncthreads();  // partial scores
 
     // ---- Reduce the 8 partial scores, scale, mask, online softmax, P.
     {
@@ -404,9 +402,10 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
         s0 += v.x;
         s1 += v.y;
       }
-      const uint32_t vw = sm.vword[st][red_nt];
-      const bool v0 = (vw >> (4 * red_n)) & 1u, v1 = (vw >> (4 * red_n + 4)) & 1u;
-      const float sc0 = sm.u.ring.scale[st][red_j], sc1 = sm.u.ring.scale[st][red_j + 1];
+      const uint64_t vb = *reinterpret_cast<const uint64_t *>(sm.vbits[st]);
+      const bool v0 = row_valid(vb, red_nt, red_n), v1 = row_valid(vb, red_nt, red_n + 1);
+      const float sc0 = *reinterpret_cast<const float *>(stage + row_offset(red_nt, red_n) + 512);
+      const float sc1 = *reinterpret_cast<const float *>(stage + row_offset(red_nt, red_n + 1) + 512);
       const float x0 = v0 ? (s0 * sc0) * p.scale_log2 : kNegLarge;
       const float x1 = v1 ? (s1 * sc1) * p.scale_log2 : kNegLarge;
       float mx = fmaxf(x0, x1);
@@ -457,7 +456,9 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_mla_kernel(const Params p)
     st = st == kRing - 1 ? 0 : st + 1;
     st_issue = st_issue == kRing - 1 ? 0 : st_issue + 1;
   }
-  cp_async_wait<0>();  // only empty groups can remain; the ring is dead from here
+  // Every issued gather was waited for; warp 0's index copies beyond the
+  // last tile are empty groups.  The ring is dead from here.
+  cp_async_wait<0>();
 
   // ---- Epilogue.  Lane (g, c) of warp w holds, for heads g and g + 8,
   // dims 64 w + 16 c + j at acc[2 s + x][2 half + e] with j = 4 s + 2 x + e.
@@ -756,6 +757,59 @@ static cudaError_t launch_combine(const Params &prm, int groups, cudaStream_t s)
   return cudaLaunchKernelEx(&cfg, sparse_mla_combine_kernel, prm);
 }
 
+// Tensor map of the cache for the row gather: a 2-D tensor of uint32 words,
+// 132 per row (528 bytes), rows kv_row_stride bytes apart; boxes of 136 words
+// by one row (the 16 bytes past the row read as zeros and are never used).
+// Rows at or beyond min(seq_kv, 2^31) are outside the map (int32 indices
+// cannot reach further).  Encoded through the driver entry point; the last
+// encoding of each host thread is reused.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static int rows_tensor_map(const void *kv, int64_t seq_kv, int64_t kv_row_stride, const void *dummy, CUtensorMap *out) {
+  static EncodeTiledFn encode = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<EncodeTiledFn>(fn);
+    else
+      cudaGetLastError();
+    looked_up = true;
+  }
+  if (encode == nullptr) return fail(TITAN_ERR_CUDA, "mla: cuTensorMapEncodeTiled is unavailable");
+  // seq_kv == 0: no row is valid and nothing is loaded; any aligned address
+  // makes a well-formed map.
+  const void *base = seq_kv > 0 ? kv : dummy;
+  const int64_t rows = seq_kv > 0 ? (seq_kv < 0x7fffffffLL ? seq_kv : 0x7fffffffLL) : 1;
+  const int64_t stride = seq_kv > 0 ? kv_row_stride : TITAN_ROW_BYTES;
+  static thread_local const void *last_base = nullptr;
+  static thread_local int64_t last_rows = -1, last_stride = -1;
+  static thread_local CUtensorMap last_map;
+  if (base == last_base && rows == last_rows && stride == last_stride) {
+    *out = last_map;
+    return TITAN_OK;
+  }
+  const cuuint64_t dims[2] = {TITAN_ROW_BYTES / 4, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)stride};
+  const cuuint32_t box[2] = {kRowPitch / 4, 1};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(base), dims, strides, box, elem,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TITAN_ERR_CUDA, "mla: cuTensorMapEncodeTiled failed (%d) for rows=%lld stride=%lld", (int)r,
+                (long long)rows, (long long)stride);
+  last_base = base;
+  last_rows = rows;
+  last_stride = stride;
+  last_map = *out;
+  return TITAN_OK;
+}
+
 // Per-device one-time setup: dynamic shared-memory opt-in, non-portable
 // cluster size opt-in, and the largest cluster size the device can schedule
 // for this kernel (queried, not assumed).
@@ -768,7 +822,7 @@ static int prepare_device(size_t smem, const int **capacity) {
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "mla: device ordinal %d out of range", dev);
   if (!g_dev_ready[dev]) {
-    void (*kernels[4])(const Params) = {sparse_mla_kernel<false, false>, sparse_mla_kernel<true, false>,
+    void (*kernels[4])(const Params, const CUtensorMap) = {sparse_mla_kernel<false, false>, sparse_mla_kernel<true, false>,
                                         sparse_mla_kernel<false, true>, sparse_mla_kernel<true, true>};
     for (auto k : kernels) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1016,6 +1070,10 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
     prm.part_lse = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + o_bytes);
   }
 
+  CUtensorMap rows_map;
+  rc = rows_tensor_map(kv, seq_kv, kv_row_stride, q, &rows_map);
+  if (rc != TITAN_OK) return rc;
+
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(num_tokens * num_kv_splits), (unsigned)groups, 1);
@@ -1033,11 +1091,11 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   cfg.numAttrs = C > 1 ? 2 : 1;
   cudaError_t e;
   if (paged != nullptr)
-    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true>, prm)
-               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true>, prm);
+    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true>, prm, rows_map)
+               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true>, prm, rows_map);
   else
-    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, false>, prm)
-               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false>, prm);
+    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, false>, prm, rows_map)
+               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false>, prm, rows_map);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla launch (C=%d): %s", C, cudaGetErrorString(e));
   if (NC == 1 || in_kernel_merge) return TITAN_OK;
   // Combine the NC cluster partials: 32 CTAs per (token, head group).
