@@ -74,6 +74,7 @@ struct Smem {
   } u;
   float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
   alignas(8) uint8_t vbits[kRing][kGroups];  // per stage and gather4 group: bit k = slot k valid
+  float scale[kBN];                        // row scales of the current tile, n-order (masked: unused)
   float alpha[kHeads];
   float2 ml[kHeads];                       // final (m, l) of this CTA
   float cw[kMaxCluster][kHeads];           // cluster merge weights
@@ -366,6 +367,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
       kb_cur[nt] = *reinterpret_cast<const uint4 *>(stage + row_offset(nt, g) + warp * 64 + c * 16);
+    // Warp 0 packs the 32 row scales (bytes 512..515 of each row) n-order for
+    // the reduction below; the next iteration rewrites them only after this
+    // iteration's second barrier.
+    if (warp == 0) sm.scale[lane] = *reinterpret_cast<const float *>(stage + row_offset(lane >> 3, lane & 7) + 512);
 
     // ---- QK^T over this warp's 64 dims; keep the bf16 B fragments for PV.
     uint32_t kf[4][4][2];
@@ -391,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         *reinterpret_cast<float2 *>(&red[(g + 8) * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[nt][2], sacc[nt][3]);
       }
     }
-    __syncthreads();  // partial scores
+    __syncthreads();  // partial scores, row scales
 
     // ---- Reduce the 8 partial scores, scale, mask, online softmax, P.
     {
@@ -404,8 +409,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const uint64_t vb = *reinterpret_cast<const uint64_t *>(sm.vbits[st]);
       const bool v0 = row_valid(vb, red_nt, red_n), v1 = row_valid(vb, red_nt, red_n + 1);
-      const float sc0 = *reinterpret_cast<const float *>(stage + row_offset(red_nt, red_n) + 512);
-      const float sc1 = *reinterpret_cast<const float *>(stage + row_offset(red_nt, red_n + 1) + 512);
+      const float2 sc = *reinterpret_cast<const float2 *>(&sm.scale[red_j]);
+      const float sc0 = sc.x, sc1 = sc.y;
       const float x0 = v0 ? (s0 * sc0) * p.scale_log2 : kNegLarge;
       const float x1 = v1 ? (s1 * sc1) * p.scale_log2 : kNegLarge;
       float mx = fmaxf(x0, x1);
