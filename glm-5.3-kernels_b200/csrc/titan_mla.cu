@@ -276,10 +276,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   // validity (bit k = slot k) in vbits[st][w].
   auto issue = [&](int j, int st) {
     if (lane == 0) {
-      const int r0 = row_at(j, grp_b), r1 = row_at(j, grp_b + 8);
-      const int r2 = row_at(j, grp_b + 1), r3 = row_at(j, grp_b + 9);
+      int r0 = row_at(j, grp_b), r1 = row_at(j, grp_b + 8);
+      int r2 = row_at(j, grp_b + 1), r3 = row_at(j, grp_b + 9);
       const uint32_t v = (uint32_t)row_ok(r0) | (uint32_t)row_ok(r1) << 1 | (uint32_t)row_ok(r2) << 2 |
                          (uint32_t)row_ok(r3) << 3;
+      // Masked rows go to the gather as row -1 (read as zeros, never used),
+      // whatever their index was.
+      r0 = (v & 1u) ? r0 : -1;
+      r1 = (v & 2u) ? r1 : -1;
+      r2 = (v & 4u) ? r2 : -1;
+      r3 = (v & 8u) ? r3 : -1;
       mbar_arrive_expect_tx(&sm.row_bar[st], v ? (uint32_t)kGroupBytes : 0u);
       if (v) tma_gather4(&sm.u.ring.rows[st][warp][0], &rows_map, 0, r0, r1, r2, r3, &sm.row_bar[st]);
       sm.vbits[st][warp] = (uint8_t)v;
