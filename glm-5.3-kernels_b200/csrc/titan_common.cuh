@@ -154,12 +154,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
-// 16 / 4 bytes global -> shared, zero-filling the destination beyond
-// `src_bytes` (0 = nothing is read: the source address is not accessed).
-__device__ __forceinline__ void cp_async_16_zfill(void *dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
+// 4 bytes global -> shared, zero-filling the destination beyond `src_bytes`
+// (0 = nothing is read: the source address is not accessed).
 __device__ __forceinline__ void cp_async_4_zfill(void *dst, const void *src, uint32_t src_bytes) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                : "memory");

@@ -4,8 +4,10 @@
 Drop-in for the reference `triton_mla_sparse_attention`
 (kernels/titan_mla.py:452-581) with the same argument order, defaults,
 assertions and split heuristic (`_choose_num_kv_splits`, :432-449).  The
-compute runs in libtitan_b200.so (csrc/titan_mla.cu): rows gathered straight
-into tensor-core fragments, bf16 MMAs with fp32 online softmax, and split
+compute runs in libtitan_b200.so (csrc/titan_mla.cu): rows gathered by the
+tensor memory accelerator (`tile::gather4`, four rows per load) into a
+shared-memory ring laid out as the lanes' tensor-core fragments, bf16 MMAs
+with fp32 online softmax, and split
 partials merged inside thread-block clusters and, across clusters, by the
 last CTA to finish (arrival counters).
 
@@ -81,15 +83,15 @@ def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int
 # per-partial term), and a penalty when more clusters are launched than fit
 # with one CTA per SM (they then share SMs and slow each other's gathers).
 # Fitted to a B200 sweep of every split count with at most one CTA per SM for
-# B = 1..8 (calls back to back in CUDA graphs, cold L2): the median of the
-# parameter sets whose picks lose the least against the best measured split
-# count (0.25 us summed over the eight batch sizes).
+# B = 1..8 (calls back to back in CUDA graphs, cold L2, the TMA-gather
+# reader): the median of the parameter sets whose picks match the best
+# measured split count at every batch size.
 _TILE_ROWS = 32
-_COST_TILE_US = 0.75
+_COST_TILE_US = 0.6
 _COST_CLUSTER_MERGE_US = 0.8
-_COST_SPLIT_MERGE_US = 0.6
+_COST_SPLIT_MERGE_US = 0.8
 _COST_COMBINE_US = 1.0
-_COST_COMBINE_PER_PARTIAL_US = 0.05
+_COST_COMBINE_PER_PARTIAL_US = 0.08
 _COST_SHARED_SM_US = 1.5
 _MAX_CLUSTER = 16
 _CLUSTER_SIZES = (1, 2, 4, 8, 16)
