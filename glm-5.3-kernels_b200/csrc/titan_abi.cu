@@ -23,6 +23,11 @@ int fail(int code, const char *fmt, ...) {
   return code;
 }
 
+std::mutex &setup_mutex() {
+  static std::mutex m;
+  return m;
+}
+
 int check_launch(const char *what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));

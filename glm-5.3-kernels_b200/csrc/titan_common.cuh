@@ -9,12 +9,19 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/titan_b200.h"
 
 namespace titan {
 
 // ---------------------------------------------------------------- host side
 void set_error(const char *fmt, ...);
+// Serialises the one-time per-device setup of the launchers (kernel
+// attributes, capacity queries, symbol lookups); readers check an atomic
+// ready flag first, so steady-state launches take no lock.
+std::mutex &setup_mutex();
 int fail(int code, const char *fmt, ...);
 int check_launch(const char *what);
 

@@ -323,18 +323,27 @@ extern "C" int titan_store_int8(const void *x, int64_t x_row_stride, void *cache
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (aligned && cache_stride1 % 8 == 0 && n_slots >= 1024) {
     // Large batches: persistent streaming kernel, three CTAs per SM.
-    static bool attr_done[64] = {false};
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(store_int8_stream_kernel<int64_t>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kKvStreamSmem);
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(store_int8_stream_kernel<int32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    // Per device, once: the kernels' shared-memory opt-in and the SM count.
+    static std::atomic<int> dev_sms[64];  // 0 = not set up
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64)
+      return fail(TITAN_ERR_CUDA, "store_int8: cudaGetDevice: %s", cudaGetErrorString(e));
+    int sms = dev_sms[dev].load(std::memory_order_acquire);
+    if (sms == 0) {
+      std::lock_guard<std::mutex> lock(setup_mutex());
+      sms = dev_sms[dev].load(std::memory_order_relaxed);
+      if (sms == 0) {
+        e = cudaFuncSetAttribute(store_int8_stream_kernel<int64_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kKvStreamSmem);
-      if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "store_int8: smem attribute: %s", cudaGetErrorString(e));
-      attr_done[dev] = true;
+        if (e == cudaSuccess)
+          e = cudaFuncSetAttribute(store_int8_stream_kernel<int32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kKvStreamSmem);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess || sms <= 0)
+          return fail(TITAN_ERR_CUDA, "store_int8: device setup: %s", cudaGetErrorString(e));
+        dev_sms[dev].store(sms, std::memory_order_release);
+      }
     }
     const int64_t warps_needed = (n_slots + 1) / 2;
     const int64_t ctas_needed = (warps_needed + kKvStreamWarps - 1) / kKvStreamWarps;

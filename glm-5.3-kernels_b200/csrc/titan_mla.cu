@@ -779,18 +779,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static int rows_tensor_map(const void *kv, int64_t seq_kv, int64_t kv_row_stride, const void *dummy, CUtensorMap *out) {
-  static EncodeTiledFn encode = nullptr;
-  static bool looked_up = false;
-  if (!looked_up) {
+  static const EncodeTiledFn encode = [] {  // looked up once (thread-safe static initialisation)
     void *fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      encode = reinterpret_cast<EncodeTiledFn>(fn);
-    else
-      cudaGetLastError();
-    looked_up = true;
-  }
+      return reinterpret_cast<EncodeTiledFn>(fn);
+    cudaGetLastError();
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
   if (encode == nullptr) return fail(TITAN_ERR_CUDA, "mla: cuTensorMapEncodeTiled is unavailable");
   // seq_kv == 0: no row is valid and nothing is loaded; any aligned address
   // makes a well-formed map.
@@ -824,7 +821,7 @@ static int rows_tensor_map(const void *kv, int64_t seq_kv, int64_t kv_row_stride
 // Per-device one-time setup: dynamic shared-memory opt-in, non-portable
 // cluster size opt-in, and the largest cluster size the device can schedule
 // for this kernel (queried, not assumed).
-static bool g_dev_ready[64] = {false};
+static std::atomic<bool> g_dev_ready[64];
 static int g_cluster_capacity[64][kMaxCluster + 1];  // [dev][C] co-resident clusters of C CTAs
 
 static int prepare_device(size_t smem, const int **capacity) {
@@ -832,7 +829,12 @@ static int prepare_device(size_t smem, const int **capacity) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "mla: device ordinal %d out of range", dev);
-  if (!g_dev_ready[dev]) {
+  if (!g_dev_ready[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(setup_mutex());
+    if (g_dev_ready[dev].load(std::memory_order_relaxed)) {
+      *capacity = g_cluster_capacity[dev];
+      return TITAN_OK;
+    }
     void (*kernels[4])(const Params, const CUtensorMap) = {sparse_mla_kernel<false, false>, sparse_mla_kernel<true, false>,
                                         sparse_mla_kernel<false, true>, sparse_mla_kernel<true, true>};
     for (auto k : kernels) {
@@ -868,7 +870,7 @@ static int prepare_device(size_t smem, const int **capacity) {
       }
       g_cluster_capacity[dev][cs] = n;
     }
-    g_dev_ready[dev] = true;
+    g_dev_ready[dev].store(true, std::memory_order_release);
   }
   *capacity = g_cluster_capacity[dev];
   return TITAN_OK;
@@ -901,7 +903,11 @@ static int max_active_clusters(int cluster_size, bool exclusive) {
   const int *capacity = nullptr;
   if (prepare_device(sizeof(Smem), &capacity) != TITAN_OK) return -1;
   size_t smem = sizeof(Smem);
+  // The exclusive query raises and restores the kernel's shared-memory
+  // ceiling: one query at a time.
+  std::unique_lock<std::mutex> lock(setup_mutex(), std::defer_lock);
   if (exclusive) {
+    lock.lock();
     int dev = 0, per_sm = 0, optin = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
@@ -1184,7 +1190,7 @@ namespace mla {
 
 constexpr int64_t kNoAllocScratchBytes = 8ll << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
-static void *g_noalloc_scratch_ptr[64] = {nullptr};
+static std::atomic<void *> g_noalloc_scratch_ptr[64];
 
 }  // namespace mla
 }  // namespace titan
@@ -1213,14 +1219,13 @@ extern "C" int titan_mla_sparse_attention_noalloc(const void *q, int64_t q_strid
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "mla noalloc: device ordinal %d out of range", dev);
-    if (g_noalloc_scratch_ptr[dev] == nullptr) {
-      void *ptr = nullptr;
-      e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-      if (e != cudaSuccess || ptr == nullptr)
+    scratch = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
+    if (scratch == nullptr) {
+      e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
+      if (e != cudaSuccess || scratch == nullptr)
         return fail(TITAN_ERR_CUDA, "mla noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-      g_noalloc_scratch_ptr[dev] = ptr;
+      g_noalloc_scratch_ptr[dev].store(scratch, std::memory_order_release);  // same address from any thread
     }
-    scratch = g_noalloc_scratch_ptr[dev];
   }
   return titan_mla_sparse_attention(q, q_stride_token, q_stride_head, kv, kv_row_stride, seq_kv, indices,
                                     indices_stride_token, topk, out, out_stride_token, out_stride_head, num_tokens,

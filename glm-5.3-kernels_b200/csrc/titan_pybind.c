@@ -11,7 +11,9 @@
  *
  * Argument kinds: 'p' pointer (Python int or None), 'i' int64, 'f' float.
  * Every argument is converted before the call; a conversion error raises
- * without launching anything.  Each wrapper returns the launcher's status.
+ * without launching anything.  The launcher runs with the GIL released (as
+ * under ctypes), so threads driving different streams or GPUs overlap; each
+ * wrapper returns the launcher's status.
  */
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
@@ -76,8 +78,11 @@ static PyObject *py_mla(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   double fv[MAX_ARGS];
   UNBOUND(p_mla);
   if (parse("mla", a, n, "piipiipiipiiiifipip", iv, fv)) return NULL;
-  int rc = p_mla(P(0), I(1), I(2), P(3), I(4), I(5), (const int32_t *)P(6), I(7), I(8), P(9), I(10), I(11), I(12),
-                 I(13), F(14), I(15), P(16), I(17), (titan_stream_t)P(18));
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_mla(P(0), I(1), I(2), P(3), I(4), I(5), (const int32_t *)P(6), I(7), I(8), P(9), I(10), I(11), I(12),
+                   I(13), F(14), I(15), P(16), I(17), (titan_stream_t)P(18));
+  Py_END_ALLOW_THREADS
   return PyLong_FromLong(rc);
 }
 
@@ -86,8 +91,11 @@ static PyObject *py_mla_sem(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   double fv[MAX_ARGS];
   UNBOUND(p_mla_sem);
   if (parse("mla_sem", a, n, "piipiipiipiiiifipipip", iv, fv)) return NULL;
-  int rc = p_mla_sem(P(0), I(1), I(2), P(3), I(4), I(5), (const int32_t *)P(6), I(7), I(8), P(9), I(10), I(11),
-                     I(12), I(13), F(14), I(15), P(16), I(17), (int32_t *)P(18), I(19), (titan_stream_t)P(20));
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_mla_sem(P(0), I(1), I(2), P(3), I(4), I(5), (const int32_t *)P(6), I(7), I(8), P(9), I(10), I(11),
+                       I(12), I(13), F(14), I(15), P(16), I(17), (int32_t *)P(18), I(19), (titan_stream_t)P(20));
+  Py_END_ALLOW_THREADS
   return PyLong_FromLong(rc);
 }
 
@@ -96,9 +104,12 @@ static PyObject *py_mla_paged(PyObject *self, PyObject *const *a, Py_ssize_t n) 
   double fv[MAX_ARGS];
   UNBOUND(p_mla_paged);
   if (parse("mla_paged", a, n, "piipiipiipipiiiiipiiiifipipip", iv, fv)) return NULL;
-  int rc = p_mla_paged(P(0), I(1), I(2), P(3), I(4), I(5), (const int32_t *)P(6), I(7), I(8), (const int32_t *)P(9),
-                       I(10), (const int32_t *)P(11), I(12), I(13), I(14), I(15), I(16), P(17), I(18), I(19), I(20),
-                       I(21), F(22), I(23), P(24), I(25), (int32_t *)P(26), I(27), (titan_stream_t)P(28));
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_mla_paged(P(0), I(1), I(2), P(3), I(4), I(5), (const int32_t *)P(6), I(7), I(8), (const int32_t *)P(9),
+                         I(10), (const int32_t *)P(11), I(12), I(13), I(14), I(15), I(16), P(17), I(18), I(19), I(20),
+                         I(21), F(22), I(23), P(24), I(25), (int32_t *)P(26), I(27), (titan_stream_t)P(28));
+  Py_END_ALLOW_THREADS
   return PyLong_FromLong(rc);
 }
 
@@ -107,7 +118,11 @@ static PyObject *py_copy(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   double fv[MAX_ARGS];
   UNBOUND(p_copy);
   if (parse("copy", a, n, "ppip", iv, fv)) return NULL;
-  return PyLong_FromLong(p_copy(P(0), P(1), I(2), (titan_stream_t)P(3)));
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_copy(P(0), P(1), I(2), (titan_stream_t)P(3));
+  Py_END_ALLOW_THREADS
+  return PyLong_FromLong(rc);
 }
 
 static PyObject *py_store_int8(PyObject *self, PyObject *const *a, Py_ssize_t n) {
@@ -115,8 +130,11 @@ static PyObject *py_store_int8(PyObject *self, PyObject *const *a, Py_ssize_t n)
   double fv[MAX_ARGS];
   UNBOUND(p_store_int8);
   if (parse("store_int8", a, n, "pipiiiipiip", iv, fv)) return NULL;
-  return PyLong_FromLong(
-      p_store_int8(P(0), I(1), P(2), I(3), I(4), I(5), I(6), P(7), (int)I(8), I(9), (titan_stream_t)P(10)));
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_store_int8(P(0), I(1), P(2), I(3), I(4), I(5), I(6), P(7), (int)I(8), I(9), (titan_stream_t)P(10));
+  Py_END_ALLOW_THREADS
+  return PyLong_FromLong(rc);
 }
 
 static PyObject *py_moe_align(PyObject *self, PyObject *const *a, Py_ssize_t n) {
@@ -124,8 +142,12 @@ static PyObject *py_moe_align(PyObject *self, PyObject *const *a, Py_ssize_t n) 
   double fv[MAX_ARGS];
   UNBOUND(p_moe_align);
   if (parse("moe_align", a, n, "piipppip", iv, fv)) return NULL;
-  return PyLong_FromLong(p_moe_align(P(0), (int)I(1), I(2), (int32_t *)P(3), (int32_t *)P(4), (int32_t *)P(5),
-                                     (int)I(6), (titan_stream_t)P(7)));
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_moe_align(P(0), (int)I(1), I(2), (int32_t *)P(3), (int32_t *)P(4), (int32_t *)P(5),
+                                       (int)I(6), (titan_stream_t)P(7));
+  Py_END_ALLOW_THREADS
+  return PyLong_FromLong(rc);
 }
 
 static PyObject *py_convert(PyObject *self, PyObject *const *a, Py_ssize_t n) {
@@ -133,9 +155,13 @@ static PyObject *py_convert(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   double fv[MAX_ARGS];
   UNBOUND(p_convert);
   if (parse("convert", a, n, "pipiiipiipiiiip", iv, fv)) return NULL;
-  return PyLong_FromLong(p_convert((const int32_t *)P(0), I(1), (const int32_t *)P(2), I(3), I(4), I(5),
-                                   (const int32_t *)P(6), I(7), I(8), (int32_t *)P(9), I(10), I(11), I(12), I(13),
-                                   (titan_stream_t)P(14)));
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_convert((const int32_t *)P(0), I(1), (const int32_t *)P(2), I(3), I(4), I(5),
+                                     (const int32_t *)P(6), I(7), I(8), (int32_t *)P(9), I(10), I(11), I(12), I(13),
+                                     (titan_stream_t)P(14));
+  Py_END_ALLOW_THREADS
+  return PyLong_FromLong(rc);
 }
 
 /* bind(mla, mla_sem, mla_paged, copy, store_int8, moe_align, convert): entry
