@@ -226,6 +226,11 @@ __device__ __forceinline__ void tma_gather4(void *dst, const void *tmap, int x, 
       : "memory");
 }
 
+// Pull a TMA descriptor (kernel parameter or global) into the descriptor cache.
+__device__ __forceinline__ void prefetch_tensormap(const void *tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 

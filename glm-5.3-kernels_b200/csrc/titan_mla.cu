@@ -181,23 +181,27 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int split = blockIdx.x - t * p.S;
   const int hg = blockIdx.y;
 
-  // Launched as a programmatic dependent of whatever ran before on the stream:
-  // CTAs may be resident early, but nothing is read before the previous grid
-  // has completed and flushed.
-  pdl_wait_primary();
-  pdl_launch_dependents();  // the combine (or the next call) may become resident now
   // Ring-stage barriers (one arrival per warp, plus the gather bytes, per
   // use) and, for clusters, the merge barrier.  Cluster peers must be
   // running, with their merge barrier initialised, before anyone writes into
   // their shared memory: initialise, publish to the cluster, arrive now, wait
-  // right before the first remote store.
+  // right before the first remote store.  None of this, nor the prefetch of
+  // the rows' tensor map, reads memory another kernel writes, so it runs
+  // before the programmatic-dependency wait, overlapping the previous grid's
+  // tail.
   if (tid == 0) {
     for (int s = 0; s < kRing; ++s) mbar_init(&sm.row_bar[s], kWarps);
     if (p.C > 1) mbar_init(&sm.merge_bar, 1);
     fence_mbar_init();
   }
+  if (tid == 32) prefetch_tensormap(&rows_map);
   __syncthreads();
   if (p.C > 1) cluster_arrive_relaxed();
+  // Launched as a programmatic dependent of whatever ran before on the stream:
+  // CTAs may be resident early, but nothing is read before the previous grid
+  // has completed and flushed.
+  pdl_wait_primary();
+  pdl_launch_dependents();  // the combine (or the next call) may become resident now
 
   const int64_t start = (int64_t)split * p.split_topk;
   const int64_t end = min(start + p.split_topk, p.topk);
