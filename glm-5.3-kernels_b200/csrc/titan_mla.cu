@@ -569,10 +569,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Bytes this CTA receives: from each of the C CTAs, its 16 x D slice of acc
   // and its 16 (m, l) pairs.
   if (tid == 0) mbar_arrive_expect_tx(&sm.merge_bar, (uint32_t)(C * kHeads * (D * 4 + 8)));
-  if ((tid & 15) == 0) {
-    const float2 ml = make_float2(m_run, l_run);
-    for (int r = 0; r < C; ++r)
-      st_async_f32x2(dsmem_addr(&sm.cml[rank][red_h], (uint32_t)r), ml, dsmem_addr(&sm.merge_bar, (uint32_t)r));
+  {
+    // Thread (head red_h, lane r of its 16) sends that head's (m, l) to peer
+    // r: all C x 16 pairs leave at once.
+    const int r = tid & 15;
+    if (r < C)
+      st_async_f32x2(dsmem_addr(&sm.cml[rank][red_h], (uint32_t)r), make_float2(m_run, l_run),
+                     dsmem_addr(&sm.merge_bar, (uint32_t)r));
   }
   {
     // Stage acc locally as [owner][head][dd] so each owner's slice is one
