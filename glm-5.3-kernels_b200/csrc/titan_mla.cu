@@ -604,45 +604,23 @@ __global__ void __launch_bounds__(kThreads, 2)
   // barrier's phase completes; only after that may it read them or exit.  No
   // cluster-wide barrier follows, and only local shared memory is read.
   mbar_wait_bounded(&sm.merge_bar, 0u, kLongWaitCycles);
-  {  // merge weights: 16 lanes per head, lane r holds peer r's (m, l)
-    const int h = tid >> 4, r = tid & 15;
-    const float2 ml = r < C ? sm.cml[r][h] : make_float2(kNegLarge, 0.0f);
-    float M = ml.x;
+  // Merge weights: 16 lanes per head (head mh), lane mr holds peer mr's (m, l).
+  const int mh = tid >> 4, mr = tid & 15;
+  const float2 mml = mr < C ? sm.cml[mr][mh] : make_float2(kNegLarge, 0.0f);
+  float M = mml.x;
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    const float w = r < C ? ex2_approx(ml.x - M) : 0.0f;
-    float L = w * ml.y;
+  for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float w = mr < C ? ex2_approx(mml.x - M) : 0.0f;
+  float L = w * mml.y;
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    if (r < C) sm.cw[r][h] = w;
-    if (r == 0) {
-      sm.cM[h] = M;
-      sm.cL[h] = L;
-    }
-  }
-  __syncthreads();
-  const int pair_shift = 8 - p.logC;       // log2(D / 2)
-  const int pairs = kHeads << pair_shift;  // float2 outputs of this CTA
-  for (int pp = tid; pp < pairs; pp += kThreads) {
-    const int h = pp >> pair_shift;
-    const int dd = 2 * (pp - (h << pair_shift));
-    float2 v[kMaxCluster];
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r)  // issue every load before any use
-      if (r < C) v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + h) * D + dd]);
-    float2 sum = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r)
-      if (r < C) {
-        const float w = sm.cw[r][h];
-        sum.x += w * v[r].x;
-        sum.y += w * v[r].y;
-      }
+  for (int o = 8; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  // Output pair (head h, dims d, d + 1 of this rank's slice) = sum over the
+  // peers of weight * partial, divided by L.
+  auto emit = [&](int h, int dd, float2 sum, float Lh) {
     const int hh = hg * kHeads + h;
     const int d = (int)rank * D + dd;
     if (hh < p.H) {
-      const float L = sm.cL[h];
-      const float inv = L > 0.0f ? 1.0f / L : 1.0f;
+      const float inv = Lh > 0.0f ? 1.0f / Lh : 1.0f;
       if constexpr (!kPartialOut) {
         *reinterpret_cast<uint32_t *>(p.out + (int64_t)t * p.out_st + (int64_t)hh * p.out_sh + d) =
             pack_bf16x2(sum.x * inv, sum.y * inv);
@@ -651,12 +629,63 @@ __global__ void __launch_bounds__(kThreads, 2)
             make_float2(sum.x * inv, sum.y * inv);
       }
     }
+  };
+  if (C == kMaxCluster) {
+    // 16 x 16 pairs = one per thread, of the head whose weights this thread's
+    // 16-lane group holds: they stay in registers (width-16 shuffles), no
+    // barrier before the reduction.
+    const int dd = 2 * mr;
+    float2 v[kMaxCluster];
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r)  // issue every load before any use
+      v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + mh) * D + dd]);
+    float2 sum = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) {
+      const float wr = __shfl_sync(0xffffffffu, w, r, 16);
+      sum.x += wr * v[r].x;
+      sum.y += wr * v[r].y;
+    }
+    emit(mh, dd, sum, L);
+    if constexpr (kPartialOut) {
+      if (mr == 0 && hg * kHeads + mh < p.H)
+        p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + mh] = (M + lg2_approx(L)) * kLn2;
+    }
+  } else {
+    if (mr < C) sm.cw[mr][mh] = w;
+    if (mr == 0) {
+      sm.cM[mh] = M;
+      sm.cL[mh] = L;
+    }
+    __syncthreads();
+    const int pair_shift = 8 - p.logC;       // log2(D / 2)
+    const int pairs = kHeads << pair_shift;  // float2 outputs of this CTA
+    for (int pp = tid; pp < pairs; pp += kThreads) {
+      const int h = pp >> pair_shift;
+      const int dd = 2 * (pp - (h << pair_shift));
+      float2 v[kMaxCluster];
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r)  // issue every load before any use
+        if (r < C) v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + h) * D + dd]);
+      float2 sum = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r)
+        if (r < C) {
+          const float wr = sm.cw[r][h];
+          sum.x += wr * v[r].x;
+          sum.y += wr * v[r].y;
+        }
+      emit(h, dd, sum, sm.cL[h]);
+    }
+    if constexpr (kPartialOut) {
+      // Every rank writes the (identical) LSE of its cluster, so the rank-r
+      // counter below orders everything the rank-r merge reads.
+      if (tid < kHeads && hg * kHeads + tid < p.H)
+        p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] =
+            (sm.cM[tid] + lg2_approx(sm.cL[tid])) * kLn2;
+    }
   }
   if constexpr (kPartialOut) {
-    // Every rank writes the (identical) LSE of its cluster, so the rank-r
-    // counter below orders everything the rank-r merge reads.
-    if (tid < kHeads && hg * kHeads + tid < p.H)
-      p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (sm.cM[tid] + lg2_approx(sm.cL[tid])) * kLn2;
     if (p.sem != nullptr) {
       // Cross-cluster merge in this kernel: the CTAs of rank r in the NC
       // clusters of (t, hg) take a ticket after publishing their slice; the
