@@ -117,6 +117,17 @@ struct Params {
   int64_t block_stride_rows;
 };
 
+// Float position of logical dim dd (0 <= dd < D = 512 / C) in the row of
+// (head hl, owner) of the cluster-merge stage and receive buffers.  The
+// 16-byte chunks of a row are XOR-swizzled (a bijection within the row): a
+// quarter-warp's 16-byte staging stores, which cover two heads and two owners
+// (C = 16) or two chunk halves (C < 16) at equal offsets, then fall on eight
+// distinct bank groups instead of two.
+__device__ __forceinline__ int merge_pos(int hl, int owner, int dd) {
+  const int chunk = dd >> 2;
+  return ((chunk ^ ((hl & 1) << 1) ^ ((chunk >> 3) & 1) ^ (owner & 1)) << 2) | (dd & 3);
+}
+
 // Last-arriver merge of the NC <= C cluster partials of (token t, head group
 // hg) over the dims of cluster rank `rank` (D = 512 / C = 32 kPer dims), same
 // arithmetic as the combine kernel below.  16 lanes per head: lane j holds
@@ -578,18 +589,20 @@ __global__ void __launch_bounds__(kThreads, 2)
                      dsmem_addr(&sm.merge_bar, (uint32_t)r));
   }
   {
-    // Stage acc locally as [owner][head][dd] so each owner's slice is one
-    // contiguous 16 x D block, then ship each block with one bulk copy.
+    // Stage acc locally as [owner][head][dd] (dd swizzled, merge_pos) so each
+    // owner's slice is one contiguous 16 x D block, then ship each block with
+    // one bulk copy; the owner reads it back through the same swizzle.
     const int owner = dim0 / D;  // 16 | D, so a lane's 16 dims have one owner
     const int dd = dim0 - owner * D;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int hl = g + 8 * half;
-      float4 *dst = reinterpret_cast<float4 *>(&sm.u.stage[(owner * kHeads + hl) * D + dd]);
+      float *row = &sm.u.stage[(owner * kHeads + hl) * D];
 #pragma unroll
       for (int s = 0; s < 4; ++s)
-        dst[s] = make_float4(acc[2 * s][2 * half], acc[2 * s][2 * half + 1], acc[2 * s + 1][2 * half],
-                             acc[2 * s + 1][2 * half + 1]);
+        *reinterpret_cast<float4 *>(row + merge_pos(hl, owner, dd + 4 * s)) =
+            make_float4(acc[2 * s][2 * half], acc[2 * s][2 * half + 1], acc[2 * s + 1][2 * half],
+                        acc[2 * s + 1][2 * half + 1]);
     }
   }
   fence_proxy_async_smem();  // make the staged block visible to the bulk-copy engine
@@ -638,7 +651,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     float2 v[kMaxCluster];
 #pragma unroll
     for (int r = 0; r < kMaxCluster; ++r)  // issue every load before any use
-      v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + mh) * D + dd]);
+      v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + mh) * D + merge_pos(mh, (int)rank, dd)]);
     float2 sum = make_float2(0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < kMaxCluster; ++r) {
@@ -666,7 +679,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       float2 v[kMaxCluster];
 #pragma unroll
       for (int r = 0; r < kMaxCluster; ++r)  // issue every load before any use
-        if (r < C) v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + h) * D + dd]);
+        if (r < C) v[r] = *reinterpret_cast<const float2 *>(&sm.rcv[(r * kHeads + h) * D + merge_pos(h, (int)rank, dd)]);
       float2 sum = make_float2(0.f, 0.f);
 #pragma unroll
       for (int r = 0; r < kMaxCluster; ++r)
