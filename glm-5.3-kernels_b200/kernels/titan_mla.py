@@ -78,20 +78,22 @@ def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int
 
 
 # Cost model of the B200 kernel (microseconds): 32-row tiles per CTA, the
-# merge inside a thread-block cluster, the merge across clusters (done by the
-# last CTA to finish when NC <= C, else by the combine kernel plus a
-# per-partial term), and a penalty when more clusters are launched than fit
-# with one CTA per SM (they then share SMs and slow each other's gathers).
-# Fitted to a B200 sweep of every split count with at most one CTA per SM for
-# B = 1..8 (calls back to back in CUDA graphs, cold L2, the TMA-gather
-# reader): the median of the parameter sets whose picks match the best
-# measured split count at every batch size.
+# merge inside a thread-block cluster (cheaper for larger clusters: each CTA
+# reduces 512 / C dims), the merge across clusters (done by the last CTA to
+# finish when NC <= C, else by the combine kernel; both plus a per-partial
+# term), and a penalty when more clusters are launched than fit with one CTA
+# per SM (they then share SMs and slow each other's gathers).  Fitted to a
+# B200 sweep of every split count with at most one CTA per SM for B = 1..8
+# (calls back to back in CUDA graphs, cold L2, the current reader): the
+# median of the parameter sets whose picks match the best measured split
+# count at every batch size.
 _TILE_ROWS = 32
-_COST_TILE_US = 0.6
-_COST_CLUSTER_MERGE_US = 0.8
+_COST_TILE_US = 0.5
+_COST_CLUSTER_MERGE_US = {2: 1.0, 4: 1.0, 8: 0.8, 16: 0.6}
 _COST_SPLIT_MERGE_US = 0.8
+_COST_SPLIT_MERGE_PER_PARTIAL_US = 0.05
 _COST_COMBINE_US = 1.0
-_COST_COMBINE_PER_PARTIAL_US = 0.08
+_COST_COMBINE_PER_PARTIAL_US = 0.05
 _COST_SHARED_SM_US = 1.5
 _MAX_CLUSTER = 16
 _CLUSTER_SIZES = (1, 2, 4, 8, 16)
@@ -143,10 +145,10 @@ def _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count, ta
         C, nc = _launch_layout(units, S, tables)
         rows = -(-index_topk // S)
         cost = max(1, -(-rows // _TILE_ROWS)) * _COST_TILE_US
-        cost += _COST_CLUSTER_MERGE_US if C > 1 else 0.0
+        cost += _COST_CLUSTER_MERGE_US[C] if C > 1 else 0.0
         if nc > 1:
             if C >= 2 and nc <= C:
-                cost += _COST_SPLIT_MERGE_US
+                cost += _COST_SPLIT_MERGE_US + _COST_SPLIT_MERGE_PER_PARTIAL_US * nc
             else:
                 cost += _COST_COMBINE_US + _COST_COMBINE_PER_PARTIAL_US * nc
         if units * nc > max(0, exclusive.get(C, 0)):

@@ -72,9 +72,11 @@ def test_b200_split_policy_picks():
     layout (cluster size C, clusters per token NC) the launcher derives."""
     from kernels.titan_mla import _choose_kv_splits_b200, _launch_layout
     picks = {B: _choose_kv_splits_b200(B, 1, 2176, 148, B200_CLUSTER_TABLES) for B in range(1, 9)}
-    assert picks == {1: 80, 2: 40, 3: 40, 4: 24, 5: 24, 6: 16, 7: 16, 8: 17}, picks
+    assert picks == {1: 80, 2: 48, 3: 40, 4: 16, 5: 16, 6: 16, 7: 16, 8: 17}, picks
     assert _launch_layout(1, 80, B200_CLUSTER_TABLES) == (16, 5)   # last-arriver merge (NC <= C)
     assert _launch_layout(2, 40, B200_CLUSTER_TABLES) == (8, 5)
+    assert _launch_layout(2, 48, B200_CLUSTER_TABLES) == (16, 3)   # last-arriver merge
+    assert _launch_layout(4, 16, B200_CLUSTER_TABLES) == (16, 1)   # one cluster per token
     assert _launch_layout(8, 17, B200_CLUSTER_TABLES) == (1, 17)   # combine kernel
     assert _launch_layout(8, 16, B200_CLUSTER_TABLES) == (16, 1)
     assert _launch_layout(7, 16, B200_CLUSTER_TABLES) == (16, 1)   # one cluster per token
