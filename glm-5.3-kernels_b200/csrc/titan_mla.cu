@@ -179,7 +179,9 @@ __device__ __forceinline__ void merge_cluster_partials(const Params &p, int t, i
   }
 }
 
-template <bool kPartialOut, bool kPaged>
+// kCluster: launched with clusters of C >= 2 CTAs (the cluster merge is
+// compiled only into these instantiations; C == 1 launches carry none of it).
+template <bool kPartialOut, bool kPaged, bool kCluster>
 __global__ void __launch_bounds__(kThreads, 2)
     sparse_mla_kernel(const Params p, const __grid_constant__ CUtensorMap rows_map) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -202,12 +204,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   // tail.
   if (tid == 0) {
     for (int s = 0; s < kRing; ++s) mbar_init(&sm.row_bar[s], kWarps);
-    if (p.C > 1) mbar_init(&sm.merge_bar, 1);
+    if (kCluster) mbar_init(&sm.merge_bar, 1);
     fence_mbar_init();
   }
   if (tid == 32) prefetch_tensormap(&rows_map);
   __syncthreads();
-  if (p.C > 1) cluster_arrive_relaxed();
+  if constexpr (kCluster) cluster_arrive_relaxed();
   // Launched as a programmatic dependent of whatever ran before on the stream:
   // CTAs may be resident early, but nothing is read before the previous grid
   // has completed and flushed.
@@ -520,9 +522,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   // dims 64 w + 16 c + j at acc[2 s + x][2 half + e] with j = 4 s + 2 x + e.
   if ((tid & 15) == 0) sm.ml[red_h] = make_float2(m_run, l_run);
   const int dim0 = warp * 64 + c * 16;
-  const int C = p.C;
+  const int C = kCluster ? p.C : 1;
   const int cl = split / C;  // partial index when kPartialOut
-  if (C == 1) {
+  if constexpr (!kCluster) {
     __syncthreads();
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -914,8 +916,11 @@ static int prepare_device(size_t smem, const int **capacity) {
       *capacity = g_cluster_capacity[dev];
       return TITAN_OK;
     }
-    void (*kernels[4])(const Params, const CUtensorMap) = {sparse_mla_kernel<false, false>, sparse_mla_kernel<true, false>,
-                                        sparse_mla_kernel<false, true>, sparse_mla_kernel<true, true>};
+    void (*kernels[8])(const Params, const CUtensorMap) = {
+        sparse_mla_kernel<false, false, false>, sparse_mla_kernel<true, false, false>,
+        sparse_mla_kernel<false, true, false>,  sparse_mla_kernel<true, true, false>,
+        sparse_mla_kernel<false, false, true>,  sparse_mla_kernel<true, false, true>,
+        sparse_mla_kernel<false, true, true>,   sparse_mla_kernel<true, true, true>};
     for (auto k : kernels) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -923,7 +928,8 @@ static int prepare_device(size_t smem, const int **capacity) {
     }
     int sms = 0, per_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sparse_mla_kernel<false, false>, kThreads, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sparse_mla_kernel<false, false, false>, kThreads, smem) !=
+            cudaSuccess ||
         per_sm < 1) {
       cudaGetLastError();
       per_sm = 1;
@@ -943,7 +949,7 @@ static int prepare_device(size_t smem, const int **capacity) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false, false>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<true, false, true>, &cfg) != cudaSuccess) {
         cudaGetLastError();  // clear a rejected query: that size is not schedulable
         n = 0;
       }
@@ -999,7 +1005,7 @@ static int max_active_clusters(int cluster_size, bool exclusive) {
     if (smem > (size_t)optin) return -1;
     // Raise the opt-in ceiling so the query is legal; launches still request
     // sizeof(Smem).
-    if (cudaFuncSetAttribute(sparse_mla_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(sparse_mla_kernel<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess) {
       cudaGetLastError();
       return -1;
@@ -1017,9 +1023,10 @@ static int max_active_clusters(int cluster_size, bool exclusive) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<false, false>, &cfg);
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, sparse_mla_kernel<true, false, true>, &cfg);
   if (exclusive)  // back to the launch setting
-    cudaFuncSetAttribute(sparse_mla_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+    cudaFuncSetAttribute(sparse_mla_kernel<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(Smem));
   if (e != cudaSuccess) {
     cudaGetLastError();
     return -1;
@@ -1187,11 +1194,15 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   cfg.numAttrs = C > 1 ? 2 : 1;
   cudaError_t e;
   if (paged != nullptr)
-    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true>, prm, rows_map)
-               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true>, prm, rows_map);
+    e = C > 1 ? (NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true, true>, prm, rows_map)
+                        : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true, true>, prm, rows_map))
+              : (NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true, false>, prm, rows_map)
+                        : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true, false>, prm, rows_map));
   else
-    e = NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, false>, prm, rows_map)
-               : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false>, prm, rows_map);
+    e = C > 1 ? (NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, false, true>, prm, rows_map)
+                        : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false, true>, prm, rows_map))
+              : (NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, false, false>, prm, rows_map)
+                        : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false, false>, prm, rows_map));
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla launch (C=%d): %s", C, cudaGetErrorString(e));
   if (NC == 1 || in_kernel_merge) return TITAN_OK;
   // Combine the NC cluster partials: 32 CTAs per (token, head group).
