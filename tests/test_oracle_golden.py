@@ -116,7 +116,9 @@ def test_mla_oracle_vs_reference_golden(case, mla_golden):
 
 
 def test_split_heuristic_restatement_table():
-    """oracle.choose_num_kv_splits on the survey's worked cases (titan_mla.py:441-449)."""
+    """oracle.choose_num_kv_splits on hand-worked cases of the reference heuristic
+    (kernels/titan_mla.py:441-449): decode at 70 and 148 SMs, B=8, T=37 (single
+    pass) and T=0."""
     assert O.choose_num_kv_splits(1, 1, 2176, 70) == 32
     assert O.choose_num_kv_splits(1, 1, 2176, 148) == 32
     assert O.choose_num_kv_splits(8, 1, 2176, 148) == 16
