@@ -29,6 +29,7 @@ static __typeof__(&titan_copy) p_copy;
 static __typeof__(&titan_store_int8) p_store_int8;
 static __typeof__(&titan_moe_align_small) p_moe_align;
 static __typeof__(&titan_convert_req_index_to_global) p_convert;
+static __typeof__(&titan_device_pointer) p_device_pointer;
 
 #define MAX_ARGS 32
 
@@ -164,13 +165,27 @@ static PyObject *py_convert(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   return PyLong_FromLong(rc);
 }
 
-/* bind(mla, mla_sem, mla_paged, copy, store_int8, moe_align, convert): entry
- * point addresses (Python ints) of the loaded library. */
+/* device_pointer(ptr) -> (status, device address): titan_device_pointer. */
+static PyObject *py_device_pointer(PyObject *self, PyObject *const *a, Py_ssize_t n) {
+  int64_t iv[MAX_ARGS];
+  double fv[MAX_ARGS];
+  UNBOUND(p_device_pointer);
+  if (parse("device_pointer", a, n, "p", iv, fv)) return NULL;
+  void *dev = NULL;
+  int rc;
+  Py_BEGIN_ALLOW_THREADS
+    rc = p_device_pointer(P(0), &dev);
+  Py_END_ALLOW_THREADS
+  return Py_BuildValue("(iK)", rc, (unsigned long long)(uintptr_t)dev);
+}
+
+/* bind(mla, mla_sem, mla_paged, copy, store_int8, moe_align, convert,
+ * device_pointer): entry point addresses (Python ints) of the loaded library. */
 static PyObject *py_bind(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   int64_t iv[MAX_ARGS];
   double fv[MAX_ARGS];
-  if (parse("bind", a, n, "ppppppp", iv, fv)) return NULL;
-  for (int k = 0; k < 7; ++k)
+  if (parse("bind", a, n, "pppppppp", iv, fv)) return NULL;
+  for (int k = 0; k < 8; ++k)
     if (iv[k] == 0) {
       PyErr_SetString(PyExc_ValueError, "bind: null entry point");
       return NULL;
@@ -182,6 +197,7 @@ static PyObject *py_bind(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   p_store_int8 = (__typeof__(p_store_int8))P(4);
   p_moe_align = (__typeof__(p_moe_align))P(5);
   p_convert = (__typeof__(p_convert))P(6);
+  p_device_pointer = (__typeof__(p_device_pointer))P(7);
   Py_RETURN_NONE;
 }
 
@@ -194,6 +210,7 @@ static PyMethodDef methods[] = {
     {"store_int8", (PyCFunction)(void (*)(void))py_store_int8, METH_FASTCALL, "titan_store_int8"},
     {"moe_align", (PyCFunction)(void (*)(void))py_moe_align, METH_FASTCALL, "titan_moe_align_small"},
     {"convert", (PyCFunction)(void (*)(void))py_convert, METH_FASTCALL, "titan_convert_req_index_to_global"},
+    {"device_pointer", (PyCFunction)(void (*)(void))py_device_pointer, METH_FASTCALL, "titan_device_pointer"},
     {NULL, NULL, 0, NULL},
 };
 

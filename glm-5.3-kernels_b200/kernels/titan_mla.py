@@ -14,7 +14,6 @@ last CTA to finish (arrival counters).
 528 bytes/token: 512 signed INT8 values followed by 1 FP32 scale + 12 zero bytes.
 """
 
-import ctypes
 import functools
 
 import torch
@@ -226,10 +225,9 @@ def _destination(out, dev, shape):
         assert out.get_device() == dev, "out must be on q's device"
         return out.data_ptr()
     assert out.is_pinned(), "a host `out` must be pinned memory (tensor.pin_memory())"
-    ptr = ctypes.c_void_p()
-    _native.check(_native.load().titan_device_pointer(out.data_ptr(), ctypes.byref(ptr)),
-                  "triton_mla_sparse_attention(out=)")
-    return ptr.value
+    rc, ptr = _native.entry().device_pointer(out.data_ptr())
+    _native.check(rc, "triton_mla_sparse_attention(out=)")
+    return ptr
 
 
 def triton_mla_sparse_attention(

@@ -36,6 +36,7 @@ _HOT = {
     "store_int8": "titan_store_int8",
     "moe_align": "titan_moe_align_small",
     "convert": "titan_convert_req_index_to_global",
+    "device_pointer": "titan_device_pointer",
 }
 
 _i64 = ctypes.c_int64
@@ -123,10 +124,17 @@ def _load_pybind(lib):
     return mod
 
 
+def _ctypes_device_pointer(ptr):
+    out = ctypes.c_void_p()
+    rc = load().titan_device_pointer(ptr, ctypes.byref(out))
+    return rc, out.value or 0
+
+
 def entry():
     """The hot launchers (`mla`, `mla_sem`, `mla_paged`, `copy`, `store_int8`,
-    `moe_align`, `convert`), positional arguments as in include/titan_b200.h,
-    returning the status: the fast-call module, else the ctypes functions."""
+    `moe_align`, `convert`; positional arguments as in include/titan_b200.h,
+    returning the status) and `device_pointer(ptr) -> (status, address)`: the
+    fast-call module, else the same calls through ctypes."""
     global _entry
     if _entry is not None:
         return _entry
@@ -134,8 +142,11 @@ def entry():
     with _lock:
         if _entry is None:
             fast = None if os.environ.get("TITAN_B200_CTYPES_ONLY") else _load_pybind(lib)
-            _entry = fast if fast is not None else types.SimpleNamespace(
-                **{name: getattr(lib, c_name) for name, c_name in _HOT.items()})
+            if fast is None:
+                calls = {name: getattr(lib, c_name) for name, c_name in _HOT.items()}
+                calls["device_pointer"] = _ctypes_device_pointer
+                fast = types.SimpleNamespace(**calls)
+            _entry = fast
     return _entry
 
 
