@@ -460,7 +460,7 @@ def run_ours(args, dist):
     from kernels.titan_io import copy_ as staged_copy
 
     def e2e_step(k):
-        staged_copy(landing, staging[k % sets])
+        staged_copy(landing, staging[k % sets], src_ready=True)
         attn(qd, kvs[k % REPLICAS], idd, SM_SCALE, sm_count=sms, out=out_host[k % sets])
 
     def e2e_step_copy_engine(k):

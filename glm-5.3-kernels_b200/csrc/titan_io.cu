@@ -45,16 +45,20 @@ static void *device_view(const void *p, const char *what) {
   }
 }
 
-// grid-stride copy of n16 16-byte words, then the byte tail (bytes % 16) by
-// block 0.  `vec` = both pointers 16-byte aligned; otherwise bytes only.
+// grid-stride copy of n16 16-byte words, then the byte tail (bytes % 16).
+// `vec` = both pointers 16-byte aligned; otherwise bytes only.  The
+// destination may still be read by the previous grid on the stream (e.g. the
+// reader of the last call's landing buffer), so nothing is stored before the
+// programmatic-dependency wait.  With `early_read` (the source is not written
+// by earlier work on the stream) the first round of loads is issued before
+// that wait, overlapping the source's latency with the previous grid's tail.
 __global__ void __launch_bounds__(kCopyThreads)
-    staged_copy_kernel(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src, int64_t bytes, bool vec) {
-  // The destination may still be read by the previous grid on the stream
-  // (e.g. the reader of the last call's landing buffer).
-  pdl_wait_primary();
-  pdl_launch_dependents();
+    staged_copy_kernel(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src, int64_t bytes, bool vec,
+                       bool early_read) {
   const int64_t nthreads = (int64_t)gridDim.x * kCopyThreads;
   const int64_t tid = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x;
+  pdl_launch_dependents();  // the next kernel may start its own set-up; it still waits for this grid
+  if (!early_read) pdl_wait_primary();
   int64_t done = 0;
   if (vec) {
     const int64_t n16 = bytes >> 4;
@@ -67,6 +71,7 @@ __global__ void __launch_bounds__(kCopyThreads)
         const int64_t i = base + u * nthreads + tid;
         if (i < n16) v[u] = s[i];
       }
+      if (early_read && base == 0) pdl_wait_primary();
 #pragma unroll
       for (int u = 0; u < kCopyUnroll; ++u) {
         const int64_t i = base + u * nthreads + tid;
@@ -75,6 +80,7 @@ __global__ void __launch_bounds__(kCopyThreads)
     }
     done = n16 << 4;
   }
+  if (early_read && done == 0) pdl_wait_primary();  // no vector round ran
   for (int64_t i = done + tid; i < bytes; i += nthreads) dst[i] = src[i];
 }
 
@@ -92,7 +98,12 @@ extern "C" int titan_device_pointer(const void *ptr, void **device_ptr_out) {
 }
 
 extern "C" int titan_copy(void *dst, const void *src, int64_t bytes, titan_stream_t stream) {
+  return titan_copy_ex(dst, src, bytes, 0, stream);
+}
+
+extern "C" int titan_copy_ex(void *dst, const void *src, int64_t bytes, int flags, titan_stream_t stream) {
   using namespace titan;
+  if (flags & ~TITAN_COPY_SRC_READY) return fail(TITAN_ERR_INVALID_ARGUMENT, "copy: unknown flags 0x%x", flags);
   if (bytes < 0) return fail(TITAN_ERR_INVALID_ARGUMENT, "copy: negative size");
   if (bytes == 0) return TITAN_OK;
   if (dst == nullptr || src == nullptr) return fail(TITAN_ERR_INVALID_ARGUMENT, "copy: null pointer");
@@ -118,7 +129,8 @@ extern "C" int titan_copy(void *dst, const void *src, int64_t bytes, titan_strea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, staged_copy_kernel, d8, s8, bytes, vec);
+  const bool early_read = (flags & TITAN_COPY_SRC_READY) != 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, staged_copy_kernel, d8, s8, bytes, vec, early_read);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "copy launch: %s", cudaGetErrorString(e));
   return TITAN_OK;
 }

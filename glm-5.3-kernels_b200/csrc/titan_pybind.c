@@ -25,7 +25,7 @@
 static __typeof__(&titan_mla_sparse_attention) p_mla;
 static __typeof__(&titan_mla_sparse_attention_sem) p_mla_sem;
 static __typeof__(&titan_mla_sparse_attention_paged) p_mla_paged;
-static __typeof__(&titan_copy) p_copy;
+static __typeof__(&titan_copy_ex) p_copy;
 static __typeof__(&titan_store_int8) p_store_int8;
 static __typeof__(&titan_moe_align_small) p_moe_align;
 static __typeof__(&titan_convert_req_index_to_global) p_convert;
@@ -118,10 +118,10 @@ static PyObject *py_copy(PyObject *self, PyObject *const *a, Py_ssize_t n) {
   int64_t iv[MAX_ARGS];
   double fv[MAX_ARGS];
   UNBOUND(p_copy);
-  if (parse("copy", a, n, "ppip", iv, fv)) return NULL;
+  if (parse("copy", a, n, "ppiip", iv, fv)) return NULL;
   int rc;
   Py_BEGIN_ALLOW_THREADS
-    rc = p_copy(P(0), P(1), I(2), (titan_stream_t)P(3));
+    rc = p_copy(P(0), P(1), I(2), (int)I(3), (titan_stream_t)P(4));
   Py_END_ALLOW_THREADS
   return PyLong_FromLong(rc);
 }
@@ -206,7 +206,7 @@ static PyMethodDef methods[] = {
     {"mla", (PyCFunction)(void (*)(void))py_mla, METH_FASTCALL, "titan_mla_sparse_attention"},
     {"mla_sem", (PyCFunction)(void (*)(void))py_mla_sem, METH_FASTCALL, "titan_mla_sparse_attention_sem"},
     {"mla_paged", (PyCFunction)(void (*)(void))py_mla_paged, METH_FASTCALL, "titan_mla_sparse_attention_paged"},
-    {"copy", (PyCFunction)(void (*)(void))py_copy, METH_FASTCALL, "titan_copy"},
+    {"copy", (PyCFunction)(void (*)(void))py_copy, METH_FASTCALL, "titan_copy_ex"},
     {"store_int8", (PyCFunction)(void (*)(void))py_store_int8, METH_FASTCALL, "titan_store_int8"},
     {"moe_align", (PyCFunction)(void (*)(void))py_moe_align, METH_FASTCALL, "titan_moe_align_small"},
     {"convert", (PyCFunction)(void (*)(void))py_convert, METH_FASTCALL, "titan_convert_req_index_to_global"},

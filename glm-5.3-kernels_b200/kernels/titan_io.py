@@ -18,12 +18,15 @@ except ImportError:
     import titan_native as _native
 
 
-def copy_(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+def copy_(dst: torch.Tensor, src: torch.Tensor, *, src_ready: bool = False) -> torch.Tensor:
     """dst <- src, bytewise, by a kernel on the current stream of the CUDA side.
 
     Both tensors contiguous with the same number of bytes; one of them (or
     both) on a CUDA device, the other may be PINNED host memory.  Ordered
-    after the stream's previous work; returns dst.
+    after the stream's previous work; returns dst.  `src_ready=True` declares
+    that no earlier work on the stream writes `src` (host-written input, say):
+    the kernel then starts reading it before the preceding kernel has
+    finished, and only its stores wait.
     """
     if not (dst.is_contiguous() and src.is_contiguous()):
         raise ValueError("copy_: tensors must be contiguous")
@@ -42,6 +45,6 @@ def copy_(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
     if nbytes == 0:
         return dst
     with _native.on_device(side.device):
-        _native.check(_native.entry().copy(dst.data_ptr(), src.data_ptr(), nbytes, _native.stream_of(side)),
-                      "titan_io.copy_")
+        _native.check(_native.entry().copy(dst.data_ptr(), src.data_ptr(), nbytes, 1 if src_ready else 0,
+                                           _native.stream_of(side)), "titan_io.copy_")
     return dst

@@ -32,7 +32,7 @@ _HOT = {
     "mla": "titan_mla_sparse_attention",
     "mla_sem": "titan_mla_sparse_attention_sem",
     "mla_paged": "titan_mla_sparse_attention_paged",
-    "copy": "titan_copy",
+    "copy": "titan_copy_ex",
     "store_int8": "titan_store_int8",
     "moe_align": "titan_moe_align_small",
     "convert": "titan_convert_req_index_to_global",
@@ -78,6 +78,7 @@ SIGNATURES = {
     "titan_moe_align_small": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _int, _vp]),
     "titan_device_error": (_int, [ctypes.POINTER(_int), _int, _vp]),
     "titan_copy": (_int, [_vp, _vp, _i64, _vp]),
+    "titan_copy_ex": (_int, [_vp, _vp, _i64, _int, _vp]),
     "titan_device_pointer": (_int, [_vp, ctypes.POINTER(_vp)]),
 }
 

@@ -254,6 +254,12 @@ int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int64_t num_ro
  * reader stores its result straight into host memory.
  */
 int titan_copy(void *dst, const void *src, int64_t bytes, titan_stream_t stream);
+/* titan_copy with flags.  TITAN_COPY_SRC_READY: no earlier work on the stream
+ * writes src (e.g. host-written input in pinned memory), so the kernel issues
+ * its first round of loads before waiting for the preceding kernel, hiding
+ * the source's latency behind that kernel's tail; stores still wait. */
+#define TITAN_COPY_SRC_READY 1
+int titan_copy_ex(void *dst, const void *src, int64_t bytes, int flags, titan_stream_t stream);
 int titan_device_pointer(const void *ptr, void **device_ptr_out);
 
 /*

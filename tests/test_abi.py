@@ -65,11 +65,12 @@ def test_fast_call_binding_is_built_and_bound(native_lib):
     assert b"num_routes" in native_lib.titan_last_error()
     assert e.mla(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, 1, 16, 0.1, 0, None, 0, None) == 1
     assert e.store_int8(None, 512, None, 1, 256, 0, 0, None, 1, 0, None) == 0
-    assert e.copy(None, None, 0, None) == 0
-    assert e.copy(None, None, 16, None) == 1 and b"null" in native_lib.titan_last_error()
+    assert e.copy(None, None, 0, 0, None) == 0
+    assert e.copy(None, None, 16, 0, None) == 1 and b"null" in native_lib.titan_last_error()
+    assert e.copy(None, None, 16, 2, None) == 1 and b"flags" in native_lib.titan_last_error()
     with pytest.raises(TypeError):
         e.mla_sem(*([0] * 20))                   # one argument short
     with pytest.raises(TypeError):
-        e.copy(0, 0, 1.5, 0)                     # float where an int64 belongs
+        e.copy(0, 0, 1.5, 0, 0)                  # float where an int64 belongs
     with pytest.raises(TypeError):
         e.store_int8("x", 512, None, 1, 256, 0, 0, None, 1, 0, None)

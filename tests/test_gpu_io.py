@@ -30,9 +30,12 @@ def test_copy_round_trip_bit_exact(nbytes, native_lib, cuda_device):
     dev2 = torch.empty_like(dev)
     copy_(dev2, dev)        # device -> device
     copy_(back, dev2)       # device -> host
+    dev3 = torch.empty_like(dev)
+    copy_(dev3, host, src_ready=True)   # host-written source: loads start before the previous kernel ends
     torch.cuda.synchronize()
     assert torch.equal(dev.cpu(), host)
     assert torch.equal(back, host)
+    assert torch.equal(dev3.cpu(), host)
 
 
 @pytest.mark.parametrize("shift", [1, 3, 8, 15])
@@ -63,6 +66,8 @@ def test_copy_rejects_pageable_and_overlap(native_lib, cuda_device):
     assert rc == 1 and b"pageable" in lib.titan_last_error()
     rc = lib.titan_copy(dev.data_ptr() + 8, dev.data_ptr(), 32, titan_native.stream_of(dev))
     assert rc == 1 and b"overlap" in lib.titan_last_error()
+    rc = lib.titan_copy_ex(dev.data_ptr(), dev.data_ptr() + 32, 16, 4, titan_native.stream_of(dev))
+    assert rc == 1 and b"flags" in lib.titan_last_error()
     p = ctypes.c_void_p()
     assert lib.titan_device_pointer(pageable.data_ptr(), ctypes.byref(p)) == 1
     pinned = torch.zeros(64, dtype=torch.uint8).pin_memory()
@@ -94,3 +99,32 @@ def test_mla_pinned_host_output_matches(tokens, splits, native_lib, cuda_device)
     assert torch.equal(dev_out.view(torch.int16), ref.view(torch.int16))
     with pytest.raises(AssertionError):
         attn(q, kv, idx, 512 ** -0.5, out=torch.empty(tokens, 16, 512, dtype=torch.bfloat16))  # pageable
+
+
+def test_src_ready_copy_waits_for_the_previous_reader(native_lib, cuda_device):
+    """With src_ready the copy's loads may start early, but its stores into a
+    landing buffer still wait for the kernel reading that buffer: a chain of
+    copy -> attention steps on one landing buffer gives every step's own result."""
+    from kernels.titan_io import copy_
+    from kernels.titan_kv import store_int8
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    g = torch.Generator().manual_seed(5)
+    rows, steps = 8192, 12
+    cache = torch.empty(rows, 1, 528, dtype=torch.int8, device=cuda_device)
+    store_int8(torch.randn(rows, 512, generator=g).to(torch.bfloat16).to(cuda_device), cache,
+               torch.arange(rows, device=cuda_device))
+    q = torch.randn(steps, 1, 16, 512, generator=g).to(torch.bfloat16)
+    idx = torch.randint(-8, rows, (steps, 1, 1, 2176), generator=g, dtype=torch.int32)
+    staging = torch.cat([q.reshape(steps, -1).view(torch.uint8), idx.reshape(steps, -1).view(torch.uint8)], 1)
+    staging = staging.pin_memory()
+    nq = q[0].numel() * 2
+    landing = torch.empty(staging.shape[1], dtype=torch.uint8, device=cuda_device)
+    outs = torch.empty(steps, 1, 16, 512, dtype=torch.bfloat16).pin_memory()
+    for k in range(steps):
+        copy_(landing, staging[k], src_ready=True)
+        attn(landing[:nq].view(torch.bfloat16).view(1, 16, 512), cache, landing[nq:].view(torch.int32).view(1, 1, 2176),
+             0.05, out=outs[k])
+    torch.cuda.synchronize()
+    for k in range(steps):
+        ref = attn(q[k].to(cuda_device), cache, idx[k].to(cuda_device), 0.05)
+        assert torch.equal(outs[k].view(torch.int16), ref.cpu().view(torch.int16)), k
