@@ -623,6 +623,33 @@ def run_ours(args, dist):
         moe[f"B{B}_zipf_in_graph_us"] = statistics.median(samples)
         gz.reset()
     secondary["moe_align_graph_replay"] = moe
+
+    # ---- prefill split align (the consumer side of config 5 at whole-expert
+    # prefill): M = 2304 tokens x top-8 over 288 experts, uniform and
+    # Zipf(1.1); 100 calls on one buffer set inside one graph.
+    from kernels import titan_moe_split_align as split_mod
+    split = {}
+    for M in (2304, 8192):
+        sbuf = split_mod.buffers(M * 8, 288, dev)
+        for dist_name in ("uniform", "zipf"):
+            if dist_name == "uniform":
+                sids = torch.randint(0, 288, (M, 8), generator=gm, dtype=torch.int32)
+            else:
+                zw = (torch.arange(1, 289, dtype=torch.float64) ** -1.1)
+                sids = torch.multinomial(zw, M * 8, replacement=True, generator=gm).view(M, 8).to(torch.int32)
+            sids = sids.to(dev)
+            gs, _ = capture(lambda: [split_mod.split_align(sids, 288, sbuf) for _ in range(100)])
+            gs.replay()
+            samples = []
+            for _ in range(5):
+                a.record()
+                gs.replay()
+                b.record()
+                torch.cuda.synchronize()
+                samples.append(a.elapsed_time(b) * 1000 / 100)
+            split[f"M{M}_{dist_name}_in_graph_us"] = statistics.median(samples)
+            gs.reset()
+    secondary["moe_split_align"] = split
     clocks = sampler.stop()
     dist.barrier()
 

@@ -3,6 +3,7 @@
 #include "titan_abi.cu"
 #include "titan_kv.cu"
 #include "titan_moe_align.cu"
+#include "titan_moe_split_align.cu"
 #include "titan_mla.cu"
 #include "titan_index.cu"
 #include "titan_io.cu"

@@ -8,6 +8,7 @@
  *   titan_store_int8              replaces kernels/titan_kv.py:23-28
  *   titan_mla_sparse_attention    replaces kernels/titan_mla.py:452-581
  *   titan_moe_align_small         replaces kernels/titan_moe_align.py:49-81
+ *   titan_moe_split_align         replaces profiles/sm74/titan_prefill/moe_split_align.py:204-223
  *   titan_convert_req_index_to_global / titan_mla_sparse_attention_paged
  *                                 replace the index conversion before the
  *                                 reader, integration/titan_backend.py:48-54
@@ -236,6 +237,35 @@ int titan_mla_sparse_attention_noalloc(const void *q, int64_t q_stride_token, in
 int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int64_t num_routes,
                           int32_t *sorted_ids, int32_t *expert_ids, int32_t *postpad,
                           int num_warps, titan_stream_t stream);
+
+/*
+ * Split MoE block alignment for whole-expert prefill: the routed rows sorted
+ * by expert into four block lists, block sizes {64, 48, 32, 16}, one Marlin
+ * launch per list.  Replaces `split_align(topk_ids, E, buf)`,
+ * profiles/sm74/titan_prefill/moe_split_align.py:204-223 (kernels :44-169).
+ * One launch of one CTA; no scratch memory.
+ *
+ *   topk_ids     int32 (ids_is_int64 = 0) or int64 (1), num_routes = M * topk
+ *                entries, contiguous; int64 ids are narrowed to int32 first
+ *   num_experts  E in [1, TITAN_SPLIT_ALIGN_MAX_EXPERTS]; ids outside [0, E) are dropped
+ *   cover_tab    int32 [cover_rows][4] on the device: blocks of each size in the
+ *                cheapest cover of r rows (moe_split_align.py:172-185);
+ *                cover_rows >= num_routes + 1
+ *   t_max        capacity the lists were allocated for, num_routes <= t_max:
+ *   sorted_ids   host array of 4 device pointers, list k int32 [t_max + B_k * E]
+ *   expert_ids   host array of 4 device pointers, list k int32 [(t_max + B_k * E) / B_k + 1]
+ *   ntpp         int32 [4]: rows of each list (padding included)
+ *
+ * Padded entries of sorted_ids hold num_routes; entries beyond what the
+ * algorithm writes are left untouched.  Calls sharing lists must be ordered.
+ */
+#define TITAN_SPLIT_ALIGN_MAX_EXPERTS 1024
+int titan_moe_split_align(const void *topk_ids, int ids_is_int64, int64_t num_routes, int64_t num_experts,
+                          const int32_t *cover_tab, int64_t cover_rows, int64_t t_max,
+                          int32_t *const *sorted_ids, int32_t *const *expert_ids, int32_t *ntpp,
+                          titan_stream_t stream);
+/* Dynamic shared memory the split-align kernel uses for num_experts experts. */
+int64_t titan_moe_split_align_smem_bytes(int64_t num_experts);
 
 /*
  * Host <-> device staging (no counterpart in the reference, whose callers keep

@@ -203,6 +203,90 @@ def moe_align_small_loops(flat):
             experts + [-1] * (count - len(experts)), [postpad])
 
 
+# ------------------------------------------------ MoE split align (prefill)
+SPLIT_SIZES = (64, 48, 32, 16)                        # moe_split_align.py:39
+SPLIT_COST = {64: 33.3, 48: 26.4, 32: 20.3, 16: 14.1}  # moe_split_align.py:40
+SPLIT_UNWRITTEN = -2  # marker for list entries the algorithm leaves untouched
+
+
+def split_cover_table(max_rows):
+    """[max_rows + 1, 4] int32: blocks of each size in SPLIT_SIZES of the cheapest
+    cover of r rows (profiles/sm74/titan_prefill/moe_split_align.py:172-185).
+
+    Dynamic programme over r in float64: cost(r) = min over sizes s of
+    COST[s] + cost(max(r - s, 0)), ties to the smaller (cost, size) pair.
+    """
+    best = [0.0] * (max_rows + 1)
+    choice = [0] * (max_rows + 1)
+    for r in range(1, max_rows + 1):
+        best[r], choice[r] = min((SPLIT_COST[s] + best[max(r - s, 0)], s) for s in SPLIT_SIZES)
+    table = np.zeros((max_rows + 1, len(SPLIT_SIZES)), dtype=np.int32)
+    for r in range(1, max_rows + 1):
+        table[r] = table[max(r - choice[r], 0)]
+        table[r, SPLIT_SIZES.index(choice[r])] += 1
+    return table
+
+
+def moe_split_align(routes, num_experts, t_max=None, table=None):
+    """Split block alignment of profiles/sm74/titan_prefill/moe_split_align.py:204-223.
+
+    routes: integer expert ids of the T = M * topk routed rows (any shape;
+    int64 ids are narrowed to int32 first, as :207-209 does).  Returns a list,
+    one entry per block size in SPLIT_SIZES, of (block_size, sorted_ids,
+    expert_ids, ntpp) where sorted_ids / expert_ids are the full buffers of
+    :196-199 (t_max + B*E and (t_max + B*E) // B + 1 entries) with entries the
+    algorithm does not write left at SPLIT_UNWRITTEN, and ntpp the list's row
+    count.  Steps:
+      plan (:73-99)    r_e = valid rows of expert e; n_k = table[r_e, k];
+                       rows_k = n_k * B_k; off_k = exclusive prefix over
+                       experts; rank boundaries lo1, lo2, lo3; ntpp_k = sum rows_k.
+      fill (:102-135)  the last non-empty list of an expert pads its tail with
+                       the sentinel T; every list gets its blocks' expert id.
+      scatter (:138-169) row j of expert e with stable rank q (flat order) goes
+                       to the list whose rank range holds q, at off + q - lo.
+    """
+    flat = np.asarray(routes).reshape(-1).astype(np.int64)
+    flat = ((flat + 2 ** 31) % 2 ** 32 - 2 ** 31)  # ids.to(torch.int32) wraps
+    T = flat.size
+    E = int(num_experts)
+    t_max = T if t_max is None else int(t_max)
+    assert 0 < T <= t_max
+    table = split_cover_table(t_max) if table is None else np.asarray(table)
+    valid = (flat >= 0) & (flat < E)
+    r = np.bincount(flat[valid], minlength=E).astype(np.int64)
+    rows = np.stack([table[r, k].astype(np.int64) * b for k, b in enumerate(SPLIT_SIZES)])
+    off = np.cumsum(rows, axis=1) - rows
+    lo1, lo2, lo3 = rows[0], rows[0] + rows[1], rows[0] + rows[1] + rows[2]
+    sorted_ids = [np.full(t_max + b * E, SPLIT_UNWRITTEN, dtype=np.int32) for b in SPLIT_SIZES]
+    expert_ids = [np.full((t_max + b * E) // b + 1, SPLIT_UNWRITTEN, dtype=np.int32) for b in SPLIT_SIZES]
+    for e in range(E):
+        b3 = SPLIT_SIZES[3]
+        hi3 = lo3[e] + (r[e] + b3 - 1 - lo3[e]) // b3 * b3 if r[e] > lo3[e] else lo3[e]
+        last3 = hi3 > lo3[e]
+        last2 = lo3[e] > lo2[e] and not last3
+        last1 = lo2[e] > lo1[e] and lo3[e] == lo2[e] and not last3
+        last0 = lo1[e] > 0 and lo2[e] == lo1[e] and lo3[e] == lo2[e] and not last3
+        spans = ((0, lo1[e], last0), (lo1[e], lo2[e], last1), (lo2[e], lo3[e], last2), (lo3[e], hi3, last3))
+        for k, (lo, hi, last) in enumerate(spans):
+            b = SPLIT_SIZES[k]
+            n = hi - lo
+            pad = hi - r[e] if last else 0
+            start = off[k, e] + n - pad
+            for j in range(min(max(pad, 0), 64)):  # :107-108, pad < 64 by construction
+                sorted_ids[k][start + j] = T
+            for blk in range(n // b):
+                expert_ids[k][off[k, e] // b + blk] = e
+    seen = np.zeros(E, dtype=np.int64)
+    for j in np.nonzero(valid)[0]:
+        e = flat[j]
+        q = seen[e]
+        seen[e] += 1
+        k = 3 if q >= lo3[e] else 2 if q >= lo2[e] else 1 if q >= lo1[e] else 0
+        base = (0, lo1[e], lo2[e], lo3[e])[k]
+        sorted_ids[k][off[k, e] + q - base] = j
+    return [(b, sorted_ids[k], expert_ids[k], int(rows[k].sum())) for k, b in enumerate(SPLIT_SIZES)]
+
+
 # ------------------------------------------------------ paged index conversion
 def convert_req_index_to_global(req_id, block_table, token_indices, block_size, block_stride_rows=None):
     """Request-local top-k positions -> global cache rows (int32 [T, topk]).

@@ -51,6 +51,23 @@ def test_invalid_arguments_rejected_on_host(native_lib):
     assert native_lib.titan_store_int8(None, 512, None, 1, 256, 0, 0, None, 1, 0, None) == 0  # nothing to do
 
 
+def test_split_align_invalid_arguments_rejected_on_host(native_lib):
+    """Host validation of titan_moe_split_align: routes within (0, t_max], expert
+    count within the shared-memory limit, a cover table of T + 1 rows, pointers."""
+    lists = (ctypes.c_void_p * 4)(16, 16, 16, 16)
+    split = native_lib.titan_moe_split_align
+    assert split(16, 0, 0, 288, 16, 1, 8, lists, lists, 16, None) == 1
+    assert b"num_routes" in native_lib.titan_last_error()
+    assert split(16, 0, 9, 288, 16, 10, 8, lists, lists, 16, None) == 1   # T > t_max
+    assert split(16, 0, 8, 1025, 16, 9, 8, lists, lists, 16, None) == 1
+    assert b"num_experts" in native_lib.titan_last_error()
+    assert split(16, 0, 8, 288, 16, 8, 8, lists, lists, 16, None) == 1    # table too short
+    assert b"cover table" in native_lib.titan_last_error()
+    assert split(None, 0, 8, 288, 16, 9, 8, lists, lists, 16, None) == 1
+    assert b"null" in native_lib.titan_last_error()
+    assert native_lib.titan_moe_split_align_smem_bytes(288) == 41 * 288 * 4
+
+
 def test_fast_call_binding_is_built_and_bound(native_lib):
     """The hot launchers go through the CPython fast-call module (bound to the
     loaded library), which validates argument count and types before calling."""

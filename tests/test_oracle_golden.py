@@ -140,3 +140,47 @@ def test_index_conversion_oracle_matches_vllm_goldens():
         want = gold[f"{case.name}__out"]
         assert np.array_equal(got, want), case.name
         assert (want == -1).any() and (want >= 0).any()
+
+
+def _split_golden_cases():
+    golden = np.load(f"{GOLDEN}/split_align_golden.npz")
+    for name in golden["names"]:
+        E, t_max = (int(v) for v in golden[f"{name}/meta"])
+        yield str(name), golden[f"{name}/routes"], E, t_max, golden
+
+
+def test_split_align_cover_table_is_cost_optimal():
+    """Every r's cover reaches r rows, pads less than its smallest block and costs
+    no more than any single-size cover (profiles/sm74/titan_prefill/moe_split_align.py:8-20)."""
+    table = O.split_cover_table(600)
+    for r in range(1, 601):
+        n = table[r]
+        covered = int(sum(int(c) * b for c, b in zip(n, O.SPLIT_SIZES)))
+        smallest = min(b for c, b in zip(n, O.SPLIT_SIZES) if c)
+        assert r <= covered < r + smallest
+        cost = sum(int(c) * O.SPLIT_COST[b] for c, b in zip(n, O.SPLIT_SIZES))
+        for b in O.SPLIT_SIZES:
+            assert cost <= -(-r // b) * O.SPLIT_COST[b] + 1e-9
+
+
+def test_split_align_oracle_bit_exact():
+    """The split-align oracle equals the reference's five Triton kernels (run by the
+    interpreter, tests/golden/make_split_align_golden.py) on whole buffers,
+    untouched entries included: uniform, Zipf, invalid, int64-wrapped ids, one
+    expert, a single route and three experts."""
+    sizes = 0
+    for name, routes, E, t_max, golden in _split_golden_cases():
+        lists = O.moe_split_align(routes, E, t_max)
+        assert [n for _, _, _, n in lists] == golden[f"{name}/ntpp"].tolist(), name
+        for k, (bs, s, e, _) in enumerate(lists):
+            assert bs == int(golden["sizes"][k])
+            assert np.array_equal(s, golden[f"{name}/sorted{k}"]), (name, k)
+            assert np.array_equal(e, golden[f"{name}/experts{k}"]), (name, k)
+            sizes |= 1 << k if lists[k][3] else 0
+    assert sizes == 0b1111  # every block size holds rows in some case
+
+
+def test_split_align_product_cover_table_matches_oracle():
+    from kernels import titan_moe_split_align as S
+    assert np.array_equal(S.cover_table(3000).numpy(), O.split_cover_table(3000))
+    assert S.SIZES == O.SPLIT_SIZES and S.COST == O.SPLIT_COST
