@@ -30,8 +30,9 @@ platform, so single-call latency (`secondary.isolated_call_us`) is coarse.
 
 Secondary measurements ride along in "secondary": store_int8 cache fill
 (config 2 fill, 408.9 MB), B=8 decode sharded over ranks (config 3),
-prefill-shaped T=4096 (config 4, sharded over ranks) and MoE align B1/2/4/8
-(config 5).
+prefill-shaped T=4096 (config 4, sharded over ranks), MoE align B1/2/4/8
+(config 5) and the prefill split align of the MoE layer (M = 2304 and 8192
+tokens x top-8, 288 experts, uniform and Zipf(1.1) routes).
 
 --impl reference times the reference algorithm's CPU restatement (oracle/,
 the only CPU implementation of this path; the reference ships Triton GPU
@@ -769,12 +770,21 @@ def run_profile(args):
     from kernels.titan_mla import triton_mla_sparse_attention as attn
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    n = args.warmup + args.steps
+    if args.profile == "split_align":  # M = 2304 tokens x top-8, 288 uniform experts
+        from kernels import titan_moe_split_align as split_mod
+        g = torch.Generator().manual_seed(1)
+        ids = torch.randint(0, 288, (2304, 8), generator=g, dtype=torch.int32).to(dev)
+        sbuf = split_mod.buffers(2304 * 8, 288, dev)
+        for _ in range(n):
+            split_mod.split_align(ids, 288, sbuf)
+        torch.cuda.synchronize()
+        return
     lat = latents(KV_ROWS, 1234, dev)
     cache = torch.zeros(KV_ROWS // BLOCK, BLOCK, ROW_BYTES, dtype=torch.int8, device=dev)
     slots = torch.arange(KV_ROWS, device=dev)
     store_int8(lat, cache, slots)
     kv = cache.view(KV_ROWS, 1, ROW_BYTES)
-    n = args.warmup + args.steps
     if args.profile == "store_int8":
         for _ in range(n):
             store_int8(lat, cache, slots)
@@ -817,7 +827,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1"), default=None,
+    ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1", "split_align"),
+                    default=None,
                     help="run only this workload (warmup + steps calls) as an ncu target; prints nothing")
     args = ap.parse_args()
     rank, world, local_rank = env_rank()

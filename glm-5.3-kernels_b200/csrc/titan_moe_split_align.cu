@@ -20,17 +20,19 @@
 // threads where the device holds such a cluster, else 8) instead of five
 // kernels with a global histogram.  Warp w of the cluster (CTA-major order)
 // owns the w-th contiguous slice of the routes; its expert counts live in a
-// private shared-memory histogram (no atomics: match-any peer masks give
-// in-group ranks, the group leader adds the popcount).  Each CTA sums its
+// private shared-memory histogram (no atomics: peer masks of equal ids,
+// built from one ballot per id bit, give in-group ranks; the group leader
+// adds the popcount).  Each CTA sums its
 // warps' counts per expert and publishes the totals in its shared memory;
 // after a cluster barrier every CTA reads the lower CTAs' totals through
 // distributed shared memory, so prefix (CTA) + prefix (warp) is each slice's
 // stable-rank base and the sum over CTAs is r_e.  Every CTA computes the
 // plan (a CTA-wide scan of four counters per expert, E <= 1024) itself; the
-// fill takes one warp per expert across the cluster; a second cluster barrier
-// orders the fill before the scatter (as the reference's launches are
-// ordered) and keeps every CTA resident until its peers' remote reads are
-// done.  Each lane loads eight groups of route ids before using them.
+// fill takes one warp per expert across the cluster.  Fill and scatter need
+// no barrier between them (they write disjoint entries); a split cluster
+// barrier (arrive after the last remote read, wait at the end) keeps every
+// CTA resident until its peers' remote reads are done.  Each lane loads eight
+// groups of route ids before using them.
 #include "titan_common.cuh"
 
 namespace titan {
@@ -39,9 +41,11 @@ constexpr int kSplitThreads = 1024;
 constexpr int kSplitWarps = kSplitThreads / 32;
 constexpr int kSplitMaxExperts = TITAN_SPLIT_ALIGN_MAX_EXPERTS;
 constexpr int kSplitBatch = 8;  // route groups loaded per lane before use
-// Shared memory: 32 warp histograms + CTA total + r + 4 offsets + 3 rank
-// boundaries per expert.
-constexpr int kSplitWordsPerExpert = kSplitWarps + 1 + 1 + 4 + 3;
+// Shared memory: 32 warp histograms (rows of E | 1 words: an odd stride, so
+// one expert's column is read without bank conflicts) + per expert the CTA
+// total, r, the lower CTAs' rows, 4 list offsets and 3 rank boundaries.
+constexpr int kSplitWordsPerExpert = 1 + 1 + 1 + 4 + 3;
+__host__ __device__ constexpr int split_hist_stride(int E) { return E | 1; }
 constexpr int kSplitClusterMax = 16;
 
 // Full cluster barrier: release this CTA's prior memory operations, acquire
@@ -64,6 +68,20 @@ struct SplitLists {
   int32_t *s0, *s1, *s2, *s3;
   int32_t *e0, *e1, *e2, *e3;
 };
+
+// Lanes of the warp holding the same valid expert id as this lane (e >= 0),
+// else this lane alone: the peer mask of a match-any over the ids, built from
+// one ballot per id bit (nbits = bits of E - 1), which on this GPU is far
+// cheaper than match-any over ~30 distinct values.
+__device__ __forceinline__ unsigned split_peers(int e, int nbits, int lane) {
+  unsigned m = __ballot_sync(0xffffffffu, e >= 0);
+  for (int b = 0; b < nbits; ++b) {  // warp-uniform trip count
+    const bool bit = (e >> b) & 1;
+    const unsigned v = __ballot_sync(0xffffffffu, bit);
+    m &= bit ? v : ~v;
+  }
+  return e >= 0 ? m : (1u << lane);
+}
 
 __device__ __forceinline__ int split_block_size(int k) { return k == 0 ? 64 : k == 1 ? 48 : k == 2 ? 32 : 16; }
 
@@ -98,24 +116,27 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     moe_split_align_kernel(const IdT *__restrict__ ids, int T, int E, const int32_t *__restrict__ cover_tab,
                            int64_t t_max, SplitLists out, int32_t *__restrict__ ntpp) {
   extern __shared__ int split_smem[];
-  int *hist = split_smem;              // [32][E]: slice counts, then slice rank bases
-  int *total = hist + kSplitWarps * E;  // [E]     this CTA's rows per expert (read by peers)
-  int *count = total + E;              // [E]     r_e
-  int *off = count + E;                // [4][E]  list offsets
-  int *lo = off + 4 * E;               // [3][E]  lo1, lo2, lo3
+  const int hs = split_hist_stride(E);
+  int *hist = split_smem;                // [32][hs]: slice counts, then rank bases within the CTA
+  int *total = hist + kSplitWarps * hs;  // [E]      this CTA's rows per expert (read by peers)
+  int *count = total + E;                // [E]      r_e
+  int *below = count + E;                // [E]      rows of this expert in lower CTAs
+  int *off = below + E;                  // [4][E]   list offsets
+  int *lo = off + 4 * E;                 // [3][E]   lo1, lo2, lo3
   __shared__ int4 warp_total[kSplitWarps];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cta = (int)cluster_ctarank(), ncta = (int)split_cluster_size();
   const int gwarp = cta * kSplitWarps + warp, nwarps = ncta * kSplitWarps;
   const unsigned lower = (1u << lane) - 1u;
-  for (int i = tid; i < kSplitWarps * E; i += kSplitThreads) hist[i] = 0;
+  const int nbits = E > 1 ? 32 - __clz(E - 1) : 0;
+  for (int i = tid; i < kSplitWarps * hs; i += kSplitThreads) hist[i] = 0;
   __syncthreads();
 
   // Pass 1: per-slice expert counts.
   const int per_warp = (T + nwarps - 1) / nwarps;
   const int beg = min(gwarp * per_warp, T), end = min(beg + per_warp, T);
-  int *my_hist = hist + warp * E;
+  int *my_hist = hist + warp * hs;
   for (int g0 = beg; g0 < end; g0 += 32 * kSplitBatch) {
     int ex[kSplitBatch];
 #pragma unroll
@@ -123,42 +144,61 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 #pragma unroll
     for (int b = 0; b < kSplitBatch; ++b) {
       if (g0 + 32 * b >= end) break;  // warp-uniform
-      // Invalid lanes get a key of their own (>= E), so they match nobody.
-      const unsigned peers = __match_any_sync(0xffffffffu, ex[b] >= 0 ? ex[b] : E + lane);
+      const unsigned peers = split_peers(ex[b], nbits, lane);  // invalid lanes match nobody
       if (ex[b] >= 0 && (peers & lower) == 0) my_hist[ex[b]] += __popc(peers);
       __syncwarp();
     }
   }
   __syncthreads();
 
-  // Per expert: exclusive prefix over this CTA's slices, and the CTA total.
-  for (int x = tid; x < E; x += kSplitThreads) {
-    int c = 0;
-    for (int w = 0; w < kSplitWarps; ++w) {
-      const int h = hist[w * E + x];
-      hist[w * E + x] = c;
-      c += h;
+  // Per expert (one warp per expert, lane w = slice w): exclusive prefix of
+  // the slice counts over this CTA's warps, and the CTA total.
+  // Four experts at a time, so their shuffle chains overlap.
+  for (int x0 = warp; x0 < E; x0 += 4 * kSplitWarps) {
+    int h[4], inc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int x = x0 + u * kSplitWarps;
+      h[u] = x < E ? hist[lane * hs + x] : 0;
+      inc[u] = h[u];
     }
-    total[x] = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = __shfl_up_sync(0xffffffffu, inc[u], o);
+        if (lane >= o) inc[u] += t;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int x = x0 + u * kSplitWarps;
+      if (x < E) {
+        hist[lane * hs + x] = inc[u] - h[u];
+        if (lane == 31) total[x] = inc[u];
+      }
+    }
   }
   split_cluster_sync();  // every CTA's totals are published
-  // Rows of lower CTAs come first: add their totals to the slice bases; the
-  // sum over all CTAs is r_e.
+  // Rows of lower CTAs come first (added to the rank in the scatter); the sum
+  // over all CTAs is r_e.
   for (int x = tid; x < E; x += kSplitThreads) {
     int v[kSplitClusterMax];
 #pragma unroll
     for (int c = 0; c < kSplitClusterMax; ++c)  // all remote loads in flight at once
       v[c] = c < ncta ? split_ld_dsmem(dsmem_addr(&total[x], (uint32_t)c)) : 0;
-    int below = 0, r = 0;
+    int lower_rows = 0, r = 0;
 #pragma unroll
     for (int c = 0; c < kSplitClusterMax; ++c) {
-      below += c < cta ? v[c] : 0;
+      lower_rows += c < cta ? v[c] : 0;
       r += v[c];
     }
-    if (below != 0)
-      for (int w = 0; w < kSplitWarps; ++w) hist[w * E + x] += below;
+    below[x] = lower_rows;
     count[x] = r;
   }
+  // This CTA reads no peer's shared memory after this point; the matching
+  // wait at the end keeps every CTA resident until all peers got here.
+  cluster_arrive_relaxed();
   __syncthreads();
 
   // Plan: rows_k per expert from the cover table, exclusive prefix over experts
@@ -223,9 +263,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     split_fill_list(2, x, r, off[2 * E + x], lo2, lo3, last2, T, cap_s[2], cap_s[2] / 32 + 1, out.s2, out.e2, lane);
     split_fill_list(3, x, r, off[3 * E + x], lo3, hi3, last3, T, cap_s[3], cap_s[3] / 16 + 1, out.s3, out.e3, lane);
   }
-  // The reference's scatter kernel runs after its fill kernel; past this
-  // barrier no CTA reads a peer's shared memory, so CTAs may exit freely.
-  split_cluster_sync();
+  // Fill and scatter write disjoint entries: the sentinels of an expert's
+  // last list start at its rank r, and its rows go below r.
 
   // Pass 2: stable ranks and the scatter into the lists.
   for (int g0 = beg; g0 < end; g0 += 32 * kSplitBatch) {
@@ -236,8 +275,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     for (int b = 0; b < kSplitBatch; ++b) {
       if (g0 + 32 * b >= end) break;  // warp-uniform
       const int e = ex[b];
-      const unsigned peers = __match_any_sync(0xffffffffu, e >= 0 ? e : E + lane);
-      const int q = e >= 0 ? my_hist[e] + __popc(peers & lower) : 0;
+      const unsigned peers = split_peers(e, nbits, lane);
+      const int q = e >= 0 ? below[e] + my_hist[e] + __popc(peers & lower) : 0;
       __syncwarp();
       if (e >= 0 && (peers & lower) == 0) my_hist[e] += __popc(peers);
       __syncwarp();
@@ -251,12 +290,13 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       }
     }
   }
+  cluster_wait();
 }
 
 }  // namespace titan
 
 extern "C" int64_t titan_moe_split_align_smem_bytes(int64_t num_experts) {
-  return (int64_t)titan::kSplitWordsPerExpert * num_experts * 4;
+  return ((int64_t)titan::kSplitWarps * (num_experts | 1) + (int64_t)titan::kSplitWordsPerExpert * num_experts) * 4;
 }
 
 extern "C" int titan_moe_split_align(const void *topk_ids, int ids_is_int64, int64_t num_routes,

@@ -250,7 +250,11 @@ int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int64_t num_ro
  *   num_experts  E in [1, TITAN_SPLIT_ALIGN_MAX_EXPERTS]; ids outside [0, E) are dropped
  *   cover_tab    int32 [cover_rows][4] on the device: blocks of each size in the
  *                cheapest cover of r rows (moe_split_align.py:172-185);
- *                cover_rows >= num_routes + 1
+ *                cover_rows >= num_routes + 1.  Every block of a cover must
+ *                hold at least one row (true of the cost-optimal table, whose
+ *                covers pad less than their smallest block): the padding and
+ *                the rows then land in disjoint entries, which the kernel
+ *                writes without ordering them.
  *   t_max        capacity the lists were allocated for, num_routes <= t_max:
  *   sorted_ids   host array of 4 device pointers, list k int32 [t_max + B_k * E]
  *   expert_ids   host array of 4 device pointers, list k int32 [(t_max + B_k * E) / B_k + 1]

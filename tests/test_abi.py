@@ -65,7 +65,7 @@ def test_split_align_invalid_arguments_rejected_on_host(native_lib):
     assert b"cover table" in native_lib.titan_last_error()
     assert split(None, 0, 8, 288, 16, 9, 8, lists, lists, 16, None) == 1
     assert b"null" in native_lib.titan_last_error()
-    assert native_lib.titan_moe_split_align_smem_bytes(288) == 41 * 288 * 4
+    assert native_lib.titan_moe_split_align_smem_bytes(288) == (32 * 289 + 10 * 288) * 4
 
 
 def test_fast_call_binding_is_built_and_bound(native_lib):
