@@ -16,6 +16,8 @@ plan as a CTA-wide scan and the fill/scatter in the same kernel.  No host
 sync and fixed buffers: CUDA-graph capturable.  Calls that share one buffer
 set must be ordered on the GPU (one stream).
 """
+from __future__ import annotations
+
 import ctypes
 import functools
 

@@ -41,7 +41,8 @@ def test_import_does_not_touch_cuda_or_library():
         with patch.dict(sys.modules, {"titan_native": native}):
             for filename, exported in (("titan_kv.py", "store_int8"),
                                        ("titan_mla.py", "triton_mla_sparse_attention"),
-                                       ("titan_moe_align.py", "titan_moe_align_small")):
+                                       ("titan_moe_align.py", "titan_moe_align_small"),
+                                       ("titan_moe_split_align.py", "split_align")):
                 mod = _load("isolated_" + filename[:-3], PKG / filename)
                 assert callable(getattr(mod, exported))
         assert native._lib is None, "importing must not load the library"
@@ -137,3 +138,27 @@ def test_kv_argument_errors_are_assertions():
         store_int8(x, cache, torch.arange(5))
     with pytest.raises(AssertionError):
         store_int8(x, cache, torch.arange(4))                                    # CPU tensors
+
+
+def test_split_align_buffers_and_errors():
+    """Buffer layout of profiles/sm74/titan_prefill/moe_split_align.py:187-201
+    (lists sized t_max + B*E and (t_max + B*E) // B + 1, four-entry ntpp, the
+    cover table of t_max + 1 rows); the reference's AssertionError on T = 0,
+    T > t_max or a different E; a CPU tensor is refused (no CPU fallback)."""
+    import torch
+    from kernels import titan_moe_split_align as S
+    buf = S.buffers(100, 288, torch.device("cpu"))
+    assert buf["t_max"] == 100 and buf["E"] == 288 and buf["ntpp"].numel() == 4
+    assert tuple(buf["tab"].shape) == (101, 4) and buf["tab"].dtype == torch.int32
+    for k, bs in enumerate(S.SIZES):
+        assert buf["s"][k].numel() == 100 + bs * 288 and buf["s"][k].dtype == torch.int32
+        assert buf["e"][k].numel() == (100 + bs * 288) // bs + 1
+    ids = torch.zeros(2, 8, dtype=torch.int32)
+    for bad_ids, E in ((torch.zeros(0, 8, dtype=torch.int32), 288), (torch.zeros(13, 8, dtype=torch.int32), 288),
+                       (ids, 287)):
+        with pytest.raises(AssertionError):
+            S.split_align(bad_ids, E, buf)
+    with pytest.raises(ValueError):
+        S.split_align(ids, 288, buf)
+    with pytest.raises(ValueError):
+        S.buffers(10, 1025, torch.device("cpu"))
