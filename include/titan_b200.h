@@ -1,7 +1,7 @@
 /*
  * titan_b200.h — C ABI of the B200 (sm_100a) GLM-5.3 sparse-MLA decode path.
  *
- * Three hot-path operations, each one `extern "C"` launcher that takes plain
+ * The path's operations, each an `extern "C"` launcher that takes plain
  * device pointers, sizes, strides and a CUDA stream, launches on that stream,
  * never synchronises and never allocates.  The caller owns every buffer.
  *
@@ -13,9 +13,10 @@
  *                                 replace the index conversion before the
  *                                 reader, integration/titan_backend.py:48-54
  *
- * The Python modules titan_kv / titan_mla / titan_moe_align keep the
- * reference's names, argument meaning and exception types and call these
- * entry points through ctypes.
+ * The Python modules titan_kv / titan_mla / titan_moe_align / titan_index /
+ * titan_moe_split_align keep the reference's names, argument meaning and
+ * exception types and call these entry points (through ctypes, or the
+ * CPython fast-call module for the hot launchers).
  *
  * Return value: TITAN_OK (0) or a non-zero TITAN_ERR_* code; the message of
  * the last failure on the calling thread is available from titan_last_error().
