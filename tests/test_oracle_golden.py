@@ -184,3 +184,37 @@ def test_split_align_product_cover_table_matches_oracle():
     from kernels import titan_moe_split_align as S
     assert np.array_equal(S.cover_table(3000).numpy(), O.split_cover_table(3000))
     assert S.SIZES == O.SPLIT_SIZES and S.COST == O.SPLIT_COST
+
+
+def test_split_align_oracle_properties_at_prefill_size():
+    """Size-independent checks of the split layout at M = 4096 x top-8 (uniform
+    and Zipf experts): every valid route appears exactly once, in stable order
+    within its expert; padding is the sentinel T only, at the tail of a block
+    that holds at least one row; every block's expert id matches its rows; ntpp
+    is a multiple of B."""
+    rng = np.random.default_rng(11)
+    E, M = 288, 4096
+    w = 1.0 / np.arange(1, E + 1) ** 1.1
+    for routes in (rng.integers(-2, E + 2, (M, 8)), rng.choice(E, size=(M, 8), p=w / w.sum())):
+        flat = routes.reshape(-1)
+        T = flat.size
+        lists = O.moe_split_align(routes, E)
+        seen = []
+        for bs, s, e, n in lists:
+            assert n % bs == 0
+            rows, blocks = s[:n], e[:n // bs]
+            for blk in range(n // bs):
+                members = rows[blk * bs:(blk + 1) * bs]
+                real = members[members != T]
+                assert real.size > 0 and np.all(flat[real] == blocks[blk])
+                pad = np.nonzero(members == T)[0]
+                assert pad.size == 0 or pad[0] == bs - pad.size  # padding only at the block's tail
+            seen.extend(rows[rows != T].tolist())
+        valid = np.nonzero((flat >= 0) & (flat < E))[0]
+        assert sorted(seen) == valid.tolist()
+        order = {}
+        for bs, s, e, n in lists:  # lists are taken largest block first, so ranks ascend across them
+            for j in s[:n]:
+                if j != T:
+                    order.setdefault(flat[j], []).append(j)
+        assert all(v == sorted(v) for v in order.values())
