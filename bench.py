@@ -36,7 +36,8 @@ tokens x top-8, 288 experts, uniform and Zipf(1.1) routes).
 
 --impl reference times the reference algorithm's CPU restatement (oracle/,
 the only CPU implementation of this path; the reference ships Triton GPU
-kernels only) on the host cores for the same config and metric.
+kernels only) on the host cores for the same config and metric, with the
+same protocol as the cpu_baseline key of our arm (time_cpu_port).
 """
 import argparse
 import json
@@ -657,7 +658,7 @@ def run_ours(args, dist):
     err = titan_native.device_error(caches[0])
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
-        cpu = cpu_baseline_b1(caches[0], q_sets, idx_sets, args.cpu_seconds)
+        cpu = cpu_baseline_b1(caches[0], K, args.cpu_seconds)
 
     if rank == 0:
         traffic = profile_traffic("mla_decode_b1")
@@ -701,33 +702,62 @@ def run_ours(args, dist):
         print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_b1(cache, q_sets, idx_sets, seconds):
-    """The oracle (CPU restatement of the reference algorithm) on the same B=1
-    workload, all host threads, bounded to ~`seconds` of work."""
+CPU_INDEX_SEED = 99   # the B=1 index sets both CPU legs time (the headline's rank-0 seed)
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def time_cpu_port(rows, steps, seconds, sets=64):
+    """One protocol for both CPU legs (the reference arm and the cpu_baseline
+    key): the oracle (CPU restatement of the reference algorithm, torch fp32,
+    all host threads) on `sets` distinct config-2 B=1 index sets (seed
+    CPU_INDEX_SEED); one untimed pass over every set, then blocks of `steps`
+    calls (set k % sets) repeated until at least `seconds` have elapsed.
+    Returns (us per call, calls timed, seconds timed, threads)."""
     from oracle import oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
-    rows = cache.view(KV_ROWS, ROW_BYTES).cpu()
-    sets = q_sets.shape[0]
-    O.mla_sparse_attention(q_sets[0], rows, idx_sets[0], SM_SCALE)  # warm
+    q_sets, idx_sets = decode_sets(1, sets, CPU_INDEX_SEED)
+    for k in range(sets):
+        O.mla_sparse_attention(q_sets[k], rows, idx_sets[k], SM_SCALE)
     n, t0 = 0, time.perf_counter()
-    while n < 3 or (time.perf_counter() - t0 < seconds and n < 100000):
-        O.mla_sparse_attention(q_sets[n % sets], rows, idx_sets[n % sets], SM_SCALE)
-        n += 1
-    dt = time.perf_counter() - t0
-    return {"value": dt / n * 1e6, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n} B=1 calls of oracle.mla_sparse_attention over the 262144-row cache "
-                      f"({dt:.1f} s, torch CPU fp32)"}
+    while True:
+        for _ in range(steps):
+            O.mla_sparse_attention(q_sets[n % sets], rows, idx_sets[n % sets], SM_SCALE)
+            n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return dt / n * 1e6, n, dt, torch.get_num_threads()
+
+
+def cpu_baseline_b1(cache, steps, seconds):
+    """The oracle on the same B=1 workload as the reference arm (same index
+    sets, same protocol: time_cpu_port), over the cache the GPU built."""
+    rows = cache.view(KV_ROWS, ROW_BYTES).cpu()
+    us, n, dt, cores = time_cpu_port(rows, steps, seconds)
+    return {"value": us, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
+            "sample": f"{n} B=1 calls of oracle.mla_sparse_attention over the 262144-row cache in {dt:.1f} s: "
+                      f"64 index sets (seed {CPU_INDEX_SEED}) each run once untimed, then blocks of {steps} calls "
+                      "until the time bound (torch CPU fp32, all host threads)"}
 
 
 # ------------------------------------------------------------ reference arm
 def run_reference(args):
     """CPU restatement of the reference algorithm (oracle/) on the host cores:
     the cache is filled by the oracle's store_int8 (C restatement) from the
-    same-shape latents, then K B=1 calls are timed."""
+    same-shape latents, then the B=1 calls are timed with time_cpu_port (the
+    protocol of the cpu_baseline key of our arm)."""
     import numpy as np
     from oracle import c_oracle
     from oracle import oracle as O
-    torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(1234)
     lat = torch.randn(KV_ROWS, 512, generator=g).to(torch.bfloat16)
     bits = np.ascontiguousarray(O.tensor_bf16_bits(lat))
@@ -735,28 +765,19 @@ def run_reference(args):
     t0 = time.perf_counter()
     c_oracle().oracle_store_int8_rows(bits.ctypes.data, KV_ROWS, rows.ctypes.data)
     fill_s = time.perf_counter() - t0
-    rows_t = torch.from_numpy(rows)
-    q_sets, idx_sets = decode_sets(1, args.index_sets, 99)
-    sets = q_sets.shape[0]
-    # At least 20 untimed calls: the first few pay one-time costs (allocator
-    # pages, thread pool start) that would inflate a short timed run.
-    for k in range(max(args.warmup, 20)):
-        O.mla_sparse_attention(q_sets[k % sets], rows_t, idx_sets[k % sets], SM_SCALE)
-    t0 = time.perf_counter()
-    for k in range(args.steps):
-        O.mla_sparse_attention(q_sets[k % sets], rows_t, idx_sets[k % sets], SM_SCALE)
-    dt = time.perf_counter() - t0
-    us = dt / args.steps * 1e6
-    cores = torch.get_num_threads()
+    us, n, dt, cores = time_cpu_port(torch.from_numpy(rows), args.steps, args.cpu_seconds)
     line = {
         "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": us / 1000, "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "config2: B=1 sparse MLA decode, 16 heads, 262144-row INT8 cache, 2176 indices "
-                               "(2048 valid)", "index_sets": sets},
-        "cpu_baseline": {"value": us, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} B=1 calls of the CPU restatement (torch fp32); cache fill by the "
-                                   f"C restatement of store_int8 took {fill_s:.2f} s single-threaded"},
+        "config": {"workload": "config2: B=1 sparse MLA decode, 16 heads x 512 NoPE latent, 262144-row INT8 "
+                               "528-B-row cache filled by store_int8, 2176 indices (2048 distinct valid + 128 x -1)",
+                   "index_sets": 64},
+        "cpu_baseline": {"value": us, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
+                         "sample": f"{n} B=1 calls of the CPU restatement (torch fp32) in {dt:.1f} s: 64 index "
+                                   f"sets (seed {CPU_INDEX_SEED}) each run once untimed, then blocks of "
+                                   f"{args.steps} calls until the time bound; cache fill by the C restatement "
+                                   f"of store_int8 took {fill_s:.2f} s single-threaded"},
         "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -823,8 +844,8 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--index-sets", type=int, default=64)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="time bound of both CPU legs (reference arm and cpu_baseline)")
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1", "split_align"),

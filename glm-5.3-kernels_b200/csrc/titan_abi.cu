@@ -56,3 +56,27 @@ extern "C" int titan_device_error(int *error_out, int clear_after, titan_stream_
   *error_out = v;
   return TITAN_OK;
 }
+
+namespace titan {
+
+// One warp waits on an mbarrier that nothing arrives at, with the same
+// bounded wait the kernels use: it gives up after `limit_cycles`, records
+// kDevErrMbarrierTimeout in the device error word and returns.
+__global__ void selftest_bounded_wait_kernel(long long limit_cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  mbar_wait_bounded(&bar, 0u, limit_cycles);  // phase 0 never completes
+}
+
+}  // namespace titan
+
+extern "C" int titan_selftest_bounded_wait(long long limit_cycles, titan_stream_t stream) {
+  if (limit_cycles < 1 || limit_cycles > 4000000000LL)
+    return titan::fail(TITAN_ERR_INVALID_ARGUMENT, "selftest: limit_cycles must be in [1, 4e9]");
+  titan::selftest_bounded_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_cycles);
+  return titan::check_launch("selftest_bounded_wait launch");
+}

@@ -74,9 +74,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait: gives up after ~`limit_cycles` SM clocks, records the failure
 // in the device error word and returns false.  Never traps, never spins forever.
-// Bulk copies land in microseconds; the first wait of a CTA allows ~0.1 s, and
-// after one failure the caller switches to kShortWaitCycles so a CTA with a
-// lost copy finishes its remaining tiles quickly instead of stalling the grid.
+// Bulk copies land in microseconds; a wait allows ~0.1 s (kLongWaitCycles).
+// After a give-up the caller stops issuing copies and drains the ones already
+// in flight with kShortWaitCycles waits (~0.5 ms each), so a CTA with a lost
+// copy ends quickly instead of stalling the grid.
 constexpr long long kLongWaitCycles = 200000000LL;
 constexpr long long kShortWaitCycles = 1000000LL;
 

@@ -5,6 +5,9 @@
 //   q     = clamp(nearbyint(x / scale), -127, 127)
 //   row   = cache + (slot / block) * stride0 + (slot % block) * stride1
 //   bytes [0,512) = q, bytes [512,528) = fp32 {scale, 0, 0, 0}; slot < 0 skips.
+//   max / maximum / minimum drop NaN operands, as Triton's default forms do on
+//   the GPU: NaN values are ignored by the row max and store -127; an inf
+//   makes the scale inf (finite values store 0, +-inf stores -127).
 //
 // Layout of the work: for each of its rows, lane l of the warp owns latent
 // values [16 l, 16 l + 16): two 16-byte loads of bf16, one 16-byte store of int8.
@@ -87,6 +90,27 @@ __device__ __forceinline__ float row_scale(float amax) {
   return fmaxf(__fmaf_rn(r, kInv127, y0), 1.0e-12f);
 }
 
+// Rows holding NaN or inf (rare; taken by whole warps so the fast paths keep
+// their arithmetic).  The reference's max, maximum and minimum drop NaN
+// operands (Triton's default PropagateNan.NONE lowers them to maxnum /
+// minnum), so the row max ignores NaN values, an infinite row max gives an
+// infinite scale, and a NaN quotient (a NaN value, or +-inf / inf) clamps to
+// -127 — CUDA's fmaxf / fminf have the same NaN rule.  A finite row gets the
+// same bytes here as on the fast paths: IEEE division throughout.
+__device__ __forceinline__ float nonfinite_row_scale(float amax_without_nan) {
+  return isinf(amax_without_nan) ? __int_as_float(0x7F800000) : row_scale(amax_without_nan);
+}
+
+__device__ __forceinline__ uint32_t quant4_exact(float a, float b, float c, float d, float scale) {
+  auto q = [scale](float v) {
+    return (uint32_t)__float2int_rn(fminf(fmaxf(rintf(__fdiv_rn(v, scale)), -127.0f), 127.0f)) & 0xFFu;
+  };
+  return q(a) | q(b) << 8 | q(c) << 16 | q(d) << 24;
+}
+
+// True when |v| is inf or NaN.
+__device__ __forceinline__ bool not_finite(float v) { return !(fabsf(v) < __int_as_float(0x7F800000)); }
+
 // Each warp quantises kKvRowsPerWarp rows; every row's two 16-byte loads per
 // lane are issued before any arithmetic so ~4 KB per warp is in flight.
 template <typename SlotT>
@@ -125,12 +149,24 @@ __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
     bf16x2_to_f32(b[r].y, v[10], v[11]);
     bf16x2_to_f32(b[r].z, v[12], v[13]);
     bf16x2_to_f32(b[r].w, v[14], v[15]);
-    float amax = 0.0f;
+    float amax = 0.0f;  // fmaxf drops NaN: the max of the non-NaN magnitudes
+    bool bad = false;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    const float scale = row_scale(warp_amax(amax));
+    for (int i = 0; i < 16; ++i) {
+      amax = fmaxf(amax, fabsf(v[i]));
+      bad |= not_finite(v[i]);
+    }
+    amax = warp_amax(amax);
     uint32_t q[4];
-    quant16(v, scale, __frcp_rn(scale), q);
+    float scale;
+    if (__any_sync(0xffffffffu, bad)) {  // the row (one per warp here) holds NaN or inf
+      scale = nonfinite_row_scale(amax);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) q[w] = quant4_exact(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3], scale);
+    } else {
+      scale = row_scale(amax);
+      quant16(v, scale, __frcp_rn(scale), q);
+    }
     int8_t *dst = cache + blk * cs0 + off * cs1;
     *reinterpret_cast<uint4 *>(dst + lane * 16) = make_uint4(q[0], q[1], q[2], q[3]);
     if (lane == 0) *reinterpret_cast<uint4 *>(dst + 512) = make_uint4(__float_as_uint(scale), 0u, 0u, 0u);
@@ -246,9 +282,27 @@ __global__ void __launch_bounds__(kKvStreamWarps * 32, 3)
     mx = max(mx & 0xFFFFu, mx >> 16);  // |x| as bf16 bits; integer order = value order
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float scale = row_scale(__uint_as_float(mx << 16));
     uint32_t q[8];
-    quant32(w, scale, __frcp_rn(scale), q);
+    float scale;
+    // Bits >= 0x7F80 (inf, or NaN, which outranks every number): a row of
+    // this warp holds a non-finite value, and both half-warps take the exact
+    // path (same bytes for a finite row).
+    if (__any_sync(0xffffffffu, mx >= 0x7F80u)) {
+      float amax = 0.0f;  // fmaxf drops NaN
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(w[k] << 16)), fabsf(__uint_as_float(w[k] & 0xFFFF0000u))));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      scale = nonfinite_row_scale(amax);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        q[k] = quant4_exact(__uint_as_float(w[2 * k] << 16), __uint_as_float(w[2 * k] & 0xFFFF0000u),
+                            __uint_as_float(w[2 * k + 1] << 16), __uint_as_float(w[2 * k + 1] & 0xFFFF0000u), scale);
+    } else {
+      scale = row_scale(__uint_as_float(mx << 16));
+      quant32(w, scale, __frcp_rn(scale), q);
+    }
     __syncwarp();  // the stage may be refilled once every lane has read it
     int64_t blk = 0, off = 0;
     if (slot >= 0) split_slot(slot, block, block_shift, blk, off);
@@ -279,15 +333,25 @@ __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
   if (blk >= num_blocks) return;
   const __nv_bfloat16 *src = x + row * x_row_stride;
   float v[16];
-  float amax = 0.0f;
+  float amax = 0.0f;  // fmaxf drops NaN
+  bool bad = false;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     v[k] = __bfloat162float(src[lane + 32 * k]);
     amax = fmaxf(amax, fabsf(v[k]));
+    bad |= not_finite(v[k]);
   }
-  const float scale = row_scale(warp_amax(amax));
+  amax = warp_amax(amax);
   uint32_t q[4];
-  quant16(v, scale, __frcp_rn(scale), q);
+  float scale;
+  if (__any_sync(0xffffffffu, bad)) {
+    scale = nonfinite_row_scale(amax);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) q[w] = quant4_exact(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3], scale);
+  } else {
+    scale = row_scale(amax);
+    quant16(v, scale, __frcp_rn(scale), q);
+  }
   int8_t *dst = cache + blk * cs0 + off * cs1;
 #pragma unroll
   for (int k = 0; k < 16; ++k) dst[lane + 32 * k] = (int8_t)((q[k >> 2] >> (8 * (k & 3))) & 0xFF);

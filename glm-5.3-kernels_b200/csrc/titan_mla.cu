@@ -397,8 +397,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int red_nt = red_j >> 3;
   const int red_n = red_j & 7;
 
+  // A ring wait that gives up (a gather that never landed: the device error
+  // word is set) ends the tile loop for the whole CTA at the next barrier:
+  // no further gathers are issued and the remaining tiles are skipped; the
+  // gathers already in flight are then waited for with short bounded waits,
+  // so none lands after the CTA has exited.  The CTA still completes the
+  // split-merge protocol below with the state it has (cluster pushes, ticket
+  // and counter reset), so its cluster peers are not left to time out and
+  // the next call's arrival counters start from zero; that call's outputs
+  // are undefined and the error word reports it.
   int st = 0, st_issue = 2;  // ring stage of tile i and of tile i + 2
-  long long wait_limit = kLongWaitCycles;
+  int i_end = n_tiles;       // tiles started (fewer after a give-up)
+  bool gave_up = false;
   for (int i = 0; i < n_tiles; ++i) {
     // Tile i + 2 goes in flight (its indices were published by the last
     // iteration's barriers); warp 0 stages later tiles' indices.
@@ -414,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       cp_async_commit();
     }
     // Tile i's rows (this stage's k-th use has parity k & 1).
-    if (!mbar_wait_bounded(&sm.row_bar[st], (uint32_t)(i / kRing) & 1u, wait_limit)) wait_limit = kShortWaitCycles;
+    const bool landed = mbar_wait_bounded(&sm.row_bar[st], (uint32_t)(i / kRing) & 1u, kLongWaitCycles);
     const uint8_t *stage = sm.u.ring.rows[st][0];
     uint4 kb_cur[4];
 #pragma unroll
@@ -449,7 +459,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         *reinterpret_cast<float2 *>(&red[(g + 8) * kRedStride + nt * 8 + 2 * c]) = make_float2(sacc[nt][2], sacc[nt][3]);
       }
     }
-    __syncthreads();  // partial scores, row scales
+    if (__syncthreads_or(!landed)) {  // partial scores, row scales; or a thread's wait gave up
+      i_end = i + 1;
+      gave_up = true;
+      break;
+    }
 
     // ---- Reduce the 8 partial scores, scale, mask, online softmax, P.
     {
@@ -514,6 +528,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     st = st == kRing - 1 ? 0 : st + 1;
     st_issue = st_issue == kRing - 1 ? 0 : st_issue + 1;
   }
+  // After a give-up at tile i_end - 1, that tile's gather and those of the
+  // next two tiles (already issued) may still be in flight: short bounded
+  // waits by every thread on their stages.
+  if (gave_up)
+    for (int k = i_end - 1; k < n_tiles && k < i_end + kRing - 1; ++k)
+      mbar_wait_bounded(&sm.row_bar[k % kRing], (uint32_t)(k / kRing) & 1u, kShortWaitCycles);
   // Every issued gather was waited for; warp 0's index copies beyond the
   // last tile are empty groups.  The ring is dead from here.
   cp_async_wait<0>();

@@ -35,6 +35,8 @@
 // groups of route ids before using them.
 #include "titan_common.cuh"
 
+#include <cstdlib>
+
 namespace titan {
 
 constexpr int kSplitThreads = 1024;
@@ -330,8 +332,8 @@ extern "C" int titan_moe_split_align(const void *topk_ids, int ids_is_int64, int
   static std::atomic<int> dev_cluster[64];  // 0 = not set up
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64)
-    return fail(TITAN_ERR_CUDA, "moe_split_align: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "moe_split_align: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "moe_split_align: device ordinal %d out of range", dev);
   const int max_smem = (int)titan_moe_split_align_smem_bytes(kSplitMaxExperts);
   int cluster = dev_cluster[dev].load(std::memory_order_acquire);
   if (cluster == 0) {
@@ -362,6 +364,11 @@ extern "C" int titan_moe_split_align(const void *topk_ids, int ids_is_int64, int
         n = 0;
       }
       cluster = n >= 1 ? kSplitClusterMax : 8;
+      // TITAN_SPLIT_ALIGN_CLUSTER=8, read here once per device, forces the
+      // portable 8-CTA cluster (the fallback of devices that cannot hold 16),
+      // so that path can be tested on a device that can.
+      const char *force = getenv("TITAN_SPLIT_ALIGN_CLUSTER");
+      if (force != nullptr && atoi(force) == 8) cluster = 8;
       dev_cluster[dev].store(cluster, std::memory_order_release);
     }
   }

@@ -2,8 +2,9 @@
 """Sparse NoPE MLA over a per-token INT8 KV cache, for B200 (sm_100a).
 
 Drop-in for the reference `triton_mla_sparse_attention`
-(kernels/titan_mla.py:452-581) with the same argument order, defaults,
-assertions and split heuristic (`_choose_num_kv_splits`, :432-449).  The
+(kernels/titan_mla.py:452-581) with the same argument order, defaults and
+assertions; the automatic split count is this kernel's own policy
+(`_choose_kv_splits_b200`), an explicit `num_kv_splits` is honoured.  The
 compute runs in libtitan_b200.so (csrc/titan_mla.cu): rows gathered by the
 tensor memory accelerator (`tile::gather4`, four rows per load) into a
 shared-memory ring laid out as the lanes' tensor-core fragments, bf16 MMAs
@@ -38,11 +39,6 @@ _ROW_BYTES = 528
 # kernels/titan_mla.py:45-49); kept so the same inputs are accepted/rejected.
 _MIN_BLOCK_N = 32
 
-# Split-count candidates and heuristic constants (kernels/titan_mla.py:53-56).
-KV_SPLITS_CANDIDATES = (1, 2, 4, 8, 16)
-_MIN_TOPK_PER_SPLIT = 128
-_SPLIT_MAX_OCCUPANCY = 4
-
 
 @functools.lru_cache(maxsize=64)
 def num_compute_units(device_index):
@@ -51,29 +47,6 @@ def num_compute_units(device_index):
 
 def _cdiv(a, b):
     return -(-a // b)
-
-
-def _next_power_of_2(n):
-    return 1 if n <= 1 else 1 << (int(n) - 1).bit_length()
-
-
-@functools.lru_cache(maxsize=256)
-def _choose_num_kv_splits(num_tokens: int, num_head_groups: int, index_topk: int, sm_count: int) -> int:
-    """Pick a power-of-2 split count that fills the device without dropping
-    per-split work below _MIN_TOPK_PER_SPLIT; 1 when the single-pass grid
-    already reaches ~1/_SPLIT_MAX_OCCUPANCY of the SMs.  Same policy and
-    results as kernels/titan_mla.py:432-449.
-    """
-    baseline = num_tokens * num_head_groups
-    if baseline == 0 or baseline * _SPLIT_MAX_OCCUPANCY >= sm_count:
-        return 1
-    ideal = _next_power_of_2(max(1, index_topk // _MIN_TOPK_PER_SPLIT))
-    max_splits = max(1, sm_count // baseline)
-    max_splits = 1 << (max_splits.bit_length() - 1)  # floor to a power of 2
-    num_kv_splits = min(ideal, max_splits)
-    while num_kv_splits > 1 and index_topk % num_kv_splits != 0:
-        num_kv_splits //= 2
-    return max(1, num_kv_splits)
 
 
 # Cost model of the B200 kernel (microseconds): 32-row tiles per CTA, the
@@ -132,8 +105,9 @@ def _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count, ta
 
     Candidates keep the whole grid (tokens x groups x S CTAs) within one CTA
     per SM; the cheapest under the cost model above wins (ties: fewer
-    splits).  The reference's `_choose_num_kv_splits` targets its own SM80
-    kernel and stays available through an explicit num_kv_splits.
+    splits).  The reference's heuristic (`_choose_num_kv_splits`,
+    kernels/titan_mla.py:432-449) targets its SM80 kernel; any split count it
+    would pick can still be passed explicitly as num_kv_splits.
     """
     units = num_tokens * num_head_groups
     if units == 0 or units >= sm_count:

@@ -9,10 +9,12 @@ are covered by the cheapest multiset of blocks under the per-block cost model
 COST, filled largest size first, only the last (smallest) block padded with the
 sentinel T = M * topk.  Rows keep their stable flat order within an expert.
 
-The five Triton kernels of the reference become one launch of one CTA
+The five Triton kernels of the reference become one launch of one 16-CTA
+thread-block cluster, 8 CTAs where the device cannot hold 16
 (`titan_moe_split_align` in libtitan_b200.so, csrc/titan_moe_split_align.cu):
-per-warp shared-memory histograms, a prefix over warps for stable ranks, the
-plan as a CTA-wide scan and the fill/scatter in the same kernel.  No host
+per-warp shared-memory histograms, stable ranks from a prefix over warps and
+over the cluster's CTAs (distributed shared memory), the plan as a CTA-wide
+scan and the fill/scatter in the same kernel.  No host
 sync and fixed buffers: CUDA-graph capturable.  Calls that share one buffer
 set must be ordered on the GPU (one stream).
 """
@@ -86,6 +88,9 @@ def split_align(topk_ids: torch.Tensor, E: int, buf: dict):
         raise AssertionError("split_align buffers too small")
     if not ids.is_cuda:
         raise ValueError("split_align requires CUDA route IDs")
+    if any(t.device != ids.device for t in (buf["tab"], buf["ntpp"], *buf["s"], *buf["e"])):
+        raise ValueError("split_align buffers must be on the route IDs' device")
+    ids = ids.contiguous()  # the kernel reads the flat ids with stride 1
     s, e, ntpp = buf["s"], buf["e"], buf["ntpp"]
     lists_s = (ctypes.c_void_p * 4)(*(t.data_ptr() for t in s))
     lists_e = (ctypes.c_void_p * 4)(*(t.data_ptr() for t in e))

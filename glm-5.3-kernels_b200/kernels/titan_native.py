@@ -80,6 +80,7 @@ SIGNATURES = {
         _int, [_vp, _int, _i64, _i64, _vp, _i64, _i64, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, _vp]),
     "titan_moe_split_align_smem_bytes": (_i64, [_i64]),
     "titan_device_error": (_int, [ctypes.POINTER(_int), _int, _vp]),
+    "titan_selftest_bounded_wait": (_int, [ctypes.c_longlong, _vp]),
     "titan_copy": (_int, [_vp, _vp, _i64, _vp]),
     "titan_copy_ex": (_int, [_vp, _vp, _i64, _int, _vp]),
     "titan_device_pointer": (_int, [_vp, ctypes.POINTER(_vp)]),

@@ -244,7 +244,9 @@ int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int64_t num_ro
  * by expert into four block lists, block sizes {64, 48, 32, 16}, one Marlin
  * launch per list.  Replaces `split_align(topk_ids, E, buf)`,
  * profiles/sm74/titan_prefill/moe_split_align.py:204-223 (kernels :44-169).
- * One launch of one CTA; no scratch memory.
+ * One launch of one 16-CTA thread-block cluster (8 CTAs where the device
+ * cannot hold 16; the environment variable TITAN_SPLIT_ALIGN_CLUSTER=8, read
+ * at the first call on a device, forces 8); no scratch memory.
  *
  *   topk_ids     int32 (ids_is_int64 = 0) or int64 (1), num_routes = M * topk
  *                entries, contiguous; int64 ids are narrowed to int32 first
@@ -303,6 +305,15 @@ int titan_device_pointer(const void *ptr, void **device_ptr_out);
  * the current device; synchronises the stream first.  0 = no error.
  */
 int titan_device_error(int *error_out, int clear_after, titan_stream_t stream);
+
+/*
+ * Self-test of the bounded waits (no counterpart in the reference): one warp
+ * waits on an mbarrier that nothing completes, gives up after about
+ * `limit_cycles` SM clocks (1 .. 4e9), sets the device error word to 1
+ * (mbarrier timeout) and returns; the context stays usable.  Lets a test show
+ * that a wait that runs out is reported through titan_device_error.
+ */
+int titan_selftest_bounded_wait(long long limit_cycles, titan_stream_t stream);
 
 #ifdef __cplusplus
 }

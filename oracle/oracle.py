@@ -42,14 +42,19 @@ def store_int8_rows(x_bits):
     Follows kernels/titan_kv.py:15-21 with IEEE fp32 arithmetic:
       scale = max(max|x| / 127, 1e-12); q = clamp(nearbyint(x / scale), -127, 127)
     Row bytes: [0,512) q as int8, [512,516) scale (fp32 LE), [516,528) zero.
+    The reference's max, maximum and minimum (Triton's default
+    PropagateNan.NONE: maxnum / minnum on the GPU) drop NaN operands: the row
+    max ignores NaN values, an infinite value gives an infinite scale, and a
+    NaN quotient (a NaN value, or +-inf / inf) clamps to -127.
     Returns uint8 [N, 528].
     """
     x = bf16_bits_to_f32(np.asarray(x_bits).reshape(-1, LATENT_DIM))
-    amax = np.abs(x).max(axis=1)
-    scale = np.maximum(amax / np.float32(127.0), np.float32(1.0e-12)).astype(np.float32)
     with np.errstate(invalid="ignore", divide="ignore"):
+        a = np.abs(x)
+        amax = np.where(np.isnan(a), np.float32(0.0), a).max(axis=1)
+        scale = np.fmax(amax / np.float32(127.0), np.float32(1.0e-12)).astype(np.float32)
         q = np.rint(x / scale[:, None])  # np.rint rounds half to even, like nearbyint
-    q = np.clip(q, -127, 127).astype(np.int8)
+    q = np.fmin(np.fmax(q, np.float32(-127)), np.float32(127)).astype(np.int8)
     rows = np.zeros((x.shape[0], ROW_BYTES), dtype=np.uint8)
     rows[:, :LATENT_DIM] = q.view(np.uint8)
     rows[:, LATENT_DIM:LATENT_DIM + 4] = scale.view(np.uint8).reshape(-1, 4)
@@ -132,20 +137,31 @@ def mla_sparse_attention(q, rows, indices, sm_scale, threads=None):
     return out
 
 
-def mla_reference_test_metrics(out, q, original_bf16, indices, seq_kv, sm_scale):
+def mla_reference_test_metrics(out, q, original_bf16, indices, seq_kv, sm_scale, chunk=64):
     """The reference test's own numerical criteria (tests/verify_mla.py:79-90):
-    FP32 softmax attention over the ORIGINAL bf16 latents; returns (nmse, cosine)."""
+    FP32 softmax attention over the ORIGINAL bf16 latents; returns (nmse, cosine).
+    Tokens are processed `chunk` at a time (the gathered latents of a
+    4096-token prefill would not fit in host memory at once)."""
     qf = q.detach().cpu().float()
     idx = torch.as_tensor(indices).cpu().reshape(qf.shape[0], -1).long()
-    valid = (idx >= 0) & (idx < seq_kv)
-    chosen = original_bf16.detach().cpu().float()[idx.clamp(0, seq_kv - 1)]
-    chosen.masked_fill_(~valid[:, :, None], 0)
-    logits = torch.bmm(qf, chosen.transpose(1, 2)) * sm_scale
-    logits.masked_fill_(~valid[:, None, :], -float("inf"))
-    ref = torch.bmm(torch.nan_to_num(logits.softmax(-1), nan=0.0), chosen)
-    o = out.detach().cpu().float()
-    nmse = ((o - ref).square().sum() / ref.square().sum().clamp_min(1e-30)).item()
-    cos = torch.nn.functional.cosine_similarity(o.flatten(), ref.flatten(), dim=0).item()
+    lat = original_bf16.detach().cpu()
+    o_all = out.detach().cpu().float()
+    err = ref2 = dot = o2 = 0.0
+    for t0 in range(0, qf.shape[0], chunk):
+        ii = idx[t0:t0 + chunk]
+        valid = (ii >= 0) & (ii < seq_kv)
+        chosen = lat[ii.clamp(0, seq_kv - 1)].float()
+        chosen.masked_fill_(~valid[:, :, None], 0)
+        logits = torch.bmm(qf[t0:t0 + chunk], chosen.transpose(1, 2)) * sm_scale
+        logits.masked_fill_(~valid[:, None, :], -float("inf"))
+        ref = torch.bmm(torch.nan_to_num(logits.softmax(-1), nan=0.0), chosen).double()
+        o = o_all[t0:t0 + chunk].double()
+        err += (o - ref).square().sum().item()
+        ref2 += ref.square().sum().item()
+        dot += (o * ref).sum().item()
+        o2 += o.square().sum().item()
+    nmse = err / max(ref2, 1e-30)
+    cos = dot / max((o2 ** 0.5) * (ref2 ** 0.5), 1e-30)
     return nmse, cos
 
 

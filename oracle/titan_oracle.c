@@ -5,7 +5,9 @@
  *
  * oracle_store_int8_rows  follows kernels/titan_kv.py:15-21 in IEEE fp32
  *                         (compile without fast-math; rintf in the default
- *                         round-to-nearest-even mode is nearbyint).
+ *                         round-to-nearest-even mode is nearbyint); NaN
+ *                         operands are dropped by max / maximum / minimum as
+ *                         in the reference (Triton's maxnum / minnum).
  * oracle_moe_align_small  follows kernels/titan_moe_align.py:17-46 (the
  *                         pairwise rank/count/offset formulation of
  *                         benchmarks/moe_align.py:34-46).
@@ -25,7 +27,7 @@ void oracle_store_int8_rows(const uint16_t *x_bits, int64_t n, uint8_t *rows_out
   for (int64_t i = 0; i < n; ++i) {
     const uint16_t *x = x_bits + i * 512;
     uint8_t *row = rows_out + i * 528;
-    float amax = 0.0f;
+    float amax = 0.0f; /* a NaN never compares greater: the row max ignores it */
     for (int d = 0; d < 512; ++d) {
       float a = fabsf(bf16_to_f32(x[d]));
       if (a > amax) amax = a;
@@ -34,9 +36,10 @@ void oracle_store_int8_rows(const uint16_t *x_bits, int64_t n, uint8_t *rows_out
     float scale = amax / q127;
     if (!(scale >= 1.0e-12f)) scale = 1.0e-12f;
     for (int d = 0; d < 512; ++d) {
+      /* fmaxf / fminf return the non-NaN operand, like the reference's
+         maximum / minimum: a NaN quotient clamps to -127. */
       float y = rintf(bf16_to_f32(x[d]) / scale);
-      if (y < -127.0f) y = -127.0f;
-      if (y > 127.0f) y = 127.0f;
+      y = fminf(fmaxf(y, -127.0f), 127.0f);
       row[d] = (uint8_t)(int8_t)y;
     }
     memcpy(row + 512, &scale, 4);

@@ -40,6 +40,25 @@ def kv_latents():
     x[7] = -3.0                                    # constant row -> all -127
     x[8] = (torch.randn(512, generator=g) * 0.01).to(torch.bfloat16)
     x[8, 17] = 40.0                                # one large outlier
+    # Non-finite latents.  The reference's max / maximum / minimum drop NaN
+    # operands (Triton's default PropagateNan.NONE), so a NaN value is
+    # ignored by the row max and quantises to -127; an infinite value makes
+    # the scale infinite, finite values then quantise to 0 and +-inf to -127.
+    nan_bits = [0x7FC0, 0xFFC0, 0x7F81, 0x7FFF]    # quiet, negative, signalling, max-payload NaN
+    x[9] = (torch.randn(512, generator=g)).to(torch.bfloat16)
+    x[9, 5] = float("nan")                         # one NaN among finite values
+    x[10] = (torch.randn(512, generator=g) * 3).to(torch.bfloat16)
+    x[10, 100] = float("inf")                      # one +inf: scale = inf
+    x[11] = (torch.randn(512, generator=g)).to(torch.bfloat16)
+    x[11, 300] = float("-inf")
+    x[11, 301] = float("nan")                      # -inf and NaN together
+    x[12] = float("nan")                           # all NaN: scale floor, every value -127
+    x[13] = (torch.randn(512, generator=g) * 1e30).to(torch.bfloat16)
+    x[13, ::64] = float("inf")
+    x[13, 1::64] = float("-inf")                   # several infinities of both signs
+    x14 = x[14].view(torch.int16)
+    for k, b in enumerate(nan_bits):               # NaN payloads and signs, as raw bf16 bits
+        x14[64 * k + 3] = b - (1 << 16) if b >= 0x8000 else b
     return x
 
 

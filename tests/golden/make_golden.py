@@ -21,14 +21,18 @@ the tests read the committed .npz files).  Sources of truth:
   calls before the reader (integration/titan_backend.py:49-52), executed by the
   Triton interpreter (vLLM version recorded in the file).
 
-The interpreter needs three shims, all inside this script and none in the
+The interpreter needs four shims, all inside this script and none in the
 reference's code: libdevice `nearbyint` (absent from the interpreter) is
 np.rint (round half to even, as nearbyint in the default mode); bf16 casts
 round to nearest even through torch (the interpreter stores bf16 as raw
-uint16 bits and would otherwise convert integers to bits); and `tl.dot` on
+uint16 bits and would otherwise convert integers to bits); `tl.dot` on
 bf16 operands multiplies exactly in fp32 with fp32 accumulation (the
-interpreter would otherwise multiply the raw bits).  Fp32 division in the
-interpreter is IEEE division.  The autotuned MLA kernels are run with their
+interpreter would otherwise multiply the raw bits); and elementwise
+`tl.maximum` / `tl.minimum` drop a NaN operand (np.fmax / np.fmin), as
+their default PropagateNan.NONE form does on the GPU, where they lower to
+maxnum / minnum (the interpreter's `tl.max` reduction already drops NaN
+with np.nanmax, but its elementwise forms would propagate it).  Fp32
+division in the interpreter is IEEE division.  The autotuned MLA kernels are run with their
 first listed config (the interpreter has no benchmarker).
 
 MLA inputs are regenerated in the tests from the recorded seeds with torch's
@@ -92,6 +96,12 @@ def install_interpreter_shims():
         return orig_dot(self, a, b, d, input_precision, max_num_imprecise_acc)
 
     B = interp.InterpreterBuilder
+    # tl.maximum / tl.minimum with the default PropagateNan.NONE are maxnumf /
+    # minnumf, which return the non-NaN operand when compiled for the GPU
+    # (and the interpreter's own tl.max reduction already uses np.nanmax);
+    # the interpreter's elementwise forms would propagate NaN instead.
+    B.create_maxnumf = lambda self, lhs, rhs: self.binary_op(lhs, rhs, np.fmax)
+    B.create_minnumf = lambda self, lhs, rhs: self.binary_op(lhs, rhs, np.fmin)
     B.create_extern_elementwise = extern_elementwise
     B.cast_impl = cast_impl
     B.create_si_to_fp = lambda self, src, dst_type: cast_impl(self, src, dst_type)

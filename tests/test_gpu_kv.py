@@ -29,6 +29,37 @@ def test_golden_bytes(native_lib, cuda_device):
         assert np.array_equal(cache.cpu().numpy().view(np.uint8), gold["cache"]), slot_dtype
 
 
+@pytest.mark.parametrize("kernel", ["stream", "unaligned"])
+def test_nonfinite_rows_every_kernel(native_lib, cuda_device, kernel):
+    """The golden rows (NaN and inf rows among them) on the streaming kernel
+    (>= 1024 rows: the 128 golden rows tiled 32 times, shuffled) and on the
+    unaligned-row kernel: bytes equal the golden-pinned oracle's."""
+    from kernels.titan_kv import store_int8
+    gold = np.load(f"{GOLDEN}/kv_golden.npz")
+    x = C.kv_latents()
+    assert not torch.isfinite(x.float()).all(1).all()
+    g = torch.Generator().manual_seed(5)
+    if kernel == "stream":
+        xs = x.repeat(32, 1)[torch.randperm(32 * x.shape[0], generator=g)]
+        src = xs.to(cuda_device)
+    else:
+        xs = x
+        wide = torch.zeros(x.shape[0], 520, dtype=torch.bfloat16)
+        wide[:, 3:515] = x
+        src = wide.to(cuda_device)[:, 3:515]            # rows 6 bytes off 16-byte alignment
+    n = xs.shape[0]
+    cache = torch.zeros((n + 255) // 256, 256, 528, dtype=torch.int8, device=cuda_device)
+    store_int8(src, cache, torch.arange(n, device=cuda_device))
+    got = cache.view(-1, 528)[:n].cpu().numpy().view(np.uint8)
+    want = O.store_int8_rows(O.tensor_bf16_bits(xs))
+    assert np.array_equal(got, want)
+    assert np.array_equal(_c_rows(xs), want)
+    if kernel == "unaligned":
+        flat = gold["cache"].reshape(-1, 528)
+        keep = gold["slots"] >= 0
+        assert np.array_equal(got[keep], flat[gold["slots"][keep]])
+
+
 def test_uint8_cache_and_unaligned_rows(native_lib, cuda_device):
     """A uint8 cache and an x view whose rows are not 16-byte aligned (scalar kernel)."""
     from kernels.titan_kv import store_int8

@@ -116,3 +116,65 @@ def test_errors(native_lib, cuda_device):
         S.split_align(torch.zeros(1, 8, dtype=torch.int32, device=cuda_device), 287, buf)  # E mismatch
     with pytest.raises(AssertionError):
         S.split_align(torch.zeros(0, 8, dtype=torch.int32, device=cuda_device), 288, buf)  # T == 0
+
+
+def test_int64_ids_narrowed_like_the_reference(native_lib, cuda_device):
+    """int64 ids that do not fit in int32 are narrowed by wrapping, as the
+    reference's `.to(torch.int32)` does (moe_split_align.py:207-209): 2^32 + 5
+    becomes expert 5, -2^32 + 3 becomes 3, 2^31 becomes -2^31 (dropped)."""
+    E, t_max = 288, 64
+    wide = np.array([[2 ** 32 + 5, -(2 ** 32) + 3, 2 ** 31, 7, 2 ** 33 + 287, -1, 2 ** 32 + 288, 5]], np.int64)
+    want = O.moe_split_align(wide, E, t_max)
+    narrowed = torch.from_numpy(wide).to(torch.int32).numpy()
+    assert narrowed.tolist() == [[5, 3, -2 ** 31, 7, 287, -1, 288, 5]]
+    _assert_equal(want, O.moe_split_align(narrowed, E, t_max), "oracle wraps like torch")
+    _assert_equal(_run(wide, E, t_max, cuda_device, torch.int64), want, "kernel")
+
+
+def test_noncontiguous_ids_and_foreign_buffers(native_lib, cuda_device):
+    """A strided id view gives the contiguous ids' lists; buffers on another
+    device than the ids are refused."""
+    from kernels import titan_moe_split_align as S
+    rng = np.random.default_rng(11)
+    wide = torch.from_numpy(rng.integers(0, 288, (64, 16)).astype(np.int32)).to(cuda_device)
+    view = wide.reshape(-1)[::2]                          # 1-D, stride 2: reshape(-1) keeps the view
+    assert not view.is_contiguous()
+    buf = S.buffers(512, 288, cuda_device)
+    got = [(bs, s.cpu().numpy(), e.cpu().numpy(), int(n.item())) for bs, s, e, n in S.split_align(view, 288, buf)]
+    want = O.moe_split_align(view.cpu().numpy(), 288, 512)
+    for (bs, s, e, n), (_, ws, we, wn) in zip(got, want):
+        assert n == wn and np.array_equal(s[:n], ws[:n]) and np.array_equal(e[:n // bs], we[:n // bs])
+    cpu_buf = S.buffers(512, 288, torch.device("cpu"))
+    with pytest.raises(ValueError):
+        S.split_align(view, 288, cpu_buf)
+
+
+def test_eight_cta_cluster(native_lib, cuda_device, tmp_path):
+    """The portable 8-CTA cluster (what a device that cannot hold a 16-CTA
+    cluster runs), forced by TITAN_SPLIT_ALIGN_CLUSTER=8 in a fresh process:
+    bit-exact against the oracle for several sizes, expert counts and skews."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    script = tmp_path / "split8.py"
+    script.write_text(f"""
+import sys
+sys.path[:0] = [{str(root)!r}, {str(root / 'glm-5.3-kernels_b200')!r}]
+import numpy as np, torch
+from tests.test_gpu_moe_split_align import _run, _assert_equal
+from oracle import oracle as O
+dev = torch.device('cuda:0')
+for M, E, zipf in ((1, 288, False), (333, 288, False), (2304, 288, True), (8192, 288, False), (512, 1024, False)):
+    rng = np.random.default_rng(M + E)
+    if zipf:
+        w = 1.0 / np.arange(1, E + 1) ** 1.1
+        routes = rng.choice(E, size=(M, 8), p=w / w.sum()).astype(np.int32)
+    else:
+        routes = rng.integers(-2, E + 2, (M, 8)).astype(np.int32)
+    _assert_equal(_run(routes, E, M * 8 + 5, dev), O.moe_split_align(routes, E, M * 8 + 5), (M, E))
+print('split8 ok')
+""")
+    env = dict(__import__("os").environ, TITAN_SPLIT_ALIGN_CLUSTER="8")
+    r = subprocess.run([sys.executable, str(script)], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "split8 ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]

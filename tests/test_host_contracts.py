@@ -55,13 +55,6 @@ def test_no_triton_or_vllm_imports():
         assert not re.search(r"^\s*(import|from)\s+(triton|vllm)\b", text, re.M), f
 
 
-def test_split_heuristic_matches_restatement():
-    from kernels.titan_mla import _choose_num_kv_splits
-    for T, G, topk, sms in itertools.product((0, 1, 2, 3, 5, 8, 16, 37, 64), (1, 2, 3), (0, 32, 128, 256, 2176, 2048, 96),
-                                             (70, 132, 148, 160)):
-        assert _choose_num_kv_splits(T, G, topk, sms) == O.choose_num_kv_splits(T, G, topk, sms), (T, G, topk, sms)
-
-
 # (cluster size, co-resident clusters, clusters with one CTA per SM) of the MLA
 # kernel on a 148-SM B200, as titan_mla_max_active_clusters /
 # titan_mla_max_exclusive_clusters report them.

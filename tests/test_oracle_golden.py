@@ -61,8 +61,40 @@ def test_kv_reference_quantisation_criteria(kv_golden):
     expected = np.maximum(np.abs(x).max(1), 127e-12) / 127
     np.testing.assert_allclose(scales[finite], expected[finite].astype(np.float32), rtol=1e-6, atol=1e-12)
     ints = rows[:, :512].view(np.int8).astype(np.float32)
-    assert np.abs(ints - np.clip(np.round(x / scales[:, None]), -127, 127)).max() <= 1
+    assert np.abs(ints[finite] - np.clip(np.round(x[finite] / scales[finite, None]), -127, 127)).max() <= 1
     assert not rows[:, 516:].any()
+
+
+def test_kv_nonfinite_rows(kv_golden):
+    """Rows with NaN or inf, as the reference's NaN-dropping max / maximum /
+    minimum treat them: NaN values are ignored by the row max and store -127;
+    an infinite value makes the scale infinite, so finite values store 0 and
+    +-inf (inf / inf = NaN) store -127; an all-NaN row keeps the 1e-12 floor."""
+    x = O.bf16_bits_to_f32(kv_golden["x_bits"])
+    flat = kv_golden["cache"].reshape(-1, 528)
+    slots = kv_golden["slots"]
+    seen_nan = seen_inf = 0
+    for r in range(x.shape[0]):
+        if np.isfinite(x[r]).all() or slots[r] < 0:
+            continue
+        row = flat[slots[r]]
+        q = row[:512].view(np.int8)
+        scale = row[512:516].copy().view(np.float32)[0]
+        nan = np.isnan(x[r])
+        assert (q[nan] == -127).all()
+        if np.isinf(x[r]).any():
+            seen_inf += 1
+            assert np.isinf(scale) and scale > 0
+            assert (q[np.isinf(x[r])] == -127).all() and (q[np.isfinite(x[r])] == 0).all()
+        elif nan.all():
+            assert scale == np.float32(1e-12)
+        else:
+            seen_nan += 1
+            finite = ~nan
+            assert scale == np.float32(np.abs(x[r][finite]).max() / np.float32(127))
+            want = np.clip(np.rint(x[r][finite] / scale), -127, 127)
+            assert np.array_equal(q[finite].astype(np.float32), want)
+    assert seen_nan >= 2 and seen_inf >= 3
 
 
 def _moe_cases(golden):
