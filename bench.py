@@ -652,6 +652,19 @@ def run_ours(args, dist):
             split[f"M{M}_{dist_name}_in_graph_us"] = statistics.median(samples)
             gs.reset()
     secondary["moe_split_align"] = split
+
+    # ---- the reference's own Triton kernels on this B200 (rank 0 of a
+    # single-GPU run only; comparison lines, not our path)
+    if rank == 0 and world == 1 and not args.skip_reference_triton:
+        ref = load_reference_triton()
+        if ref is None:
+            secondary["reference_triton_b200"] = {"unavailable": "baseline/_ref is not installed"}
+        else:
+            try:
+                secondary["reference_triton_b200"] = reference_triton_b200(ref, kvs, lat, slots, flush, sms, K,
+                                                                           caches[0])
+            except Exception as exc:  # a Triton compile or launch failure is reported, not fatal
+                secondary["reference_triton_b200"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     clocks = sampler.stop()
     dist.barrier()
 
@@ -690,6 +703,19 @@ def run_ours(args, dist):
                                           "output into pinned host memory (out=)",
                     "issue": f"public-API steps captured in a CUDA graph, {Je} per replay, L2 flushed before "
                              "each timed replay; eager loops in secondary"},
+            # The sharded workloads (the ones whose 1 -> N curve can bend):
+            # config 3 (B=8, tokens split over the ranks) and config 4
+            # (prefill T=4096 split over the ranks), max-over-ranks device time.
+            "sharded": {
+                "decode_b8": {"us_per_call": secondary["decode_b8"]["us_per_call"],
+                              "tokens_per_s": secondary["decode_b8"]["tokens_per_s"],
+                              "tokens_per_rank": secondary["decode_b8"]["tokens_per_rank"],
+                              "per_gpu_roofline_frac": secondary["decode_b8"]["GBps_per_rank"] / peak},
+                **({"prefill_t4096": {"ms_per_call": secondary["prefill_t4096"]["ms_per_call"],
+                                      "tokens_per_s": secondary["prefill_t4096"]["tokens_per_s"],
+                                      "tokens_per_rank": secondary["prefill_t4096"]["tokens_per_rank"],
+                                      "per_gpu_tflops": secondary["prefill_t4096"]["tflops"]}}
+                   if "prefill_t4096" in secondary else {})},
             "gpu_launches": K * launches_per_call,
             "cache_replicas_identical_across_ranks": cache_identical,
             "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"], "reasons": clocks["reasons"],
@@ -703,6 +729,109 @@ def run_ours(args, dist):
 
 
 CPU_INDEX_SEED = 99   # the B=1 index sets both CPU legs time (the headline's rank-0 seed)
+
+
+def load_reference_triton():
+    """The reference's own modules (titan_kv, titan_mla, titan_moe_align) from
+    baseline/_ref, the unmodified package pip-installed from the reference
+    checkout, loaded under private names; None when it is not installed."""
+    import importlib.util
+    ref_dir = ROOT / "baseline" / "_ref"
+    mods = {}
+    for name in ("titan_kv", "titan_mla", "titan_moe_align"):
+        path = ref_dir / f"{name}.py"
+        if not path.exists():
+            return None
+        spec = importlib.util.spec_from_file_location(f"reference_{name}", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mods[name] = mod
+    return mods
+
+
+def reference_triton_b200(ref, kvs, lat, slots, flush, sms, K, ours):
+    """The reference's Triton kernels JIT-compiled for this B200 and called
+    through their public API (its split heuristic, autotuner and merge kernel
+    included), on the same inputs and timing protocol as our lines: a
+    comparison of the two implementations on one box, not a shipped path
+    (the reference targets SM80; no Triton runs on our path)."""
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    mla, kv, moe = ref["titan_mla"], ref["titan_kv"], ref["titan_moe_align"]
+    out = {"what": "reference Triton on B200 (not a shipped sm_100 path): baseline/_ref, public API, "
+                   "same inputs and protocol as the lines above"}
+    dev = kvs[0].device
+    # Same inputs, both implementations: outputs within the path tolerance.
+    q, idx = decode_sets(8, 1, 4321, tail_mode="random")
+    q, idx = q[0].to(dev), idx[0].to(dev)
+    a = attn(q, kvs[0], idx, SM_SCALE, sm_count=sms).float()
+    b = mla.triton_mla_sparse_attention(q, kvs[0], idx, SM_SCALE, sm_count=sms).float()
+    out["b8_outputs_max_abs_diff"] = float((a - b).abs().max())
+    out["b8_outputs_within_tolerance"] = bool(((a - b).abs() <= 2e-2 + 1e-2 * b.abs()).all())
+    J = graph_calls(K)
+    d1 = DecodeBench(mla.triton_mla_sparse_attention, kvs, 1, J, 99, "fixed", sms)
+    d1.time(1, flush)
+    out["decode_b1_us_per_call"] = sum(d1.time(max(1, K // J), flush)) / (max(1, K // J) * J) * 1000.0
+    d1.close()
+    J8 = graph_calls(min(K, 256))
+    d8 = DecodeBench(mla.triton_mla_sparse_attention, kvs, 8, J8, 777, "random", sms)
+    d8.time(1, flush)
+    out["decode_b8_us_per_call"] = sum(d8.time(max(1, min(K, 256) // J8), flush)) / (
+        max(1, min(K, 256) // J8) * J8) * 1000.0
+    d8.close()
+    ip = prefill_indices(4096, 4242).to(dev)
+    qp = torch.randn(4096, HEADS, 512, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(
+        torch.bfloat16)
+    run = lambda k: mla.triton_mla_sparse_attention(qp, kvs[0], ip, SM_SCALE, sm_count=sms)  # noqa: E731
+    timed_cold(run, 2, flush)
+    out["prefill_t4096_ms_per_call"] = statistics.fmean(timed_cold(run, 3, flush))
+    cache = torch.empty(KV_ROWS // BLOCK, BLOCK, ROW_BYTES, dtype=torch.int8, device=dev)
+    a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for perm in (False, True):
+        sl = torch.randperm(KV_ROWS, device=dev) if perm else slots
+        for _ in range(2):
+            kv.store_int8(lat, cache, sl)
+        a_ev.record()
+        for _ in range(10):
+            kv.store_int8(lat, cache, sl)
+        b_ev.record()
+        torch.cuda.synchronize()
+        us = a_ev.elapsed_time(b_ev) * 100.0
+        out["store_int8_random_perm_us" if perm else "store_int8_us"] = us
+        if not perm:
+            out["store_int8_GBps"] = KV_ROWS * (1024 + ROW_BYTES + 8) / (us * 1e-6) / 1e9
+            # Bytes against ours: the reference divides with an approximate
+            # fp32 division (its own test allows +-1), ours with the IEEE one.
+            diff = (cache.view(-1, ROW_BYTES)[:, :512].int() - ours.view(-1, ROW_BYTES)[:, :512].int()).abs()
+            out["store_int8_int8_values_differing"] = int((diff > 0).sum())
+            out["store_int8_int8_max_abs_diff"] = int(diff.max())
+    gm = torch.Generator().manual_seed(37)
+    for B in (1, 8):
+        ids = torch.stack([torch.randperm(288, generator=gm)[:8] for _ in range(B)]).to(torch.int32).to(dev)
+        gr, _ = capture(lambda: moe.titan_moe_align_small(ids))
+        for _ in range(5):
+            gr.replay()
+        samples = []
+        for _ in range(5):
+            a_ev.record()
+            for _ in range(100):
+                gr.replay()
+            b_ev.record()
+            torch.cuda.synchronize()
+            samples.append(a_ev.elapsed_time(b_ev) * 1000 / 100)
+        out[f"moe_align_B{B}_us"] = statistics.median(samples)
+        gr.reset()
+        g100, _ = capture(lambda: [moe.titan_moe_align_small(ids) for _ in range(100)])
+        g100.replay()
+        samples = []
+        for _ in range(5):
+            a_ev.record()
+            g100.replay()
+            b_ev.record()
+            torch.cuda.synchronize()
+            samples.append(a_ev.elapsed_time(b_ev) * 1000 / 100)
+        out[f"moe_align_B{B}_in_graph_us"] = statistics.median(samples)
+        g100.reset()
+    return out
 
 
 def cpu_model():
@@ -848,6 +977,8 @@ def main():
                     help="time bound of both CPU legs (reference arm and cpu_baseline)")
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-reference-triton", action="store_true",
+                    help="skip the secondary lines of the reference's Triton kernels run on this GPU")
     ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1", "split_align"),
                     default=None,
                     help="run only this workload (warmup + steps calls) as an ncu target; prints nothing")

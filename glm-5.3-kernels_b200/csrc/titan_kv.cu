@@ -186,37 +186,46 @@ constexpr int kKvStreamStages = 4;
 constexpr int kKvStageBytes = 2 * 1024;  // two rows
 constexpr size_t kKvStreamSmem = (size_t)kKvStreamWarps * kKvStreamStages * kKvStageBytes;
 
-__device__ __forceinline__ uint32_t umax16x2(uint32_t a, uint32_t b) {
+// Packed bf16 max of magnitudes: |result| = max(|a|, |b|) per half (the
+// sign is the XOR of the inputs' signs and is masked off by the caller); a
+// NaN operand gives NaN (0x7FFF after masking), so a non-finite row is seen.
+__device__ __forceinline__ uint32_t bf16x2_absmax(uint32_t a, uint32_t b) {
   uint32_t d;
-  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
 
 // 32 values (16 bf16x2 words) of one row held by one lane -> 8 packed int8
-// words, four values at a time (same arithmetic and fallback as quant16).
-// y = v * rcp and the rounding residual d = y - rint(y) (exact) are packed
-// f32x2 operations.  The window test stays per group of four values: a warp
-// executes the exact path whenever any of its lanes needs it, so a wider
-// group would multiply the divisions executed (one lane in a 32-value group
-// hits the window for ~12 % of warp steps).
+// words, four values at a time, on packed f32x2 arithmetic.  With
+// rcp = fl(1/scale) the product p = v * rcp is taken exactly inside an FMA
+// and rounded once to an integer by adding 1.5 * 2^23: m = RN(p + magic)
+// holds rint(p), ties to even.  |p - v/scale| <= |v/scale| 2^-24 <= 7.6e-6
+// and the correctly rounded quotient Q = fl(v/scale) is within 2^-18 of
+// v/scale, so |p - Q| < 1.15e-5: rint(p) = rint(Q) unless p lies within
+// 1.15e-5 of a half-integer.  The residual d = RN(p - rint(p)) (again one
+// FMA) flags such values, |d| > 0.5 - 2^-14 (window 6.1e-5, ~5x margin);
+// their group of four is recomputed with the IEEE division.  The window test
+// stays per group of four values: a warp executes the exact path whenever
+// any of its lanes needs it, so wider groups would multiply the divisions.
 __device__ __forceinline__ void quant32(const uint32_t (&w)[16], float scale, float rcp, uint32_t (&out)[8]) {
   const float2 rcp2 = make_float2(rcp, rcp);
   const float2 mag2 = make_float2(kRoundMagic, kRoundMagic);
-  const float2 nmag2 = make_float2(-kRoundMagic, -kRoundMagic);
   const float2 neg1 = make_float2(-1.0f, -1.0f);
+  constexpr float kWindow = 0.49993896484375f;  // 0.5 - 2^-14
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     float2 m[2];
-    float dmax = 0.0f;
+    bool near_half = false;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const uint32_t wd = w[2 * k + e];
-      const float2 y = __fmul2_rn(make_float2(__uint_as_float(wd << 16), __uint_as_float(wd & 0xFFFF0000u)), rcp2);
-      m[e] = __fadd2_rn(y, mag2);
-      const float2 d = __ffma2_rn(__fadd2_rn(m[e], nmag2), neg1, y);
-      dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
+      const float2 v = make_float2(__uint_as_float(wd << 16), __uint_as_float(wd & 0xFFFF0000u));
+      m[e] = __ffma2_rn(v, rcp2, mag2);                      // magic + rint(v * rcp)
+      const float2 nr = __ffma2_rn(m[e], neg1, mag2);         // -rint(v * rcp), exact
+      const float2 d = __ffma2_rn(v, rcp2, nr);               // RN(v * rcp - rint(v * rcp))
+      near_half |= (fabsf(d.x) > kWindow) | (fabsf(d.y) > kWindow);
     }
-    if (dmax > 0.49993896484375f) {  // a value within 2^-14 of a half-integer: exact quotient
+    if (near_half) {  // a value within 2^-14 of a half-integer: exact quotient
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t wd = w[2 * k + e];
@@ -276,10 +285,10 @@ __global__ void __launch_bounds__(kKvStreamWarps * 32, 3)
       w[4 * k + 2] = c.z;
       w[4 * k + 3] = c.w;
     }
-    uint32_t mx = 0;
+    uint32_t mx = w[0];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) mx = umax16x2(mx, w[k] & 0x7FFF7FFFu);
-    mx = max(mx & 0xFFFFu, mx >> 16);  // |x| as bf16 bits; integer order = value order
+    for (int k = 1; k < 16; ++k) mx = bf16x2_absmax(mx, w[k]);
+    mx = max(mx & 0x7FFFu, (mx >> 16) & 0x7FFFu);  // |x| as bf16 bits; integer order = value order
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     uint32_t q[8];
