@@ -523,6 +523,8 @@ def run_ours(args, dist):
     torch.cuda.synchronize()
     st_ms = dist.max(a.elapsed_time(b) / nf)
     perm = torch.randperm(KV_ROWS, device=dev)
+    for _ in range(2):
+        store_int8(lat, caches[1], perm)
     a.record()
     for _ in range(nf):
         store_int8(lat, caches[1], perm)

@@ -124,6 +124,22 @@ __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t &lo, uint32_
   hi = prmt(__float_as_uint(f23.x), __float_as_uint(f23.y), 0x7632u);
 }
 
+// Four int8 in one word -> two f16x2 words (bytes 0,1 -> lo; bytes 2,3 ->
+// hi), exactly: each byte is biased to u = x + 128 and placed in the low
+// mantissa byte of 1024 (f16 bits 0x64uu = 1024 + u, ulp 1 in [1024, 2048));
+// one packed f16 add of -1152 then leaves x, exact since |x| <= 128.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t magic = 0x64646464u;
+  const uint32_t bias = 0xE480E480u;  // f16x2 {-1152, -1152}
+  const uint32_t a = prmt(u, magic, 0x4140u), b = prmt(u, magic, 0x4342u);
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(bias));
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(bias));
+}
+
+// 2^e as a float, exact, for -126 <= e <= 127 (0 below).
+__device__ __forceinline__ float exp2i(int e) { return e < -126 ? 0.0f : __int_as_float((e + 127) << 23); }
+
 // 8x8 b16 matrix transpose across the warp (standard fragment layout).
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
   uint32_t d;
@@ -139,6 +155,21 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// D += A * B, m16n8k16, f16 inputs, fp32 accumulate (exact products).
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {

@@ -23,13 +23,17 @@
 //    The indices reach shared memory through warp 0's 4-byte cp.async ring
 //    five tiles ahead (paged: positions eight and block-table entries five
 //    tiles ahead), so no thread waits on a load issued one tile earlier.
-//  * QK: mma.sync m16n8k16 bf16 (A = 16 heads x 16 dims of q in registers).
-//    The k dimension is permuted identically for q and k so that each lane's
-//    16 contiguous bytes feed four k-steps.  The 8 warps' partial scores meet
-//    in shared memory; 16 lanes per head run the online softmax.
-//  * PV: the bf16 K fragments are transposed in registers with movmatrix (rows
-//    become the reduction dim), A = bf16(p * scale) from shared memory; each
-//    accumulator lane then owns 16 contiguous output dims.
+//  * QK: mma.sync m16n8k16 f16 with fp32 accumulate (A = 16 heads x 16 dims
+//    of q in registers).  int8 -> f16 is exact (one PRMT + one packed add per
+//    pair); q enters as f16 scaled by a power of two per warp and head, undone
+//    in the score reduction.  The k dimension is permuted identically for q
+//    and k so that each lane's 16 contiguous bytes feed four k-steps.  The 8
+//    warps' partial scores meet in shared memory; 16 lanes per head run the
+//    online softmax, whose running max moves only by steps above 8 (log2).
+//  * PV: the f16 K fragments are transposed in registers with movmatrix (rows
+//    become the reduction dim), A = f16(p * scale * 2^-e) from shared memory
+//    (e: exponent of the largest row scale so far); each accumulator lane
+//    then owns 16 contiguous output dims.
 //  * Split merge: the C <= 16 splits of a (token, head group) that form one
 //    thread-block cluster merge through distributed shared memory, each CTA
 //    reducing 512 / C dims; a single cluster writes the bf16 output directly.
@@ -50,7 +54,7 @@ constexpr int kWarps = 8;                   // 64 dims per warp
 constexpr int kThreads = kWarps * 32;
 constexpr int kBN = 32;                     // rows per tile (four 8-row n-tiles)
 constexpr int kRedStride = 40;              // floats per head row of a warp's partial scores
-constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (bf16, 32 rows + pad)
+constexpr int kPStrideWords = 36;           // 32-bit words per head row of P (f16, 32 rows + pad)
 constexpr int kMaxCluster = 16;
 constexpr int kRing = 3;                    // row-gather ring: tiles in flight ahead of the math + 1
 constexpr int kIdxRing = 8;                 // index ring: indices are staged up to eight tiles ahead
@@ -59,10 +63,12 @@ constexpr int kGroupBytes = 4 * kRowPitch;  // one gather4 load: 2176 B, a multi
 constexpr int kGroups = kBN / 4;            // gather4 loads per tile
 constexpr float kNegLarge = -1.0e30f;       // finite mask sentinel, kernels/titan_mla.py:112
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kLazyMax = 8.0f;            // the running max moves when a tile exceeds it by more (log2 units)
+constexpr int kF16MinTiles = 16;            // single-pass CTAs of at least this many tiles use the f16 arithmetic
 
 struct Smem {
   float red[kWarps][kHeads * kRedStride];  // partial scores of each warp
-  uint32_t p[kHeads * kPStrideWords];      // bf16(p * scale), n-order
+  uint32_t p[kHeads * kPStrideWords];      // f16(p * scale * 2^-e), n-order
   float rcv[kHeads * kD];                  // cluster merge: [C][16][512/C] slices pushed by the peers
   union alignas(128) {
     float stage[kHeads * kD];              // cluster merge: this CTA's acc as [owner][16][512/C]
@@ -75,6 +81,7 @@ struct Smem {
   float2 cml[kMaxCluster][kHeads];         // cluster merge: (m, l) pushed by each peer
   alignas(8) uint8_t vbits[kRing][kGroups];  // per stage and gather4 group: bit k = slot k valid
   float scale[kBN];                        // row scales of the current tile, n-order (masked: unused)
+  float qf[kWarps][kHeads];                // 2^-kq: undoes warp w's f16 scaling of head h's q
   float alpha[kHeads];
   float2 ml[kHeads];                       // final (m, l) of this CTA
   float cw[kMaxCluster][kHeads];           // cluster merge weights
@@ -181,7 +188,12 @@ __device__ __forceinline__ void merge_cluster_partials(const Params &p, int t, i
 
 // kCluster: launched with clusters of C >= 2 CTAs (the cluster merge is
 // compiled only into these instantiations; C == 1 launches carry none of it).
-template <bool kPartialOut, bool kPaged, bool kCluster>
+// kF16: the f16 arithmetic (exact int8 -> f16 in one PRMT + one packed add
+// per pair, q scaled per warp and head, P relative to the largest row scale),
+// for single-pass CTAs that walk many tiles (prefill shapes): fewer
+// instructions per tile, at a fixed cost per CTA that short (decode) CTAs do
+// not recover; those keep the reference's bf16 arithmetic.
+template <bool kPartialOut, bool kPaged, bool kCluster, bool kF16 = false>
 __global__ void __launch_bounds__(kThreads, 2)
     sparse_mla_kernel(const Params p, const __grid_constant__ CUtensorMap rows_map) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -344,9 +356,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       cp_async_commit();
       cp_async_wait<0>();
     }
-    __syncthreads();
-    if (n_tiles > 0) issue(0, 0);
-    if (n_tiles > 1) issue(1, 1);
   } else {
     if (warp == 0 && n_tiles > 2) {  // ring copies first: in flight with the direct loads
 #pragma unroll 1
@@ -354,36 +363,79 @@ __global__ void __launch_bounds__(kThreads, 2)
       cp_async_commit();
     }
     issue_first_two();
+  }
+
+  if constexpr (kPaged) {
+    __syncthreads();
+    if (n_tiles > 0) issue(0, 0);
+    if (n_tiles > 1) issue(1, 1);
+  } else {
     if (warp == 0 && n_tiles > 2) cp_async_wait<0>();
     __syncthreads();
   }
 
-  // q fragments for this warp's 64 dims (A operand of QK), 4 k-steps.
-  uint32_t qa[4][4];
+  // q of this warp's 64 dims for heads g and g + 8 (A operand of QK), loaded
+  // after the gathers of tiles 0 and 1 are issued: loads issued ahead of the
+  // index loads delay the index -> row chain (B=1 +0.55 us when q went
+  // first), while here their latency hides behind the rows in flight.
+  const int dim0 = warp * 64 + c * 16;
+  uint4 qr[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
   {
     const int h0 = hg * kHeads + g, h1 = h0 + 8;
-    const int dim0 = warp * 64 + c * 16;
-    uint4 r0a = make_uint4(0, 0, 0, 0), r0b = r0a, r1a = r0a, r1b = r0a;
     const __nv_bfloat16 *qt = p.q + (int64_t)t * p.q_st;
     if (h0 < p.H) {
       const uint4 *src = reinterpret_cast<const uint4 *>(qt + (int64_t)h0 * p.q_sh + dim0);
-      r0a = src[0];
-      r0b = src[1];
+      qr[0] = src[0];
+      qr[1] = src[1];
     }
     if (h1 < p.H) {
       const uint4 *src = reinterpret_cast<const uint4 *>(qt + (int64_t)h1 * p.q_sh + dim0);
-      r1a = src[0];
-      r1b = src[1];
+      qr[2] = src[0];
+      qr[3] = src[1];
     }
-    const uint32_t w0[8] = {r0a.x, r0a.y, r0a.z, r0a.w, r0b.x, r0b.y, r0b.z, r0b.w};
-    const uint32_t w1[8] = {r1a.x, r1a.y, r1a.z, r1a.w, r1b.x, r1b.y, r1b.z, r1b.w};
+  }
+
+  // q fragments (A operand of QK): k-step s of this lane uses dims
+  // 16 c + 4 s + {0, 1} (regs 0, 1: heads g, g + 8) and + {2, 3} (regs 2, 3),
+  // the same permutation as the K fragments.  bf16 as given; for the f16
+  // MMAs, q is scaled per warp and head by a power of two 2^kq that puts the
+  // warp's largest |q| of the head in [2^14, 2^15): every bf16 value then
+  // converts exactly unless it is below 2^-24 of that largest value (f16
+  // subnormal range; absolute error <= 2^-25 of it), and the score reduction
+  // multiplies this warp's partial scores by 2^-kq (qf, published to the
+  // reducing threads by the first tile's first barrier).
+  uint32_t qa[4][4];
+  {
+    const uint32_t w[2][8] = {{qr[0].x, qr[0].y, qr[0].z, qr[0].w, qr[1].x, qr[1].y, qr[1].z, qr[1].w},
+                              {qr[2].x, qr[2].y, qr[2].z, qr[2].w, qr[3].x, qr[3].y, qr[3].z, qr[3].w}};
+    float qscale[2] = {1.0f, 1.0f};
+    if constexpr (kF16) {
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      qa[s][0] = w0[2 * s];
-      qa[s][1] = w1[2 * s];
-      qa[s][2] = w0[2 * s + 1];
-      qa[s][3] = w1[2 * s + 1];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t mx = 0;  // largest |q| as bf16 bits (integer order = value order)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx = max(mx, max(w[h][k] & 0x7FFFu, (w[h][k] >> 16) & 0x7FFFu));
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const int e = mx == 0 ? 0 : max((int)(mx >> 7) - 127, -126);  // floor(log2(largest |q|))
+        const int kq = min(14 - e, 126);
+        qscale[h] = exp2i(kq);
+        if (c == 0) sm.qf[warp][g + 8 * h] = exp2i(-kq);
+      }
     }
+#pragma unroll
+    for (int s2 = 0; s2 < 4; ++s2)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t wd = w[h][2 * s2 + half];
+          if constexpr (kF16)
+            qa[s2][2 * half + h] = pack_f16x2(__uint_as_float(wd << 16) * qscale[h],
+                                              __uint_as_float(wd & 0xFFFF0000u) * qscale[h]);
+          else
+            qa[s2][2 * half + h] = wd;
+        }
   }
 
   // Softmax state of head red_h, replicated over its 16 lanes.
@@ -396,6 +448,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int red_j = (tid & 15) * 2;  // its two n-order positions
   const int red_nt = red_j >> 3;
   const int red_n = red_j & 7;
+  float qf[kWarps];                  // 2^-kq of each warp for head red_h (read at the first tile)
+  // f16: the accumulator holds sum(p_r s_r v_r) / 2^e_acc: P enters the PV
+  // MMA as p_r s_r 2^-e with e the exponent of the largest row scale seen so
+  // far (s_r 2^-e < 2), so every P value is a normal f16 unless its
+  // contribution is below 2^-14 of that largest scale.
+  int e_acc = -127;
 
   // A ring wait that gives up (a gather that never landed: the device error
   // word is set) ends the tile loop for the whole CTA at the next barrier:
@@ -425,6 +483,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // Tile i's rows (this stage's k-th use has parity k & 1).
     const bool landed = mbar_wait_bounded(&sm.row_bar[st], (uint32_t)(i / kRing) & 1u, kLongWaitCycles);
+    // A tile whose 32 rows are all masked (no gather was issued for it; its
+    // validity bits were published by earlier barriers) contributes nothing:
+    // one barrier keeps the index-ring hand-over, the math is skipped.
+    if (*reinterpret_cast<const uint64_t *>(sm.vbits[st]) == 0) {
+      if (__syncthreads_or(!landed)) {
+        i_end = i + 1;
+        gave_up = true;
+        break;
+      }
+      st = st == kRing - 1 ? 0 : st + 1;
+      st_issue = st_issue == kRing - 1 ? 0 : st_issue + 1;
+      continue;
+    }
     const uint8_t *stage = sm.u.ring.rows[st][0];
     uint4 kb_cur[4];
 #pragma unroll
@@ -435,14 +506,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     // iteration's second barrier.
     if (warp == 0) sm.scale[lane] = *reinterpret_cast<const float *>(stage + row_offset(lane >> 3, lane & 7) + 512);
 
-    // ---- QK^T over this warp's 64 dims; keep the bf16 B fragments for PV.
+    // ---- QK^T over this warp's 64 dims; keep the f16 B fragments for PV.
     uint32_t kf[4][4][2];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
-      i8x4_to_bf16x4(kb_cur[nt].x, kf[nt][0][0], kf[nt][0][1]);
-      i8x4_to_bf16x4(kb_cur[nt].y, kf[nt][1][0], kf[nt][1][1]);
-      i8x4_to_bf16x4(kb_cur[nt].z, kf[nt][2][0], kf[nt][2][1]);
-      i8x4_to_bf16x4(kb_cur[nt].w, kf[nt][3][0], kf[nt][3][1]);
+      if constexpr (kF16) {
+        i8x4_to_f16x4(kb_cur[nt].x, kf[nt][0][0], kf[nt][0][1]);
+        i8x4_to_f16x4(kb_cur[nt].y, kf[nt][1][0], kf[nt][1][1]);
+        i8x4_to_f16x4(kb_cur[nt].z, kf[nt][2][0], kf[nt][2][1]);
+        i8x4_to_f16x4(kb_cur[nt].w, kf[nt][3][0], kf[nt][3][1]);
+      } else {
+        i8x4_to_bf16x4(kb_cur[nt].x, kf[nt][0][0], kf[nt][0][1]);
+        i8x4_to_bf16x4(kb_cur[nt].y, kf[nt][1][0], kf[nt][1][1]);
+        i8x4_to_bf16x4(kb_cur[nt].z, kf[nt][2][0], kf[nt][2][1]);
+        i8x4_to_bf16x4(kb_cur[nt].w, kf[nt][3][0], kf[nt][3][1]);
+      }
     }
     float sacc[4][4];
 #pragma unroll
@@ -450,7 +528,12 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int s = 0; s < 4; ++s)  // k-step outer: four independent accumulator chains interleave
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_bf16_16816(sacc[nt], qa[s], kf[nt][s][0], kf[nt][s][1]);
+      for (int nt = 0; nt < 4; ++nt) {
+        if constexpr (kF16)
+          mma_f16_16816(sacc[nt], qa[s], kf[nt][s][0], kf[nt][s][1]);
+        else
+          mma_bf16_16816(sacc[nt], qa[s], kf[nt][s][0], kf[nt][s][1]);
+      }
     {
       float *red = sm.red[warp];
 #pragma unroll
@@ -467,12 +550,16 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     // ---- Reduce the 8 partial scores, scale, mask, online softmax, P.
     {
+      if (kF16 && i == 0) {
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) qf[w] = sm.qf[w][red_h];
+      }
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
+      for (int w = 0; w < kWarps; ++w) {  // f16: each warp's partial in its own q scaling
         const float2 v = *reinterpret_cast<const float2 *>(&sm.red[w][red_h * kRedStride + red_j]);
-        s0 += v.x;
-        s1 += v.y;
+        s0 = kF16 ? fmaf(v.x, qf[w], s0) : s0 + v.x;
+        s1 = kF16 ? fmaf(v.y, qf[w], s1) : s1 + v.y;
       }
       const uint64_t vb = *reinterpret_cast<const uint64_t *>(sm.vbits[st]);
       const bool v0 = row_valid(vb, red_nt, red_n), v1 = row_valid(vb, red_nt, red_n + 1);
@@ -481,18 +568,39 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float x0 = v0 ? (s0 * sc0) * p.scale_log2 : kNegLarge;
       const float x1 = v1 ? (s1 * sc1) * p.scale_log2 : kNegLarge;
       float mx = fmaxf(x0, x1);
+      // Largest valid row scale of the tile, as bits (positive floats: bit
+      // order = value order; masked rows may hold stale bytes and count as 0).
+      uint32_t top = max(v0 ? __float_as_uint(sc0) : 0u, v1 ? __float_as_uint(sc1) : 0u);
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = ex2_approx(m_run - m_new);
+      for (int o = 8; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if constexpr (kF16) top = max(top, __shfl_xor_sync(0xffffffffu, top, o));
+      }
+      // The running max moves only when the tile's max exceeds it by more
+      // than kLazyMax (log2 units): p stays <= 2^kLazyMax, and most tiles
+      // leave the accumulator unscaled (alpha == 1 skips the rescale below).
+      // Any reference value gives the same softmax: acc and l share it.
+      const float m_cand = fmaxf(m_run, mx);
+      const float m_new = m_cand > m_run + kLazyMax ? m_cand : m_run;
+      const int e_new = kF16 ? max(e_acc, (int)(top >> 23) - 127) : 0;
+      const float am = m_new == m_run ? 1.0f : ex2_approx(m_run - m_new);
+      const float alpha = kF16 ? am * exp2i(e_acc - e_new) : am;
       const float p0 = v0 ? ex2_approx(x0 - m_new) : 0.0f;
       const float p1 = v1 ? ex2_approx(x1 - m_new) : 0.0f;
       float ps = p0 + p1;
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      l_run = l_run * alpha + ps;
+      l_run = l_run * am + ps;
       m_run = m_new;
-      sm.p[red_h * kPStrideWords + (red_j >> 1)] = pack_bf16x2(v0 ? p0 * sc0 : 0.0f, v1 ? p1 * sc1 : 0.0f);
+      // P = bf16(p s_r), rounded as kernels/titan_mla.py:175-176 does; f16:
+      // p s_r 2^-e_new (11 significant bits against bf16's 8).
+      if constexpr (kF16) {
+        const float pe = exp2i(-e_new);
+        sm.p[red_h * kPStrideWords + (red_j >> 1)] = pack_f16x2(v0 ? p0 * (sc0 * pe) : 0.0f, v1 ? p1 * (sc1 * pe) : 0.0f);
+      } else {
+        sm.p[red_h * kPStrideWords + (red_j >> 1)] = pack_bf16x2(v0 ? p0 * sc0 : 0.0f, v1 ? p1 * sc1 : 0.0f);
+      }
+      e_acc = e_new;
       if ((tid & 15) == 0) sm.alpha[red_h] = alpha;
     }
     __syncthreads();
@@ -500,12 +608,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- PV: acc[16 heads x 64 dims] += P[16 x 32] . V[32 x 64].
     {
       const float al0 = sm.alpha[g], al1 = sm.alpha[g + 8];
+      if (__any_sync(0xffffffffu, (al0 != 1.0f) | (al1 != 1.0f))) {
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        acc[n][0] *= al0;
-        acc[n][1] *= al0;
-        acc[n][2] *= al1;
-        acc[n][3] *= al1;
+        for (int n = 0; n < 8; ++n) {
+          acc[n][0] *= al0;
+          acc[n][1] *= al0;
+          acc[n][2] *= al1;
+          acc[n][3] *= al1;
+        }
       }
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) {
@@ -520,7 +630,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int x = 0; x < 2; ++x) {
             const uint32_t b0 = movmatrix_trans(kf[2 * ks][s][x]);
             const uint32_t b1 = movmatrix_trans(kf[2 * ks + 1][s][x]);
-            mma_bf16_16816(acc[2 * s + x], a, b0, b1);
+            if constexpr (kF16)
+              mma_f16_16816(acc[2 * s + x], a, b0, b1);
+            else
+              mma_bf16_16816(acc[2 * s + x], a, b0, b1);
           }
         }
       }
@@ -537,11 +650,20 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Every issued gather was waited for; warp 0's index copies beyond the
   // last tile are empty groups.  The ring is dead from here.
   cp_async_wait<0>();
+  if constexpr (kF16) {  // back to the scale of the cache values: acc = sum(p_r s_r v_r)
+    const float es = exp2i(e_acc);
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      acc[n][0] *= es;
+      acc[n][1] *= es;
+      acc[n][2] *= es;
+      acc[n][3] *= es;
+    }
+  }
 
   // ---- Epilogue.  Lane (g, c) of warp w holds, for heads g and g + 8,
   // dims 64 w + 16 c + j at acc[2 s + x][2 half + e] with j = 4 s + 2 x + e.
   if ((tid & 15) == 0) sm.ml[red_h] = make_float2(m_run, l_run);
-  const int dim0 = warp * 64 + c * 16;
   const int C = kCluster ? p.C : 1;
   const int cl = split / C;  // partial index when kPartialOut
   if constexpr (!kCluster) {
@@ -936,11 +1058,12 @@ static int prepare_device(size_t smem, const int **capacity) {
       *capacity = g_cluster_capacity[dev];
       return TITAN_OK;
     }
-    void (*kernels[8])(const Params, const CUtensorMap) = {
-        sparse_mla_kernel<false, false, false>, sparse_mla_kernel<true, false, false>,
-        sparse_mla_kernel<false, true, false>,  sparse_mla_kernel<true, true, false>,
-        sparse_mla_kernel<false, false, true>,  sparse_mla_kernel<true, false, true>,
-        sparse_mla_kernel<false, true, true>,   sparse_mla_kernel<true, true, true>};
+    void (*kernels[10])(const Params, const CUtensorMap) = {
+        sparse_mla_kernel<false, false, false>,      sparse_mla_kernel<true, false, false>,
+        sparse_mla_kernel<false, true, false>,       sparse_mla_kernel<true, true, false>,
+        sparse_mla_kernel<false, false, true>,       sparse_mla_kernel<true, false, true>,
+        sparse_mla_kernel<false, true, true>,        sparse_mla_kernel<true, true, true>,
+        sparse_mla_kernel<false, false, false, true>, sparse_mla_kernel<false, true, false, true>};
     for (auto k : kernels) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -1213,7 +1336,13 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   cfg.attrs = attr;
   cfg.numAttrs = C > 1 ? 2 : 1;
   cudaError_t e;
-  if (paged != nullptr)
+  // Single-pass CTAs that walk at least kF16MinTiles tiles (prefill shapes)
+  // take the f16 arithmetic.
+  const bool f16 = C == 1 && NC == 1 && (prm.split_topk + kBN - 1) / kBN >= kF16MinTiles;
+  if (f16)
+    e = paged != nullptr ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true, false, true>, prm, rows_map)
+                         : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false, false, true>, prm, rows_map);
+  else if (paged != nullptr)
     e = C > 1 ? (NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true, true>, prm, rows_map)
                         : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, true, true>, prm, rows_map))
               : (NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, true, false>, prm, rows_map)

@@ -8,94 +8,95 @@
 //   sorted_ids[off_e + rank_j] = j  (rest = R),  expert_ids[off_e/8 + b] = e (rest = -1),
 //   postpad  = sum pad_e.
 //
-// B200 design: one warp computes everything with warp primitives instead of
-// the reference's R x R pairwise compare.  Routes j and j + 32 live in lane j.
-// Ranks come from __match_any_sync (peer mask) and a popcount of the lower
-// lanes; the 288 expert counts live in shared memory; the padded offsets are
-// a warp prefix scan with 9 experts per lane (32 x 9 = 288).  The result is
-// assembled in shared memory and written with 16-byte stores (4-byte stores
-// when an output is not 16-byte aligned).
+// B200 design: one warp computes everything in registers; nothing scales with
+// the 288 experts, only with the R <= 64 routes.  Routes j and j + 32 live in
+// lane j.  Every lane walks the R routes once by warp shuffles (the ids of
+// route k broadcast from lane k & 31) and counts, for each of its routes,
+// the equal experts before it (its rank) and in total (its count); a route
+// of rank 0 "leads" its expert and carries the expert's padded count.  A
+// second walk sums, for each route, the padded counts of the leaders of
+// smaller experts: that is its expert's offset.  The layout is assembled in
+// shared memory and written with 16-byte stores (4-byte stores when an
+// output is not 16-byte aligned).  Removing the 288-entry count table, its
+// zeroing and its scan shortens the single warp's serial chain.
 #include "titan_common.cuh"
+
+#include <type_traits>
 
 namespace titan {
 
 constexpr int kMoeMaxRoutes = 64;  // B <= 8, top-8
 constexpr int kMoeExperts = TITAN_MOE_NUM_EXPERTS;
-constexpr int kMoePerLane = kMoeExperts / 32;  // 9
-static_assert(kMoePerLane * 32 == kMoeExperts, "expert count must split evenly over a warp");
 
-template <typename IdT>
-__global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restrict__ ids, int R,
+template <typename IdT, int R>
+__global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restrict__ ids,
                                                               int32_t *__restrict__ sorted_ids,
                                                               int32_t *__restrict__ expert_ids,
                                                               int32_t *__restrict__ postpad, bool vec_out) {
+  constexpr bool kTwoHalves = R > 32;
   // The whole layout is built by warp 0: no CTA-wide barrier sits on the
   // critical path, which starts with the route-id loads.  Extra warps (the
   // caller's num_warps) have nothing to do.
   if (threadIdx.x >= 32) return;
-  __shared__ __align__(16) int s_count[kMoeExperts];
-  __shared__ __align__(16) int s_offset[kMoeExperts];
   __shared__ __align__(16) int s_sorted[kMoeMaxRoutes * 8];
   __shared__ __align__(16) int s_experts[kMoeMaxRoutes];
   const int lane = threadIdx.x;
-  const unsigned lt = (1u << lane) - 1u;
 
   // Route lane (half 0) and lane + 32 (half 1).  Validity is decided on the
   // full-width id, before narrowing (an int64 id of 2^32 + 5 is invalid).
   long long raw0 = -1, raw1 = -1;
   if (lane < R) raw0 = (long long)ids[lane];
-  if (lane + 32 < R) raw1 = (long long)ids[lane + 32];
+  if (kTwoHalves && lane + 32 < R) raw1 = (long long)ids[lane + 32];
 
   // Initialise while the loads are in flight: padding = R, unused blocks = -1.
   const int4 pad4 = make_int4(R, R, R, R);
   for (int i = lane; i < 2 * R; i += 32) reinterpret_cast<int4 *>(s_sorted)[i] = pad4;  // 8R ints
   for (int i = lane; i < R; i += 32) s_experts[i] = -1;
-  for (int i = lane; i < kMoeExperts; i += 32) s_count[i] = 0;
-  __syncwarp();
 
+  // Invalid routes (and lanes past R) get expert -1: they match no valid
+  // route, lead nothing and never scatter.
   const int e0 = (raw0 >= 0 && raw0 < kMoeExperts) ? (int)raw0 : -1;
   const int e1 = (raw1 >= 0 && raw1 < kMoeExperts) ? (int)raw1 : -1;
-  // Invalid routes get a key no valid expert uses; they never scatter.
-  const unsigned m0 = __match_any_sync(0xffffffffu, e0 >= 0 ? e0 : 0x7fffffff);
-  const int rank0 = __popc(m0 & lt);
-  if (e0 >= 0 && rank0 == 0) s_count[e0] = __popc(m0);
-  __syncwarp();
-  const int base1 = e1 >= 0 ? s_count[e1] : 0;  // routes of half 0 precede half 1
-  const unsigned m1 = __match_any_sync(0xffffffffu, e1 >= 0 ? e1 : 0x7fffffff);
-  const int rank1 = base1 + __popc(m1 & lt);
-  __syncwarp();
-  if (e1 >= 0 && __popc(m1 & lt) == 0) s_count[e1] = base1 + __popc(m1);
-  __syncwarp();
-
-  // Exclusive prefix of padded counts: lane owns experts [9 lane, 9 lane + 9).
-  int local[kMoePerLane];
-  int sum = 0;
+  const int j1 = lane + 32;
+  int rank0 = 0, cnt0 = 0, rank1 = 0, cnt1 = 0;
 #pragma unroll
-  for (int k = 0; k < kMoePerLane; ++k) {
-    local[k] = sum;
-    sum += (s_count[kMoePerLane * lane + k] + 7) & ~7;
+  for (int k = 0; k < R; ++k) {  // unrolled: the R shuffles are independent and pipeline
+    const int ek = __shfl_sync(0xffffffffu, (!kTwoHalves || k < 32) ? e0 : e1, k & 31);
+    const int same0 = (int)(ek == e0), same1 = (int)(ek == e1);
+    cnt0 += same0;
+    rank0 += same0 & (int)(k < lane);
+    if (kTwoHalves) {
+      cnt1 += same1;
+      rank1 += same1 & (int)(k < j1);
+    }
   }
-  int incl = sum;
+  // Padded count carried by the leader (rank 0) of each valid expert.
+  const int lead0 = (e0 >= 0 && rank0 == 0) ? (cnt0 + 7) & ~7 : 0;
+  const int lead1 = (kTwoHalves && e1 >= 0 && rank1 == 0) ? (cnt1 + 7) & ~7 : 0;
+  int off0 = 0, off1 = 0;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
+  for (int k = 0; k < R; ++k) {
+    const bool lo = !kTwoHalves || k < 32;
+    const int ek = __shfl_sync(0xffffffffu, lo ? e0 : e1, k & 31);
+    const int pk = __shfl_sync(0xffffffffu, lo ? lead0 : lead1, k & 31);
+    off0 += ek < e0 ? pk : 0;  // leaders of smaller experts (pk = 0 unless k leads)
+    if (kTwoHalves) off1 += ek < e1 ? pk : 0;
   }
-  const int excl = incl - sum;
+  int total = lead0 + lead1;
 #pragma unroll
-  for (int k = 0; k < kMoePerLane; ++k) s_offset[kMoePerLane * lane + k] = excl + local[k];
-  __syncwarp();
+  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+  __syncwarp();  // the initialisation above is complete before the scatter
   // Scatter: route j goes to off_e + rank_j.  Offsets are multiples of 8, so
   // the route whose rank is a multiple of 8 opens block (off_e + rank_j) / 8
   // of its expert: exactly ceil(count_e / 8) blocks per expert, no loop.
   if (e0 >= 0) {
-    const int pos = s_offset[e0] + rank0;
+    const int pos = off0 + rank0;
     s_sorted[pos] = lane;
     if ((rank0 & 7) == 0) s_experts[pos >> 3] = e0;
   }
-  if (e1 >= 0) {
-    const int pos = s_offset[e1] + rank1;
-    s_sorted[pos] = lane + 32;
+  if (kTwoHalves && e1 >= 0) {
+    const int pos = off1 + rank1;
+    s_sorted[pos] = j1;
     if ((rank1 & 7) == 0) s_experts[pos >> 3] = e1;
   }
   __syncwarp();
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restr
     for (int i = lane; i < 8 * R; i += 32) sorted_ids[i] = s_sorted[i];
     for (int i = lane; i < R; i += 32) expert_ids[i] = s_experts[i];
   }
-  if (lane == 31) postpad[0] = incl;
+  if (lane == 0) postpad[0] = total;
 }
 
 }  // namespace titan
@@ -127,11 +128,24 @@ extern "C" int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int R = (int)num_routes;
   const bool vec_out = (uintptr_t)sorted_ids % 16 == 0 && (uintptr_t)expert_ids % 16 == 0;
+  const dim3 grid(1), block(32 * num_warps);
+  // One instantiation per route count (R = 8 B): the route walks unroll.
+  auto launch = [&](auto ids) {
+    using IdT = std::remove_const_t<std::remove_pointer_t<decltype(ids)>>;
+    switch (R) {
+      case 8: moe_align_small_kernel<IdT, 8><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      case 16: moe_align_small_kernel<IdT, 16><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      case 24: moe_align_small_kernel<IdT, 24><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      case 32: moe_align_small_kernel<IdT, 32><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      case 40: moe_align_small_kernel<IdT, 40><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      case 48: moe_align_small_kernel<IdT, 48><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      case 56: moe_align_small_kernel<IdT, 56><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      default: moe_align_small_kernel<IdT, 64><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+    }
+  };
   if (ids_is_int64)
-    moe_align_small_kernel<long long><<<1, 32 * num_warps, 0, s>>>(static_cast<const long long *>(topk_ids), R,
-                                                                  sorted_ids, expert_ids, postpad, vec_out);
+    launch(static_cast<const long long *>(topk_ids));
   else
-    moe_align_small_kernel<int32_t><<<1, 32 * num_warps, 0, s>>>(static_cast<const int32_t *>(topk_ids), R,
-                                                                 sorted_ids, expert_ids, postpad, vec_out);
+    launch(static_cast<const int32_t *>(topk_ids));
   return check_launch("moe_align_small launch");
 }
