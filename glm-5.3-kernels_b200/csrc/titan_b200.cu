@@ -7,3 +7,4 @@
 #include "titan_mla.cu"
 #include "titan_index.cu"
 #include "titan_io.cu"
+#include "titan_moe_gemm.cu"

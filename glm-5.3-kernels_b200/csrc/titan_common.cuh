@@ -60,6 +60,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t tx
       : "memory");
 }
 
+// Plain arrival (release at CTA scope).
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

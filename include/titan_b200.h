@@ -307,6 +307,31 @@ int titan_device_pointer(const void *ptr, void **device_ptr_out);
 int titan_device_error(int *error_out, int clear_after, titan_stream_t stream);
 
 /*
+ * W4A16 MoE GEMM over one split-align block list, on the tcgen05 tensor cores.
+ * Replaces one `moe_wna16_marlin_gemm` call of the split Marlin path,
+ * profiles/sm74/titan_prefill/marlin.py:417-444 (uint4b8 weights, group 128,
+ * bf16 activations, fp32 accumulation).  For each block b < ntpp[0] /
+ * block_size with e = expert_ids[b] and routed rows s = sorted_ids[b * bs + j]
+ * (ids >= size_m * top_k are padding and are skipped):
+ *   C[s, n] = sum_k A[s / top_k, k] * bf16((q[e,n,k] - 8) * scales[e, k/128, n])
+ *   times topk_weights[s] when mul_topk_weights.
+ *   a            bf16 [size_m rows][k], rows a_stride elements apart (16-byte aligned)
+ *   c            bf16, rows c_stride elements apart; only listed rows are written
+ *   wq_packed    uint8 [E][n/128][k/64][2][128][16] (kernels/titan_moe_gemm.py
+ *                pack_weights), 16-byte aligned; titan_moe_w4a16_packed_bytes
+ *   scales       bf16 [E][k/128][n]
+ *   sorted_ids, expert_ids (max_blocks entries), ntpp: one list of
+ *                titan_moe_split_align; block_size in {16, 32, 48, 64}
+ *   n % 128 == 0, k % 128 == 0.  One persistent launch, no scratch memory.
+ */
+int64_t titan_moe_w4a16_packed_bytes(int64_t num_experts, int64_t n, int64_t k);
+int titan_moe_w4a16_gemm(const void *a, int64_t a_stride, int64_t size_m, void *c, int64_t c_stride,
+                         const void *wq_packed, const void *scales, const int32_t *sorted_ids,
+                         const int32_t *expert_ids, int64_t max_blocks, const int32_t *ntpp,
+                         const float *topk_weights, int block_size, int top_k, int mul_topk_weights,
+                         int64_t num_experts, int64_t n, int64_t k, titan_stream_t stream);
+
+/*
  * Self-test of the bounded waits (no counterpart in the reference): one warp
  * waits on an mbarrier that nothing completes, gives up after about
  * `limit_cycles` SM clocks (1 .. 4e9), sets the device error word to 1

@@ -328,3 +328,46 @@ def convert_req_index_to_global(req_id, block_table, token_indices, block_size, 
     val = base * stride_rows + (tok - blk * block_size)
     val = ((val + 2 ** 31) % 2 ** 32) - 2 ** 31          # two's-complement int32 wrap
     return np.where(ok, val, -1).astype(np.int32)
+
+
+# ------------------------------------------------------- W4A16 MoE GEMM
+def moe_w4a16_dequant(q, scales):
+    """uint4b8 codes q [E, N, K] (0..15) and bf16 group scales [E, K / 128, N]
+    -> float32 [E, N, K] = bf16((q - 8) * scale), the dequantised weight the
+    tensor cores consume (Marlin rounds it to the activation type the same way)."""
+    q = torch.as_tensor(q).to(torch.int32)
+    s = torch.as_tensor(scales).float()
+    E, N, K = q.shape
+    sk = s.permute(0, 2, 1).repeat_interleave(128, dim=2)            # [E, N, K]
+    return ((q - 8).float() * sk).to(torch.bfloat16).float()
+
+
+def moe_w4a16_gemm(a, w_deq, sorted_ids, expert_ids, ntpp, topk_weights, block_size, top_k,
+                   mul_topk_weights, size_m, c):
+    """One list GEMM of the split Marlin MoE path (the per-list
+    `moe_wna16_marlin_gemm` calls, profiles/sm74/titan_prefill/marlin.py:
+    417-444; vLLM's op, not in the reference tree): for each block b <
+    ntpp / block_size with expert e = expert_ids[b] and routed rows
+    s = sorted_ids[b * block_size + j] < size_m * top_k,
+    c[s] = a[s // top_k] @ w_deq[e]^T (times topk_weights[s] when
+    mul_topk_weights), accumulated in float64 here and stored as bf16.
+    Rows not listed keep their contents.  Modifies and returns c (torch, CPU)."""
+    a = torch.as_tensor(a).double()
+    sid = np.asarray(torch.as_tensor(sorted_ids).cpu()).astype(np.int64)
+    eid = np.asarray(torch.as_tensor(expert_ids).cpu()).astype(np.int64)
+    nblocks = int(np.asarray(torch.as_tensor(ntpp).cpu()).reshape(-1)[0]) // block_size
+    pad = size_m * top_k
+    for b in range(nblocks):
+        e = int(eid[b])
+        if e < 0 or e >= w_deq.shape[0]:
+            continue
+        rows = sid[b * block_size:(b + 1) * block_size]
+        rows = rows[(rows >= 0) & (rows < pad)]
+        if rows.size == 0:
+            continue
+        r = torch.from_numpy(rows)
+        out = a[r // top_k] @ w_deq[e].double().T
+        if mul_topk_weights:
+            out = out * torch.as_tensor(topk_weights).double().reshape(-1)[r][:, None]
+        c[r] = out.to(c.dtype)
+    return c
