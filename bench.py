@@ -655,6 +655,13 @@ def run_ours(args, dist):
             gs.reset()
     secondary["moe_split_align"] = split
 
+    # ---- W4A16 MoE GEMM (the consumer of the split align): the gate/up
+    # projection of the whole-expert prefill shape, M = 2304 tokens x top-8
+    # over 288 experts, 2N = 4096, K = 4096, uint4b8 group-128 weights
+    # (profiles/sm74/titan_prefill/marlin.py:417-424), the four list GEMMs
+    # back to back in one CUDA graph; Zipf(1.1) routes.
+    if not args.skip_moe_gemm:
+        secondary["moe_w4a16_gemm"] = moe_gemm_line(dev, peak, gm)
     # ---- the reference's own Triton kernels on this B200 (rank 0 of a
     # single-GPU run only; comparison lines, not our path)
     if rank == 0 and world == 1 and not args.skip_reference_triton:
@@ -731,6 +738,53 @@ def run_ours(args, dist):
 
 
 CPU_INDEX_SEED = 99   # the B=1 index sets both CPU legs time (the headline's rank-0 seed)
+
+
+def moe_gemm_setup(dev, M, N2, K, E=288, top_k=8, seed=5):
+    """Random uint4b8 experts (packed), bf16 group scales, Zipf(1.1) routes
+    split by split_align; returns (run, useful_flops, weight_bytes_touched)."""
+    from kernels import titan_moe_split_align as split_mod
+    from kernels.titan_moe_gemm import moe_w4a16_gemm, pack_weights
+    g = torch.Generator(device=dev).manual_seed(seed)
+    packed = torch.randint(0, 256, (E * N2 * K // 2,), generator=g, device=dev, dtype=torch.uint8)
+    scales = (torch.rand(E, K // 128, N2, generator=g, device=dev) * 0.02 + 0.002).to(torch.bfloat16)
+    gc = torch.Generator().manual_seed(seed)
+    w = torch.arange(1, E + 1, dtype=torch.float64) ** -1.1
+    routes = torch.stack([torch.multinomial(w, top_k, replacement=False, generator=gc) for _ in range(M)])
+    routes = routes.to(torch.int32).to(dev)
+    buf = split_mod.buffers(M * top_k, E, dev)
+    lists = split_mod.split_align(routes, E, buf)
+    a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+    c = torch.empty(M * top_k, N2, dtype=torch.bfloat16, device=dev)
+
+    def run():
+        for bs, s_ids, e_ids, n in lists:
+            moe_w4a16_gemm(a, c, packed, scales, s_ids, e_ids, n, None, bs, top_k, False, M, N2, K)
+    experts = int(torch.unique(routes).numel())
+    return run, 2.0 * M * top_k * N2 * K, experts * N2 * K // 2 + experts * (K // 128) * N2 * 2
+
+
+def moe_gemm_line(dev, peak_gbs, gm):
+    """us per call of the four list GEMMs (one graph replay, L2 flushed
+    before each), useful TFLOP/s and the roofline: time bound = max(useful
+    FLOPs / bf16 peak, weight + scale bytes / HBM peak)."""
+    M, N2, K = 2304, 4096, 4096
+    run, flops, wbytes = moe_gemm_setup(dev, M, N2, K)
+    flush = Flusher(dev)
+    g, _ = capture(run)
+    timed_cold(lambda k: g.replay(), 2, flush)
+    ms = statistics.median(timed_cold(lambda k: g.replay(), 5, flush))
+    g.reset()
+    tf_peak = 1648.6
+    try:
+        tf_peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+    except (OSError, ValueError, KeyError):
+        pass
+    bound_us = max(flops / (tf_peak * 1e12), wbytes / (peak_gbs * 1e9)) * 1e6
+    return {"shape": f"M={M} tokens x top-8, 288 experts, 2N={N2}, K={K}, Zipf(1.1) routes, four lists",
+            "us_per_call": ms * 1000, "useful_tflops": flops / (ms * 1e-3) / 1e12,
+            "weight_GBps": wbytes / (ms * 1e-3) / 1e9, "roofline_bound_us": bound_us,
+            "frac_of_roofline": bound_us / (ms * 1000), "bf16_peak_tflops": tf_peak}
 
 
 def load_reference_triton():
@@ -923,6 +977,12 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     n = args.warmup + args.steps
+    if args.profile == "moe_gemm":  # the four list GEMMs; small: M = 512 tokens, 2N = 1024, K = 4096
+        run, _, _ = moe_gemm_setup(dev, 512, 1024, 4096)
+        for _ in range(n):
+            run()
+        torch.cuda.synchronize()
+        return
     if args.profile == "split_align":  # M = 2304 tokens x top-8, 288 uniform experts
         from kernels import titan_moe_split_align as split_mod
         g = torch.Generator().manual_seed(1)
@@ -979,9 +1039,11 @@ def main():
                     help="time bound of both CPU legs (reference arm and cpu_baseline)")
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-moe-gemm", action="store_true")
     ap.add_argument("--skip-reference-triton", action="store_true",
                     help="skip the secondary lines of the reference's Triton kernels run on this GPU")
-    ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1", "split_align"),
+    ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1", "split_align",
+                                          "moe_gemm"),
                     default=None,
                     help="run only this workload (warmup + steps calls) as an ncu target; prints nothing")
     args = ap.parse_args()

@@ -14,20 +14,28 @@
 // sums in fp32, C in bf16.  The dequantised weight is rounded to bf16 before
 // the MMA, as Marlin's W4A16 dequantisation does.
 //
-// B200 design, one persistent CTA of 10 warps per SM, work item = (block b,
-// 128 output features); the MMA computes D[128 features x bs rows] =
-// W_e[128 x K] . A_rows[bs x K]^T with M = 128 and N = bs in {16..64}:
-//  * warp 0 (one lane): per 64-wide K step, a bulk copy of the step's 4 KB
-//    of packed int4 weights and a TMA tile::gather4 of the block's activation
-//    rows (row s / top_k; padding rows read as zeros) into a 128B-swizzled,
-//    K-major shared tile, four pipeline stages;
-//  * warps 2..5: dequantise the weights into a 128B-swizzled K-major bf16
-//    tile (one thread per feature row; nibbles pre-interleaved by
-//    titan_moe_w4a16_pack so one LOP3 yields a bf16 pair);
+// B200 design, one persistent CTA of 19 warps per SM, work item = (block b,
+// 256 output features: two MMAs of M = 128 sharing the activation tile);
+// each MMA computes D[128 features x bs rows] = W_e[128 x K] . A_rows[bs x K]^T
+// with N = bs in {16..64}:
+//  * warps 0, 14..18: per 64-wide K step (each warp every sixth step), one
+//    lane bulk-copies the pair's 8 KB of packed int4 weights and its group
+//    scales; the 32 lanes copy the
+//    block's activation rows (row s / top_k; padding rows zero-filled) with
+//    16-byte cp.async straight into a 128B-swizzled, K-major shared tile;
+//    ten stages (~165 KB in flight per SM: the weight stream is
+//    latency-bound with fewer, and one warp cannot issue the small copies
+//    fast enough);
+//  * warps 2..9: dequantise the weights straight into tensor memory (one
+//    thread per feature row, one tcgen05.st of 64 bf16 per step; nibbles
+//    pre-interleaved by pack_weights so one LOP3 yields a bf16 pair), three
+//    buffers; the MMA reads its A operand there, so the weights never pass
+//    through shared memory in bf16;
 //  * warp 1 (one lane): four tcgen05.mma kind::f16 (K = 16 each) per step
-//    into a double-buffered tensor-memory accumulator (2 x 64 columns),
+//    and tile into double-buffered tensor-memory accumulators (2 x 2 x 64
+//    columns);
 //    tcgen05.commit frees the stage / publishes the accumulator;
-//  * warps 6..9: tcgen05.ld of the accumulator (one lane quarter each),
+//  * warps 10..13: tcgen05.ld of the accumulator (one lane quarter each),
 //    topk weighting, bf16 stores of the block's rows.
 // Every wait is an mbarrier wait bounded in time; a wait that gives up sets
 // the device error word and the CTA abandons its remaining work items.
@@ -36,34 +44,40 @@
 namespace titan {
 namespace moeg {
 
-constexpr int kBM = 128;           // output features per work item (MMA M)
+constexpr int kBM = 128;           // output features per MMA (M)
+constexpr int kNT = 2;             // MMAs (128-feature tiles) per work item, sharing one activation tile
 constexpr int kBK = 64;            // K per pipeline step: one 128-byte bf16 row
-constexpr int kStages = 4;
+constexpr int kStages = 10;        // raw stages (packed weights, scales, activation rows)
+constexpr int kWBufs = 3;          // dequantised weight buffers in tensor memory
 constexpr int kMaxBS = 64;         // block rows (MMA N)
-constexpr int kWarps = 10;
+constexpr int kProducers = 6;      // producer warps: 0 and 14..18, each issuing every 6th step
+constexpr int kDeqWarps = 8;
+constexpr int kWarps = 19;         // 0 producer, 1 MMA, 2..9 dequantisation, 10..13 epilogue, 14..18 producers
 constexpr int kThreads = kWarps * 32;
-constexpr int kStepWBytes = kBM * kBK / 2;  // packed int4 weights of one step: 4 KB
-constexpr int kTmemCols = 128;     // two accumulators of up to 64 fp32 columns
+constexpr int kStepWBytes = kBM * kBK / 2;  // packed int4 weights of one 128-feature tile per step: 4 KB
+constexpr int kTmemCols = 512;
+constexpr int kColAcc = 0;         // accumulators: [2 sets][kNT tiles][64 fp32 columns]
+constexpr int kColA = 256;         // dequantised weights: [kWBufs][kNT tiles][32 columns of bf16 pairs]
 
 struct Smem {
-  alignas(1024) uint8_t wtile[kStages][kBM * kBK * 2];     // 16 KB per stage, bf16, SW128 K-major
-  alignas(1024) uint8_t atile[kStages][kMaxBS * kBK * 2];  // 8 KB per stage, bf16, SW128 K-major
-  alignas(128) uint8_t wraw[kStages][kStepWBytes];         // 4 KB per stage, packed int4
-  alignas(16) uint16_t sscale[kStages][kBM];               // the step's group scales (bf16 bits)
-  alignas(8) uint64_t full_a[kStages];                     // activation rows landed (tx bytes)
-  uint64_t full_w[kStages];                                // packed weights landed (tx bytes)
-  uint64_t deq[kStages];                                   // dequantised tile written (4 warps)
-  uint64_t empty[kStages];                                 // stage consumed by the MMAs (commit)
-  uint64_t acc_full[2];                                    // accumulator ready (commit)
-  uint64_t acc_empty[2];                                   // accumulator read out (4 warps)
-  uint64_t drain;                                          // every MMA of this CTA completed
-  int rows_p[kMaxBS];                                      // producer: gather row of each block row
+  alignas(1024) uint8_t atile[kStages][kMaxBS * kBK * 2];   // 8 KB per stage, bf16, SW128 K-major
+  alignas(128) uint8_t wraw[kStages][kNT * kStepWBytes];    // 8 KB per stage: the pair's packed int4
+  alignas(16) uint16_t sscale[kStages][kNT * kBM];          // the step's group scales (bf16 bits)
+  alignas(8) uint64_t full[kStages];                        // weights + scales (tx bytes) and rows (32 lanes)
+  uint64_t empty[kStages];                                  // stage consumed (MMA commit)
+  uint64_t deq[kWBufs];                                     // dequantised tiles written (8 warps)
+  uint64_t wfree[kWBufs];                                   // dequantised tiles consumed (MMA commit)
+  uint64_t acc_full[2];                                     // accumulators ready (MMA commit)
+  uint64_t acc_empty[2];                                    // accumulators read out (4 warps)
+  uint64_t drain;                                           // every MMA of this CTA completed
   uint32_t tmem_base;
-  int abort_flag;                                          // a bounded wait gave up
+  int abort_flag;                                           // a bounded wait gave up
 };
 
 struct Params {
-  const uint8_t *wq;                 // packed weights, [E][N/128][K/64][4096 B]
+  const uint8_t *a;                  // activations, bf16 rows a_stride elements apart
+  int64_t a_stride;
+  const uint8_t *wq;                 // packed weights: per expert, tile pairs x k steps x 4 KB tiles
   const __nv_bfloat16 *scales;       // [E][K/128][N]
   const int32_t *sorted_ids;
   const int32_t *expert_ids;
@@ -102,6 +116,30 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] . B[smem desc]^T, kind::f16; A: M = 128 lanes (rows),
+// each 32-bit column two consecutive k (bf16), K = 16 = eight columns.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 consecutive 32-bit columns of this thread's lane (this warp's lane quarter).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // The mbarrier completes once every tcgen05.mma issued before by this thread has.
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -170,17 +208,40 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
+// 16-byte asynchronous global -> shared copy reading `src_bytes` (16 or 0:
+// zeros, nothing read).
+__device__ __forceinline__ void cp_async_16_zfill(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+// Arrive on the mbarrier once this thread's earlier cp.async copies have landed
+// (the barrier's expected count includes this arrival).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Wait with the CTA-wide abort flag: once one role has given up, the others
-// stop waiting at their next wait.
+// stop waiting at their next wait.  Bounded like mbar_wait_bounded, but the
+// clock is read once per 32 polls, so waiting warps take fewer issue slots
+// from the dequantisation warps.
 __device__ __forceinline__ bool wait_or_abort(Smem &sm, uint64_t *bar, uint32_t parity) {
-  if (*reinterpret_cast<volatile int *>(&sm.abort_flag)) return false;
-  if (mbar_wait_bounded(bar, parity, kLongWaitCycles)) return true;
-  *reinterpret_cast<volatile int *>(&sm.abort_flag) = 1;
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (*reinterpret_cast<volatile int *>(&sm.abort_flag)) return false;
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (clock64() - t0 > kLongWaitCycles) {
+      atomicCAS(&g_device_error, 0, kDevErrMbarrierTimeout);
+      *reinterpret_cast<volatile int *>(&sm.abort_flag) = 1;
+      return false;
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    moe_w4a16_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap a_map) {
+    moe_w4a16_gemm_kernel(const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The dynamic window is 16-byte aligned by contract; align the tiles to 1024.
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -188,10 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full_a[s], 1);
-      mbar_init(&sm.full_w[s], 1);
-      mbar_init(&sm.deq[s], 4);
+      mbar_init(&sm.full[s], 33);  // producer lane 0 (with the bulk bytes) + 32 row-copy lanes
       mbar_init(&sm.empty[s], 1);
+    }
+    for (int w = 0; w < kWBufs; ++w) {
+      mbar_init(&sm.deq[w], kDeqWarps);
+      mbar_init(&sm.wfree[w], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.acc_full[b], 1);
@@ -205,7 +268,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&sm.tmem_base, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) prefetch_tensormap(&a_map);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -216,76 +278,106 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t nb_raw = (int64_t)__ldg(p.ntpp) / bs;
   const int64_t nblocks = nb_raw < 0 ? 0 : (nb_raw > p.max_blocks ? p.max_blocks : nb_raw);
   const int ntn = p.N / kBM, nk = p.K / kBK;
-  const int64_t items = nblocks * ntn;
+  const int npairs = (ntn + kNT - 1) / kNT;  // work items per block: pairs of 128-feature tiles
+  const int64_t items = nblocks * npairs;
   const int64_t pad_id = (int64_t)p.size_m * p.top_k;
+  // Item = (block b, feature tiles kNT np .. kNT np + nts - 1).
+  auto tiles_of = [&](int np) { return min(kNT, ntn - kNT * np); };
 
-  if (warp == 0) {
-    // ---------------------------------------------------------- producer
-    uint32_t g = 0;  // global step counter of this CTA
-    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
-      const int64_t b = item / ntn;
-      const int nt = (int)(item - b * ntn);
+  if (warp == 0 || warp >= 2 + kDeqWarps + 4) {
+    // --------------------------------------------------------- producers
+    // Producer pi issues the steps g with g % kProducers == pi: the copies of
+    // one step are small (4 KB of weights per tile, 128-byte activation
+    // rows) and their issue cost, not their bytes, bounds a single issuing
+    // warp, so four warps issue in parallel.
+    const int pi = warp == 0 ? 0 : warp - (2 + kDeqWarps + 4) + 1;
+    uint32_t g = 0;  // step counter of this CTA
+    bool ok = true;
+    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const int64_t b = item / npairs;
+      const int np = (int)(item - b * npairs), nts = tiles_of(np);
       const int e = __ldg(p.expert_ids + b);
       if (e < 0 || e >= p.num_experts) continue;
-      int *rows = sm.rows_p;  // the gathers take rows as operands: reusable once issued
-      for (int j = lane; j < bs; j += 32) {
-        const int64_t sid = __ldg(p.sorted_ids + b * bs + j);
-        rows[j] = (sid >= 0 && sid < pad_id) ? (int)(sid / p.top_k) : -1;
+      // Activation row of block rows lane and lane + 32 (-1: padding).
+      int row_lo = -1, row_hi = -1;
+      {
+        const int64_t s0 = lane < bs ? __ldg(p.sorted_ids + b * bs + lane) : -1;
+        const int64_t s1 = lane + 32 < bs ? __ldg(p.sorted_ids + b * bs + lane + 32) : -1;
+        row_lo = (s0 >= 0 && s0 < pad_id) ? (int)(s0 / p.top_k) : -1;
+        row_hi = (s1 >= 0 && s1 < pad_id) ? (int)(s1 / p.top_k) : -1;
       }
-      __syncwarp();
-      const uint8_t *wsrc = p.wq + ((int64_t)e * ntn + nt) * nk * (int64_t)kStepWBytes;
-      const __nv_bfloat16 *ssrc = p.scales + (int64_t)e * (p.K / 128) * p.N + nt * kBM;
+      // Packed weights of the pair: per step, its nts tiles' 4 KB back to back.
+      const uint8_t *wsrc = p.wq + ((int64_t)e * ntn * nk + (int64_t)kNT * np * nk) * kStepWBytes;
+      const __nv_bfloat16 *ssrc = p.scales + (int64_t)e * (p.K / 128) * p.N + kNT * np * kBM;
       for (int kc = 0; kc < nk; ++kc, ++g) {
+        if ((int)(g % kProducers) != pi) continue;
         const int s = (int)(g % kStages);
         const uint32_t use = g / kStages;
-        bool ok = true;
         if (use > 0) ok = wait_or_abort(sm, &sm.empty[s], (use - 1) & 1u);
         if (!ok) break;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sm.full_w[s], (uint32_t)(kStepWBytes + kBM * 2));
-          bulk_g2s(sm.wraw[s], wsrc + (int64_t)kc * kStepWBytes, (uint32_t)kStepWBytes, &sm.full_w[s]);
-          bulk_g2s(sm.sscale[s], ssrc + (int64_t)(kc >> 1) * p.N, (uint32_t)(kBM * 2), &sm.full_w[s]);
-          mbar_arrive_expect_tx(&sm.full_a[s], (uint32_t)(bs * kBK * 2));
-          for (int j = 0; j < bs; j += 4)
-            tma_gather4(sm.atile[s] + j * (kBK * 2), &a_map, kc * kBK, rows[j], rows[j + 1], rows[j + 2], rows[j + 3],
-                        &sm.full_a[s]);
+          mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nts * (kStepWBytes + kBM * 2)));
+          bulk_g2s(sm.wraw[s], wsrc + (int64_t)kc * nts * kStepWBytes, (uint32_t)(nts * kStepWBytes), &sm.full[s]);
+          bulk_g2s(sm.sscale[s], ssrc + (int64_t)(kc >> 1) * p.N, (uint32_t)(nts * kBM * 2), &sm.full[s]);
         }
-        __syncwarp();
+        // Activation rows: lane l copies 16-byte chunk l & 7 of rows
+        // (l >> 3) + 4 i into their swizzled slots; padding rows are
+        // zero-filled without reading memory.  Each lane arrives once its
+        // copies have landed.
+        {
+          const int ch = lane & 7;
+          uint8_t *dst = sm.atile[s];
+          const int64_t kbyte = (int64_t)kc * (kBK * 2) + ch * 16;
+#pragma unroll 4
+          for (int j = lane >> 3; j < kMaxBS; j += 4) {
+            const int row = __shfl_sync(0xffffffffu, j < 32 ? row_lo : row_hi, j & 31);
+            if (j < bs) {
+              const uint8_t *src = row >= 0 ? p.a + (int64_t)row * p.a_stride * 2 + kbyte : p.a;
+              cp_async_16_zfill(dst + sw128_offset(j, ch), src, row >= 0 ? 16u : 0u);
+            }
+          }
+          cp_async_mbar_arrive_noinc(&sm.full[s]);
+        }
       }
-      if (*reinterpret_cast<volatile int *>(&sm.abort_flag)) break;
     }
+    cp_async_wait<0>();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA
     const uint32_t idesc = idesc_bf16(kBM, bs);
     uint32_t g = 0;
     int it = 0;
-    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
-      const int64_t b = item / ntn;
+    bool ok = true;
+    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const int64_t b = item / npairs;
+      const int np = (int)(item - b * npairs), nts = tiles_of(np);
       const int e = __ldg(p.expert_ids + b);
       if (e < 0 || e >= p.num_experts) continue;
-      const int buf = it & 1;
+      const int ab = it & 1;
       const uint32_t use_acc = (uint32_t)(it >> 1);
-      bool ok = true;
-      if (use_acc > 0) ok = wait_or_abort(sm, &sm.acc_empty[buf], (use_acc - 1) & 1u);
+      if (use_acc > 0) ok = wait_or_abort(sm, &sm.acc_empty[ab], (use_acc - 1) & 1u);
       tc_fence_after();
-      const uint32_t d = tmem + (uint32_t)(buf * 64);
       for (int kc = 0; kc < nk && ok; ++kc, ++g) {
-        const int s = (int)(g % kStages);
-        const uint32_t use = g / kStages;
-        ok = wait_or_abort(sm, &sm.full_a[s], use & 1u) && wait_or_abort(sm, &sm.deq[s], use & 1u);
+        const int s = (int)(g % kStages), wb = (int)(g % kWBufs);
+        const uint32_t use = g / kStages, wuse = g / kWBufs;
+        ok = wait_or_abort(sm, &sm.full[s], use & 1u) && wait_or_abort(sm, &sm.deq[wb], wuse & 1u);
         if (!ok) break;
+        fence_proxy_async_smem();  // rows written by cp.async: visible to the tensor core
         tc_fence_after();
         if (lane == 0) {
+          for (int t = 0; t < nts; ++t) {
+            const uint32_t d = tmem + (uint32_t)(kColAcc + ab * (kNT * 64) + t * 64);
+            const uint32_t aw = tmem + (uint32_t)(kColA + wb * (kNT * 32) + t * 32);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            umma_bf16(d, sw128_desc(sm.wtile[s], 32 * k), sw128_desc(sm.atile[s], 32 * k), idesc,
-                      (kc > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kBK / 16; ++k)
+              umma_bf16_ts(d, aw + 8 * k, sw128_desc(sm.atile[s], 32 * k), idesc, (kc > 0 || k > 0) ? 1u : 0u);
+          }
           umma_commit(&sm.empty[s]);
+          umma_commit(&sm.wfree[wb]);
         }
         __syncwarp();
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&sm.acc_full[buf]);
+      if (lane == 0) umma_commit(&sm.acc_full[ab]);
       __syncwarp();
       ++it;
     }
@@ -294,81 +386,99 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) umma_commit(&sm.drain);
     __syncwarp();
     mbar_wait_bounded(&sm.drain, 0u, kLongWaitCycles);
-  } else if (warp < 6) {
+  } else if (warp < 2 + kDeqWarps) {
     // ---------------------------------------------------- dequantisation
-    const int r = tid - 64;  // feature row of the tile, 0..127
+    // Warp w writes tensor-memory lanes 32 (w % 4) .. + 31: thread = feature
+    // row r of tile t, its 64 dequantised k of the step as 32 columns of bf16
+    // pairs (one tcgen05.st).
+    const int r = 32 * (warp & 3) + lane;
+    const int t = (warp - 2) >> 2;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     uint32_t g = 0;
-    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
-      const int64_t b = item / ntn;
+    bool ok = true;
+    for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const int64_t b = item / npairs;
+      const int np = (int)(item - b * npairs), nts = tiles_of(np);
       const int e = __ldg(p.expert_ids + b);
       if (e < 0 || e >= p.num_experts) continue;
-      bool ok = true;
       for (int kc = 0; kc < nk; ++kc, ++g) {
-        const int s = (int)(g % kStages);
-        const uint32_t use = g / kStages;
-        ok = wait_or_abort(sm, &sm.full_w[s], use & 1u);
+        const int s = (int)(g % kStages), wb = (int)(g % kWBufs);
+        const uint32_t use = g / kStages, wuse = g / kWBufs;
+        ok = wait_or_abort(sm, &sm.full[s], use & 1u);
+        if (ok && wuse > 0) ok = wait_or_abort(sm, &sm.wfree[wb], (wuse - 1) & 1u);
         if (!ok) break;
-        const uint32_t sc = sm.sscale[s][r];  // scale of group kc / 2, feature r
-        // Packed layout of a step: [half h][row r][16 bytes] (64 nibbles of row r).
-        const uint4 w0 = *reinterpret_cast<const uint4 *>(&sm.wraw[s][r * 16]);
-        const uint4 w1 = *reinterpret_cast<const uint4 *>(&sm.wraw[s][2048 + r * 16]);
-        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const uint32_t sc2 = sc | (sc << 16);
-        uint8_t *dst = sm.wtile[s];
+        if (t < nts) {
+          // Packed layout of a tile step: [half h][row r][16 bytes], half h =
+          // the row's 16-byte bf16 chunks 4h .. 4h + 3.
+          const uint8_t *raw = sm.wraw[s] + t * kStepWBytes;
+          const uint4 w0 = *reinterpret_cast<const uint4 *>(raw + r * 16);
+          const uint4 w1 = *reinterpret_cast<const uint4 *>(raw + 2048 + r * 16);
+          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          const uint32_t sc = sm.sscale[s][t * kBM + r];
+          const uint32_t sc2 = sc | (sc << 16);
+          uint32_t v[32];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {  // chunk c = k 8c .. 8c + 7
-          uint32_t v[4];
-          nibbles_to_bf16x8(words[c], v);
-          *reinterpret_cast<uint4 *>(dst + sw128_offset(r, c)) =
-              make_uint4(bf16x2_mul(v[0], sc2), bf16x2_mul(v[1], sc2), bf16x2_mul(v[2], sc2), bf16x2_mul(v[3], sc2));
+          for (int c = 0; c < 8; ++c) {  // chunk c = k 8c .. 8c + 7 = columns 4c .. 4c + 3
+            uint32_t x[4];
+            nibbles_to_bf16x8(words[c], x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[4 * c + i] = bf16x2_mul(x[i], sc2);
+          }
+          tmem_st32(tmem + lane_base + (uint32_t)(kColA + wb * (kNT * 32) + t * 32), v);
+          tmem_st_wait();
         }
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.deq[s]);
+        if (lane == 0) mbar_arrive(&sm.deq[wb]);
       }
-      if (!ok) break;
     }
   } else {
     // -------------------------------------------------------- epilogue
     const int q = warp & 3;             // lane quarter this warp may read
-    const int f = q * 32 + lane;        // feature row of the tile
+    const int f = q * 32 + lane;        // feature row within a tile
     int it = 0;
     for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
-      const int64_t b = item / ntn;
-      const int nt = (int)(item - b * ntn);
+      const int64_t b = item / npairs;
+      const int np = (int)(item - b * npairs), nts = tiles_of(np);
       const int e = __ldg(p.expert_ids + b);
       if (e < 0 || e >= p.num_experts) continue;
-      const int buf = it & 1;
+      const int ab = it & 1;
       // The block's sorted ids, held by every epilogue warp itself (lane l:
       // rows l and l + 32), so no barrier ties the four warps together.
       const int id_lo = lane < bs ? __ldg(p.sorted_ids + b * bs + lane) : -1;
       const int id_hi = lane + 32 < bs ? __ldg(p.sorted_ids + b * bs + lane + 32) : -1;
-      if (!wait_or_abort(sm, &sm.acc_full[buf], (uint32_t)(it >> 1) & 1u)) break;
+      if (!wait_or_abort(sm, &sm.acc_full[ab], (uint32_t)(it >> 1) & 1u)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 64);
-      float v[kMaxBS];
+      // One tile at a time (64 registers of accumulator); the accumulator
+      // set is released after the last tile's load.
+#pragma unroll 1
+      for (int t = 0; t < nts; ++t) {
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(kColAcc + ab * (kNT * 64) + t * 64);
+        float v[kMaxBS];
 #pragma unroll
-      for (int j0 = 0; j0 < kMaxBS; j0 += 16) {
-        if (j0 < bs) {
-          float t[16];
-          tmem_ld16(taddr + (uint32_t)j0, t);
+        for (int j0 = 0; j0 < kMaxBS; j0 += 16) {
+          if (j0 < bs) {
+            float x[16];
+            tmem_ld16(taddr + (uint32_t)j0, x);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[j0 + i] = t[i];
+            for (int i = 0; i < 16; ++i) v[j0 + i] = x[i];
+          }
         }
-      }
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
-      const int n = nt * kBM + f;
+        tmem_ld_wait();
+        if (t == nts - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.acc_empty[ab]);
+        }
+        __nv_bfloat16 *col = p.c + (int64_t)(kNT * np + t) * kBM + f;
 #pragma unroll
-      for (int j = 0; j < kMaxBS; ++j) {
-        if (j < bs) {
-          const int64_t sid = __shfl_sync(0xffffffffu, j < 32 ? id_lo : id_hi, j & 31);
-          if (sid >= 0 && sid < pad_id) {
-            float x = v[j];
-            if (p.mul_topk) x *= __ldg(p.topk_weights + sid);
-            p.c[sid * p.c_stride + n] = __float2bfloat16_rn(x);
+        for (int j = 0; j < kMaxBS; ++j) {
+          if (j < bs) {
+            const int64_t sid = __shfl_sync(0xffffffffu, j < 32 ? id_lo : id_hi, j & 31);
+            if (sid >= 0 && sid < pad_id) {
+              const float wgt = p.mul_topk ? __ldg(p.topk_weights + sid) : 1.0f;
+              col[sid * p.c_stride] = __float2bfloat16_rn(v[j] * wgt);
+            }
           }
         }
       }
@@ -386,21 +496,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace moeg
 
 namespace {
-typedef CUresult (*EncodeTiledFnG)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiledFnG encoder_fn() {
-  static const EncodeTiledFnG fn = [] {
-    void *f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      return reinterpret_cast<EncodeTiledFnG>(f);
-    cudaGetLastError();
-    return static_cast<EncodeTiledFnG>(nullptr);
-  }();
-  return fn;
-}
 std::atomic<int> g_moeg_ready[64];
 std::atomic<int> g_moeg_sms[64];
 }  // namespace
@@ -449,22 +544,9 @@ extern "C" int titan_moe_w4a16_gemm(const void *a, int64_t a_stride, int64_t siz
       g_moeg_ready[dev].store(1, std::memory_order_release);
     }
   }
-  EncodeTiledFnG encode = encoder_fn();
-  if (encode == nullptr) return fail(TITAN_ERR_CUDA, "moe_w4a16_gemm: cuTensorMapEncodeTiled is unavailable");
-  // A as a 2-D bf16 tensor [size_m rows][k], rows a_stride elements apart;
-  // boxes of 64 elements (128 bytes) by one row, 128-byte swizzle: a
-  // tile::gather4 of four rows lands as four rows of the swizzled K-major tile.
-  CUtensorMap amap;
-  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)size_m};
-  const cuuint64_t strides[1] = {(cuuint64_t)(a_stride * 2)};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, 1};
-  const cuuint32_t elem[2] = {1, 1};
-  CUresult r = encode(&amap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(a), dims, strides, box, elem,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(TITAN_ERR_CUDA, "moe_w4a16_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
-
   Params prm;
+  prm.a = static_cast<const uint8_t *>(a);
+  prm.a_stride = a_stride;
   prm.wq = static_cast<const uint8_t *>(wq_packed);
   prm.scales = static_cast<const __nv_bfloat16 *>(scales);
   prm.sorted_ids = sorted_ids;
@@ -492,7 +574,7 @@ extern "C" int titan_moe_w4a16_gemm(const void *a, int64_t a_stride, int64_t siz
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, moe_w4a16_gemm_kernel, prm, amap);
+  e = cudaLaunchKernelEx(&cfg, moe_w4a16_gemm_kernel, prm);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "moe_w4a16_gemm launch: %s", cudaGetErrorString(e));
   return TITAN_OK;
 }

@@ -36,18 +36,29 @@ _NIBBLE_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
 
 def pack_weights(q: torch.Tensor) -> torch.Tensor:
     """uint4b8 codes q (uint8 [E, N, K], values 0..15) -> the kernel's packed
-    layout, uint8 [E * N * K / 2]: [E][N / 128][K / 64][half][128 rows][16 B].
-    A 32-bit word holds the eight k of one 16-byte chunk of a bf16 row, its
-    nibble positions 0..7 holding k offsets 0, 2, 4, 6, 1, 3, 5, 7, so that
-    positions (i, i + 4) are the consecutive pair (2i, 2i + 1)."""
+    layout, uint8 [E * N * K / 2].  Per expert, the 128-feature tiles go in
+    pairs (a last odd tile alone); per pair and 64-wide k step, the pair's
+    tiles back to back, 4 KB each as [half][128 rows][16 B] (half h: the
+    row's k 32h .. 32h + 31).  A 32-bit word holds the eight k of one 16-byte
+    chunk of a bf16 row, its nibble positions 0..7 holding k offsets
+    0, 2, 4, 6, 1, 3, 5, 7, so that positions (i, i + 4) are the consecutive
+    pair (2i, 2i + 1)."""
     if q.dtype != torch.uint8 or q.dim() != 3:
         raise ValueError("pack_weights: q must be uint8 [E, N, K]")
     E, N, K = q.shape
     if N % TILE_N or K % GROUP:
         raise ValueError("pack_weights: N must be a multiple of 128 and K of 128")
-    x = q.reshape(E, N // TILE_N, TILE_N, K // STEP_K, 2, 4, 8)[..., list(_NIBBLE_ORDER)]
-    b = (x[..., 0::2] & 15) | ((x[..., 1::2] & 15) << 4)        # [E, nt, r, kc, h, c, 4]
-    return b.permute(0, 1, 3, 4, 2, 5, 6).contiguous().view(-1)
+    ntn, nk = N // TILE_N, K // STEP_K
+    x = q.reshape(E, ntn, TILE_N, nk, 2, 4, 8)[..., list(_NIBBLE_ORDER)]
+    b = (x[..., 0::2] & 15) | ((x[..., 1::2] & 15) << 4)        # [E, tile, r, kc, h, c, 4]
+    blocks = b.permute(0, 1, 3, 4, 2, 5, 6).reshape(E, ntn, nk, 4096)
+    parts = []
+    if ntn >= 2:
+        full = blocks[:, :ntn // 2 * 2].reshape(E, ntn // 2, 2, nk, 4096).permute(0, 1, 3, 2, 4)
+        parts.append(full.reshape(E, -1))
+    if ntn % 2:
+        parts.append(blocks[:, ntn - 1].reshape(E, -1))
+    return torch.cat(parts, dim=1).contiguous().view(-1)
 
 
 def moe_w4a16_gemm(a: torch.Tensor, c: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,

@@ -317,8 +317,10 @@ int titan_device_error(int *error_out, int clear_after, titan_stream_t stream);
  *   times topk_weights[s] when mul_topk_weights.
  *   a            bf16 [size_m rows][k], rows a_stride elements apart (16-byte aligned)
  *   c            bf16, rows c_stride elements apart; only listed rows are written
- *   wq_packed    uint8 [E][n/128][k/64][2][128][16] (kernels/titan_moe_gemm.py
- *                pack_weights), 16-byte aligned; titan_moe_w4a16_packed_bytes
+ *   wq_packed    uint8, E x n x k / 2 bytes: per expert, 128-feature tiles in
+ *                pairs, per pair and 64-wide k step the pair's 4 KB tiles back
+ *                to back (kernels/titan_moe_gemm.py pack_weights); 16-byte
+ *                aligned; titan_moe_w4a16_packed_bytes
  *   scales       bf16 [E][k/128][n]
  *   sorted_ids, expert_ids (max_blocks entries), ntpp: one list of
  *                titan_moe_split_align; block_size in {16, 32, 48, 64}

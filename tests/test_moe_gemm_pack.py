@@ -10,26 +10,34 @@ from kernels.titan_moe_gemm import pack_weights
 
 
 def _unpack_like_kernel(packed, E, N, K):
-    b = packed.numpy().reshape(E, N // 128, K // 64, 2, 128, 16)
+    """Read the packed bytes at the kernel's offsets: tile t of pair np at
+    step kc is at ((e ntn + 2 np) nk + kc nts + t) x 4 KB."""
+    ntn, nk = N // 128, K // 64
+    flat = packed.numpy()
     out = np.zeros((E, N, K), np.uint8)
     for e in range(E):
-        for nt in range(N // 128):
-            for kc in range(K // 64):
-                for h in range(2):
-                    words = b[e, nt, kc, h].copy().view(np.uint32)            # [128, 4]
-                    for c4 in range(4):
-                        w = words[:, c4].astype(np.uint64)
-                        c = 4 * h + c4                                        # 16-byte chunk of the bf16 row
-                        for i in range(4):
-                            lo = (w >> (4 * i)) & 15                          # position i      -> k 2i
-                            hi = (w >> (16 + 4 * i)) & 15                     # position i + 4  -> k 2i + 1
-                            k0 = kc * 64 + 8 * c + 2 * i
-                            out[e, nt * 128:(nt + 1) * 128, k0] = lo
-                            out[e, nt * 128:(nt + 1) * 128, k0 + 1] = hi
+        for np_ in range((ntn + 1) // 2):
+            nts = min(2, ntn - 2 * np_)
+            for kc in range(nk):
+                for t in range(nts):
+                    off = ((e * ntn + 2 * np_) * nk + kc * nts + t) * 4096
+                    blk = flat[off:off + 4096].reshape(2, 128, 16)
+                    tile = 2 * np_ + t
+                    for h in range(2):
+                        words = blk[h].copy().view(np.uint32)                  # [128, 4]
+                        for c4 in range(4):
+                            w = words[:, c4].astype(np.uint64)
+                            c = 4 * h + c4                                     # 16-byte chunk of the bf16 row
+                            for i in range(4):
+                                lo = (w >> (4 * i)) & 15                       # position i      -> k 2i
+                                hi = (w >> (16 + 4 * i)) & 15                  # position i + 4  -> k 2i + 1
+                                k0 = kc * 64 + 8 * c + 2 * i
+                                out[e, tile * 128:(tile + 1) * 128, k0] = lo
+                                out[e, tile * 128:(tile + 1) * 128, k0 + 1] = hi
     return out
 
 
-@pytest.mark.parametrize("E,N,K", [(1, 128, 128), (3, 256, 384)])
+@pytest.mark.parametrize("E,N,K", [(1, 128, 128), (3, 256, 384), (2, 384, 128)])
 def test_pack_roundtrip(E, N, K):
     g = torch.Generator().manual_seed(E * N + K)
     q = torch.randint(0, 16, (E, N, K), generator=g, dtype=torch.uint8)
