@@ -655,6 +655,12 @@ def run_ours(args, dist):
             gs.reset()
     secondary["moe_split_align"] = split
 
+    # ---- indexer pool top-k + expansion (the producer of the reader's
+    # indices): decode, 8 query rows, and a 2048-row prefill chunk, each
+    # over 65,536 pools of 4 (a 262,144-token context), k = 512, 2176-wide
+    # rows; torch.topk with a torch expansion on the same GPU beside it.
+    secondary["pool_topk_expand"] = pool_topk_line(dev, peak, flush)
+
     # ---- W4A16 MoE GEMM (the consumer of the split align): the gate/up
     # projection of the whole-expert prefill shape, M = 2304 tokens x top-8
     # over 288 experts, 2N = 4096, K = 4096, uint4b8 group-128 weights
@@ -738,6 +744,45 @@ def run_ours(args, dist):
 
 
 CPU_INDEX_SEED = 99   # the B=1 index sets both CPU legs time (the headline's rank-0 seed)
+
+
+def pool_topk_line(dev, peak_gbs, flush):
+    from kernels.titan_indexer import pool_topk_expand
+    P, k, pool, width = 65536, 512, 4, 2176
+    out = {}
+    for T in (8, 2048):
+        g = torch.Generator(device=dev).manual_seed(T)
+        logits = torch.randn(T, P, generator=g, device=dev)
+        seq = torch.randint(P * pool - 3, P * pool + 1, (T,), generator=g, device=dev, dtype=torch.int32)
+        res = torch.empty(T, width, dtype=torch.int32, device=dev)
+        gr, _ = capture(lambda: pool_topk_expand(logits, seq, k, pool, width, out=res))
+        timed_cold(lambda i: gr.replay(), 2, flush)
+        ms = statistics.median(timed_cold(lambda i: gr.replay(), 5, flush))
+        gr.reset()
+        # torch.topk over the pools each row may use, then the expansion
+        npool = (seq // pool).clamp(max=P)
+        ar = torch.arange(P, device=dev)
+        offs = torch.arange(pool, device=dev)
+
+        def torch_path():
+            masked = torch.where(ar[None, :] < npool[:, None], logits, torch.full_like(logits, -float("inf")))
+            idx = torch.topk(masked, k, dim=1).indices
+            tok = (idx[:, :, None] * pool + offs).reshape(T, -1)
+            tail = (npool * pool)[:, None] + offs[None, :pool - 1]
+            tail = torch.where(offs[None, :pool - 1] < (seq % pool)[:, None], tail, -1)
+            pad = torch.full((T, width - k * pool - pool + 1), -1, device=dev, dtype=torch.int64)
+            return torch.cat([tok, tail, pad], 1).to(torch.int32)
+        gt, _ = capture(torch_path)
+        timed_cold(lambda i: gt.replay(), 2, flush)
+        ms_t = statistics.median(timed_cold(lambda i: gt.replay(), 5, flush))
+        gt.reset()
+        nbytes = T * P * 4 + T * width * 4
+        out[f"T{T}"] = {"us": ms * 1000, "GBps": nbytes / (ms * 1e-3) / 1e9,
+                        "frac_of_hbm": nbytes / (ms * 1e-3) / 1e9 / peak_gbs,
+                        "torch_topk_expand_us": ms_t * 1000,
+                        "equal_to_torch_path": bool(torch.equal(res, torch_path()))}
+    out["shape"] = f"T rows x {P} pools of {pool}, k={k}, width={width}, seq_len in [{P * pool - 3}, {P * pool}]"
+    return out
 
 
 def moe_gemm_setup(dev, M, N2, K, E=288, top_k=8, seed=5):
@@ -909,6 +954,10 @@ def time_cpu_port(rows, steps, seconds, sets=64):
     Returns (us per call, calls timed, seconds timed, threads)."""
     from oracle import oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
+    # Both legs time against a fresh copy made by torch's parallel clone, so
+    # the 138 MB of rows are first touched (and placed in memory) the same
+    # way whichever single-threaded path produced them.
+    rows = torch.as_tensor(rows).contiguous().clone()
     q_sets, idx_sets = decode_sets(1, sets, CPU_INDEX_SEED)
     for k in range(sets):
         O.mla_sparse_attention(q_sets[k], rows, idx_sets[k], SM_SCALE)

@@ -8,3 +8,4 @@
 #include "titan_index.cu"
 #include "titan_io.cu"
 #include "titan_moe_gemm.cu"
+#include "titan_indexer.cu"

@@ -334,6 +334,24 @@ int titan_moe_w4a16_gemm(const void *a, int64_t a_stride, int64_t size_m, void *
                          int64_t num_experts, int64_t n, int64_t k, titan_stream_t stream);
 
 /*
+ * Pool top-k of the sparse indexer and its expansion into the MLA reader's
+ * token indices.  Replaces the CUDA top-k over pool logits and
+ * `kpool_ops.expand_pools_and_append_tail` of the reference's indexer
+ * (integration/patch_decode_indexer.py:49-104, integration/
+ * patch_indexer_sharding.py:58-104; expansion as tests/
+ * verify_indexer_sharding.py:68-76 `expand_row`).  For each of num_rows
+ * query rows: valid pools p < min(seq_lens[t] / pool_size, ld); the k pools of
+ * largest logits[t * ld + p] by logit descending (equal: smaller pool first;
+ * NaN above every number), -1 where fewer are valid; out[t][pool i + o] =
+ * pool_i * pool_size + o (-1 for -1), then pool_size - 1 tail entries
+ * (seq_len / pool) * pool + o for o < seq_len % pool (else -1), then -1 up
+ * to `width` (>= k * pool_size + pool_size - 1; 2176 for k = 512, pool 4).
+ * k <= 1024, pool_size <= 64.  One CTA per row.
+ */
+int titan_pool_topk_expand(const float *logits, int64_t ld, const int32_t *seq_lens, int64_t num_rows, int k,
+                           int pool_size, int32_t *out, int64_t out_stride, int width, titan_stream_t stream);
+
+/*
  * Self-test of the bounded waits (no counterpart in the reference): one warp
  * waits on an mbarrier that nothing completes, gives up after about
  * `limit_cycles` SM clocks (1 .. 4e9), sets the device error word to 1

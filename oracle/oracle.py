@@ -371,3 +371,37 @@ def moe_w4a16_gemm(a, w_deq, sorted_ids, expert_ids, ntpp, topk_weights, block_s
             out = out * torch.as_tensor(topk_weights).double().reshape(-1)[r][:, None]
         c[r] = out.to(c.dtype)
     return c
+
+
+# ------------------------------------------------- indexer pool top-k
+def expand_row(pools, seq_len, pool_size, include_tail=True):
+    """Restatement of tests/verify_indexer_sharding.py:68-76: pool p ->
+    tokens p * pool_size + o (a -1 pool -> -1s), then the tail of the partial
+    last pool (pool_size - 1 entries, -1 past seq_len % pool_size)."""
+    hist = [p * pool_size + o if p >= 0 else -1 for p in pools for o in range(pool_size)]
+    if include_tail:
+        start = seq_len // pool_size * pool_size
+        hist += [start + o if o < seq_len % pool_size else -1 for o in range(pool_size - 1)]
+    return hist
+
+
+def pool_topk_expand(logits, seq_lens, topk, pool_size, width):
+    """Top-`topk` complete pools (p < seq_len // pool_size) by logit, in the
+    order of the radix keys a CUDA top-k sorts float32 by (the IEEE bit
+    pattern made order-preserving: -0.0 below +0.0, every NaN above +inf),
+    descending, equal keys in pool order; then expand_row, then -1 up to
+    `width`.  int32 [T, width] (numpy)."""
+    lg = np.ascontiguousarray(np.asarray(torch.as_tensor(logits).float().cpu()))
+    sl = np.asarray(torch.as_tensor(seq_lens).cpu()).astype(np.int64)
+    T, P = lg.shape
+    bits = lg.view(np.uint32).astype(np.uint64)
+    keys = np.where(bits & 0x80000000, (~bits) & 0xFFFFFFFF, bits | 0x80000000)
+    keys = np.where((bits & 0x7FFFFFFF) > 0x7F800000, 0xFFFFFFFF, keys)
+    out = np.full((T, width), -1, np.int32)
+    for t in range(T):
+        n = min(max(int(sl[t]), 0) // pool_size, P)
+        order = np.lexsort((np.arange(n), -keys[t, :n].astype(np.int64)))   # key desc, then pool asc
+        pools = [int(p) for p in order[:topk]] + [-1] * max(0, topk - n)
+        row = expand_row(pools, max(int(sl[t]), 0), pool_size)
+        out[t, :len(row)] = row
+    return out
