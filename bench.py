@@ -1026,6 +1026,14 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     n = args.warmup + args.steps
+    if args.profile == "pool_topk":  # decode shape: 8 rows x 65,536 pools
+        from kernels.titan_indexer import pool_topk_expand
+        logits = torch.randn(8, 65536, device=dev)
+        seq = torch.full((8,), 262144, dtype=torch.int32, device=dev)
+        for _ in range(n):
+            pool_topk_expand(logits, seq)
+        torch.cuda.synchronize()
+        return
     if args.profile == "moe_gemm":  # the four list GEMMs; small: M = 512 tokens, 2N = 1024, K = 4096
         run, _, _ = moe_gemm_setup(dev, 512, 1024, 4096)
         for _ in range(n):
@@ -1092,7 +1100,7 @@ def main():
     ap.add_argument("--skip-reference-triton", action="store_true",
                     help="skip the secondary lines of the reference's Triton kernels run on this GPU")
     ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1", "split_align",
-                                          "moe_gemm"),
+                                          "moe_gemm", "pool_topk"),
                     default=None,
                     help="run only this workload (warmup + steps calls) as an ncu target; prints nothing")
     args = ap.parse_args()
