@@ -785,13 +785,16 @@ def pool_topk_line(dev, peak_gbs, flush):
     return out
 
 
-def moe_gemm_setup(dev, M, N2, K, E=288, top_k=8, seed=5):
-    """Random uint4b8 experts (packed), bf16 group scales, Zipf(1.1) routes
-    split by split_align; returns (run, useful_flops, weight_bytes_touched)."""
+def moe_gemm_setup(dev, M, N2, K, E=288, top_k=8, seed=5, keep_codes=False):
+    """Random uint4b8 expert codes, bf16 group scales, Zipf(1.1) routes split
+    by split_align.  Returns (run, useful_flops, weight_bytes_touched, parts):
+    run() issues the four list GEMMs into parts["c"]; parts also holds a, the
+    lists and, with keep_codes, the codes and scales (for the Marlin line)."""
     from kernels import titan_moe_split_align as split_mod
     from kernels.titan_moe_gemm import moe_w4a16_gemm, pack_weights
     g = torch.Generator(device=dev).manual_seed(seed)
-    packed = torch.randint(0, 256, (E * N2 * K // 2,), generator=g, device=dev, dtype=torch.uint8)
+    q = torch.randint(0, 16, (E, N2, K), generator=g, device=dev, dtype=torch.uint8)
+    packed = pack_weights(q)
     scales = (torch.rand(E, K // 128, N2, generator=g, device=dev) * 0.02 + 0.002).to(torch.bfloat16)
     gc = torch.Generator().manual_seed(seed)
     w = torch.arange(1, E + 1, dtype=torch.float64) ** -1.1
@@ -806,15 +809,23 @@ def moe_gemm_setup(dev, M, N2, K, E=288, top_k=8, seed=5):
         for bs, s_ids, e_ids, n in lists:
             moe_w4a16_gemm(a, c, packed, scales, s_ids, e_ids, n, None, bs, top_k, False, M, N2, K)
     experts = int(torch.unique(routes).numel())
-    return run, 2.0 * M * top_k * N2 * K, experts * N2 * K // 2 + experts * (K // 128) * N2 * 2
+    parts = {"a": a, "c": c, "lists": lists, "routes": routes, "top_k": top_k}
+    if keep_codes:
+        parts.update(q=q, scales=scales)
+    else:
+        del q
+    return run, 2.0 * M * top_k * N2 * K, experts * N2 * K // 2 + experts * (K // 128) * N2 * 2, parts
 
 
-def moe_gemm_line(dev, peak_gbs, gm):
+def moe_gemm_line(dev, peak_gbs, gm, marlin=True):
     """us per call of the four list GEMMs (one graph replay, L2 flushed
     before each), useful TFLOP/s and the roofline: time bound = max(useful
-    FLOPs / bf16 peak, weight + scale bytes / HBM peak)."""
+    FLOPs / bf16 peak, weight + scale bytes / HBM peak).  With marlin, the
+    same codes, scales, activations and lists through vLLM's Marlin MoE GEMM
+    (the reference's kernel for this step) on the same GPU, and how far the
+    two outputs are apart."""
     M, N2, K = 2304, 4096, 4096
-    run, flops, wbytes = moe_gemm_setup(dev, M, N2, K)
+    run, flops, wbytes, parts = moe_gemm_setup(dev, M, N2, K, keep_codes=marlin)
     flush = Flusher(dev)
     g, _ = capture(run)
     timed_cold(lambda k: g.replay(), 2, flush)
@@ -826,10 +837,88 @@ def moe_gemm_line(dev, peak_gbs, gm):
     except (OSError, ValueError, KeyError):
         pass
     bound_us = max(flops / (tf_peak * 1e12), wbytes / (peak_gbs * 1e9)) * 1e6
-    return {"shape": f"M={M} tokens x top-8, 288 experts, 2N={N2}, K={K}, Zipf(1.1) routes, four lists",
-            "us_per_call": ms * 1000, "useful_tflops": flops / (ms * 1e-3) / 1e12,
-            "weight_GBps": wbytes / (ms * 1e-3) / 1e9, "roofline_bound_us": bound_us,
-            "frac_of_roofline": bound_us / (ms * 1000), "bf16_peak_tflops": tf_peak}
+    out = {"shape": f"M={M} tokens x top-8, 288 experts, 2N={N2}, K={K}, Zipf(1.1) routes, four lists",
+           "us_per_call": ms * 1000, "useful_tflops": flops / (ms * 1e-3) / 1e12,
+           "weight_GBps": wbytes / (ms * 1e-3) / 1e9, "roofline_bound_us": bound_us,
+           "frac_of_roofline": bound_us / (ms * 1000), "bf16_peak_tflops": tf_peak}
+    if marlin:
+        try:
+            out["vllm_marlin_b200"] = marlin_line(parts, M, N2, K, flush, flops)
+        except Exception as exc:  # a library that does not load or launch here is reported, not fatal
+            out["vllm_marlin_b200"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    return out
+
+
+# The reference's thread configuration for its stock split path: block
+# size -> (thread_k, thread_n, blocks_per_sm) (profiles/sm74/titan_prefill/
+# marlin.py:100-102, :136-140); other block sizes let the op choose.
+MARLIN_THREAD_CFG = {64: (64, 256, 1)}
+
+
+def marlin_weights(q, scales):
+    """Codes q (uint8 [E, N, K], 0..15, CUDA) and bf16 scales [E, K/128, N]
+    -> vLLM Marlin MoE operands: per expert, GPTQ words int32 [K/8, N]
+    (k = 8i + j in bits 4j..4j+3) repacked by gptq_marlin_repack, and the
+    scales permuted by marlin_moe_permute_scales."""
+    from vllm import _custom_ops as ops
+    from vllm.model_executor.layers.quantization.utils.marlin_utils import marlin_moe_permute_scales
+    E, N, K = q.shape
+    perm = torch.empty(0, dtype=torch.int32, device=q.device)
+    shifts = torch.arange(0, 32, 4, dtype=torch.int64, device=q.device)
+    w = torch.empty(E, K // 16, N * 2, dtype=torch.int32, device=q.device)
+    for e in range(E):
+        words = (q[e].t().reshape(K // 8, 8, N).to(torch.int64) << shifts[None, :, None]).sum(1)
+        words = torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
+        w[e] = ops.gptq_marlin_repack(words.contiguous(), perm, K, N, 4)
+    return w, marlin_moe_permute_scales(scales, K, N, 128)
+
+
+def marlin_line(parts, M, N2, K, flush, flops):
+    """vLLM's moe_wna16_marlin_gemm over the four lists exactly as the
+    reference's stock split path calls it (profiles/sm74/titan_prefill/
+    marlin.py:427-437, gate/up form), timed like ours; the outputs are
+    compared element by element with ours."""
+    from vllm import _custom_ops as ops
+    from vllm.model_executor.layers.quantization.utils.marlin_utils import marlin_make_workspace_new
+    from vllm.scalar_type import scalar_types
+    dev = parts["a"].device
+    w, s = marlin_weights(parts["q"], parts["scales"])
+    del parts["q"]
+    a, lists, top_k = parts["a"], parts["lists"], parts["top_k"]
+    c = torch.zeros(M * top_k, N2, dtype=torch.bfloat16, device=dev)
+    ws = marlin_make_workspace_new(dev, 4)
+    tw = torch.ones(M, top_k, dtype=torch.float32, device=dev)
+
+    def run():
+        for bs, s_ids, e_ids, n in lists:
+            tk, tn, bps = MARLIN_THREAD_CFG.get(bs, (-1, -1, -1))
+            ops.moe_wna16_marlin_gemm(
+                a, c, w, None, s, None, None, None, None, None, ws, s_ids, e_ids, n, tw,
+                moe_block_size=bs, top_k=top_k, mul_topk_weights=False, b_q_type=scalar_types.uint4b8,
+                size_m=M, size_n=N2, size_k=K, is_k_full=True, use_atomic_add=False, use_fp32_reduce=True,
+                is_zp_float=False, thread_k=tk, thread_n=tn, blocks_per_sm=bps)
+    try:
+        gr, _ = capture(run)
+        step, how = (lambda k: gr.replay()), "one CUDA graph replay of the four calls"
+    except Exception:
+        gr, step, how = None, (lambda k: run()), "four eager calls"
+    timed_cold(step, 2, flush)
+    ms = statistics.median(timed_cold(step, 5, flush))
+    if gr is not None:
+        gr.reset()
+    ours = parts["c"].float()
+    ref = c.float()
+    listed = torch.zeros(M * top_k, dtype=torch.bool, device=dev)
+    for bs, s_ids, e_ids, n in lists:
+        ids = s_ids[: int(n.item())].long()
+        listed[ids[ids < M * top_k]] = True
+    d = (ours[listed] - ref[listed]).abs()
+    rel = d / ref[listed].abs().clamp_min(1e-30)
+    return {"us_per_call": ms * 1000, "useful_tflops": flops / (ms * 1e-3) / 1e12, "timing": how,
+            "thread_cfg": "reference table {64: (64, 256, 1)}, others chosen by the op",
+            "outputs_max_abs_diff": d.max().item(), "outputs_max_abs": ref[listed].abs().max().item(),
+            "outputs_frac_differing": (d > 0).float().mean().item(),
+            "outputs_within_one_bf16_step": bool(((rel <= 2 ** -7) | (d <= 2 ** -8 * ref[listed].abs().max())).all())}
 
 
 def load_reference_triton():
@@ -945,6 +1034,25 @@ def cpu_model():
     return "unknown"
 
 
+def pin_malloc():
+    """Fix glibc's malloc thresholds for the CPU legs.  Each oracle call
+    allocates about 13 MB of temporaries (the gathered rows as fp32, the
+    products); glibc serves a block from the heap only when it is below its
+    mmap threshold, which starts at 128 KB and rises to the size of the
+    largest mmapped block freed so far (at most 32 MB).  Left dynamic, the
+    temporaries are mmapped and page-faulted afresh on every call in a process
+    that never freed a larger block, and recycled in one that did, a 2.6x
+    difference in per-call time that depends only on what the process did
+    before.  Setting both thresholds makes every process recycle them."""
+    import ctypes
+    try:
+        libc = ctypes.CDLL("libc.so.6")
+    except OSError:
+        return False
+    m_trim_threshold, m_mmap_threshold = -1, -3
+    return bool(libc.mallopt(m_mmap_threshold, 32 << 20)) and bool(libc.mallopt(m_trim_threshold, 1 << 30))
+
+
 def time_cpu_port(rows, steps, seconds, sets=64):
     """One protocol for both CPU legs (the reference arm and the cpu_baseline
     key): the oracle (CPU restatement of the reference algorithm, torch fp32,
@@ -953,6 +1061,7 @@ def time_cpu_port(rows, steps, seconds, sets=64):
     calls (set k % sets) repeated until at least `seconds` have elapsed.
     Returns (us per call, calls timed, seconds timed, threads)."""
     from oracle import oracle as O
+    pin_malloc()
     torch.set_num_threads(os.cpu_count() or 1)
     # Both legs time against a fresh copy made by torch's parallel clone, so
     # the 138 MB of rows are first touched (and placed in memory) the same
@@ -980,7 +1089,7 @@ def cpu_baseline_b1(cache, steps, seconds):
     return {"value": us, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
             "sample": f"{n} B=1 calls of oracle.mla_sparse_attention over the 262144-row cache in {dt:.1f} s: "
                       f"64 index sets (seed {CPU_INDEX_SEED}) each run once untimed, then blocks of {steps} calls "
-                      "until the time bound (torch CPU fp32, all host threads)"}
+                      "until the time bound (torch CPU fp32, all host threads, glibc malloc thresholds pinned)"}
 
 
 # ------------------------------------------------------------ reference arm
@@ -1010,7 +1119,8 @@ def run_reference(args):
         "cpu_baseline": {"value": us, "unit": UNIT, "cores": cores, "kind": "port", "cpu_model": cpu_model(),
                          "sample": f"{n} B=1 calls of the CPU restatement (torch fp32) in {dt:.1f} s: 64 index "
                                    f"sets (seed {CPU_INDEX_SEED}) each run once untimed, then blocks of "
-                                   f"{args.steps} calls until the time bound; cache fill by the C restatement "
+                                   f"{args.steps} calls until the time bound (glibc malloc thresholds pinned); cache fill "
+                                   "by the C restatement "
                                    f"of store_int8 took {fill_s:.2f} s single-threaded"},
         "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -1035,7 +1145,7 @@ def run_profile(args):
         torch.cuda.synchronize()
         return
     if args.profile == "moe_gemm":  # the four list GEMMs; small: M = 512 tokens, 2N = 1024, K = 4096
-        run, _, _ = moe_gemm_setup(dev, 512, 1024, 4096)
+        run, _, _, _ = moe_gemm_setup(dev, 512, 1024, 4096)
         for _ in range(n):
             run()
         torch.cuda.synchronize()

@@ -145,3 +145,56 @@ def test_rejects_bad_arguments(native_lib, cuda_device):
         moe_w4a16_gemm(a, c, packed[:-1], sc, ids, ids, n, None, 16, 8, False, 4, 128, 128)
     with pytest.raises(ValueError):
         moe_w4a16_gemm(a, c, packed, sc, ids, ids, n, None, 16, 8, True, 4, 128, 128)  # weights missing
+
+
+def _vllm_marlin():
+    try:
+        from vllm import _custom_ops as ops
+        torch.ops._C.gptq_marlin_repack  # noqa: B018  (the compiled extension loaded)
+        return ops
+    except Exception as exc:  # vLLM absent or its extension does not load here
+        pytest.skip(f"vLLM Marlin unavailable: {type(exc).__name__}: {exc}")
+
+
+@pytest.mark.parametrize("E,N,K,M", [(8, 256, 512, 96), (32, 512, 1024, 300)])
+def test_matches_vllm_marlin(native_lib, cuda_device, E, N, K, M):
+    """The same codes, scales, activations and split_align lists through
+    vLLM's moe_wna16_marlin_gemm (the kernel the reference runs for this
+    step, called as profiles/sm74/titan_prefill/marlin.py:427-437 does) and
+    through ours: both round fp32 sums of the same bf16 products to bf16, so
+    each element agrees to one bf16 step of itself or 2^-8 of the largest."""
+    _vllm_marlin()
+    from vllm import _custom_ops as ops
+    from vllm.model_executor.layers.quantization.utils.marlin_utils import marlin_make_workspace_new
+    from vllm.scalar_type import scalar_types
+
+    import bench
+    from kernels import titan_moe_split_align as split_mod
+    from kernels.titan_moe_gemm import moe_w4a16_gemm, pack_weights
+    top_k, d = 8, cuda_device
+    g = torch.Generator().manual_seed(E + N + K + M)
+    q = torch.randint(0, 16, (E, N, K), generator=g, dtype=torch.uint8).to(d)
+    scales = (torch.rand(E, K // 128, N, generator=g) * 0.02 + 0.002).to(torch.bfloat16).to(d)
+    routes = _routes(M, top_k, E, "zipf", g).to(torch.int32).to(d)
+    lists = split_mod.split_align(routes, E, split_mod.buffers(M * top_k, E, d))
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(d)
+    ours = torch.zeros(M * top_k, N, dtype=torch.bfloat16, device=d)
+    packed = pack_weights(q)
+    for bs, s, e, n in lists:
+        moe_w4a16_gemm(a, ours, packed, scales, s, e, n, None, bs, top_k, False, M, N, K)
+    w, sm = bench.marlin_weights(q, scales)
+    ref = torch.zeros_like(ours)
+    ws = marlin_make_workspace_new(d, 4)
+    tw = torch.ones(M, top_k, dtype=torch.float32, device=d)
+    for bs, s, e, n in lists:
+        tk, tn, bps = bench.MARLIN_THREAD_CFG.get(bs, (-1, -1, -1))
+        ops.moe_wna16_marlin_gemm(a, ref, w, None, sm, None, None, None, None, None, ws, s, e, n, tw,
+                                  moe_block_size=bs, top_k=top_k, mul_topk_weights=False,
+                                  b_q_type=scalar_types.uint4b8, size_m=M, size_n=N, size_k=K, is_k_full=True,
+                                  use_atomic_add=False, use_fp32_reduce=True, is_zp_float=False,
+                                  thread_k=tk, thread_n=tn, blocks_per_sm=bps)
+    torch.cuda.synchronize()
+    o, r = ours.float(), ref.float()
+    tol = torch.maximum(r.abs() * 2 ** -7, torch.full_like(r, 2 ** -8) * r.abs().max())
+    assert r.abs().max() > 0
+    assert bool(((o - r).abs() <= tol).all()), (o - r).abs().max().item()
