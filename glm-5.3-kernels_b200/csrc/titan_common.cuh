@@ -3,6 +3,7 @@
 // bulk (TMA) copies.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -24,6 +25,24 @@ void set_error(const char *fmt, ...);
 std::mutex &setup_mutex();
 int fail(int code, const char *fmt, ...);
 int check_launch(const char *what);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda); nullptr when the driver does not provide it.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+inline EncodeTiledFn tensor_map_encoder() {
+  static const EncodeTiledFn encode = [] {  // looked up once (thread-safe static initialisation)
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<EncodeTiledFn>(fn);
+    cudaGetLastError();
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
+  return encode;
+}
 
 // Device error word (one per device, in this module; the library is a single
 // translation unit, titan_b200.cu).  Bounded waits that give up write a

@@ -997,20 +997,8 @@ static cudaError_t launch_combine(const Params &prm, int groups, cudaStream_t s)
 // Rows at or beyond min(seq_kv, 2^31) are outside the map (int32 indices
 // cannot reach further).  Encoded through the driver entry point; the last
 // encoding of each host thread is reused.
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
 static int rows_tensor_map(const void *kv, int64_t seq_kv, int64_t kv_row_stride, const void *dummy, CUtensorMap *out) {
-  static const EncodeTiledFn encode = [] {  // looked up once (thread-safe static initialisation)
-    void *fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      return reinterpret_cast<EncodeTiledFn>(fn);
-    cudaGetLastError();
-    return static_cast<EncodeTiledFn>(nullptr);
-  }();
+  const EncodeTiledFn encode = tensor_map_encoder();
   if (encode == nullptr) return fail(TITAN_ERR_CUDA, "mla: cuTensorMapEncodeTiled is unavailable");
   // seq_kv == 0: no row is valid and nothing is loaded; any aligned address
   // makes a well-formed map.

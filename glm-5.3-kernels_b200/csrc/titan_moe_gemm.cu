@@ -14,59 +14,59 @@
 // sums in fp32, C in bf16.  The dequantised weight is rounded to bf16 before
 // the MMA, as Marlin's W4A16 dequantisation does.
 //
-// B200 design, one persistent CTA of 19 warps per SM, work item = (block b,
-// 256 output features: two MMAs of M = 128 sharing the activation tile);
-// each MMA computes D[128 features x bs rows] = W_e[128 x K] . A_rows[bs x K]^T
-// with N = bs in {16..64}:
-//  * warps 0, 14..18: per 64-wide K step (each warp every sixth step), one
-//    lane bulk-copies the pair's 8 KB of packed int4 weights and its group
-//    scales; the 32 lanes copy the
-//    block's activation rows (row s / top_k; padding rows zero-filled) with
-//    16-byte cp.async straight into a 128B-swizzled, K-major shared tile;
-//    ten stages (~165 KB in flight per SM: the weight stream is
-//    latency-bound with fewer, and one warp cannot issue the small copies
-//    fast enough);
-//  * warps 2..9: dequantise the weights straight into tensor memory (one
-//    thread per feature row, one tcgen05.st of 64 bf16 per step; nibbles
-//    pre-interleaved by pack_weights so one LOP3 yields a bf16 pair), three
-//    buffers; the MMA reads its A operand there, so the weights never pass
-//    through shared memory in bf16;
-//  * warp 1 (one lane): four tcgen05.mma kind::f16 (K = 16 each) per step
-//    and tile into double-buffered tensor-memory accumulators (2 x 2 x 64
-//    columns);
-//    tcgen05.commit frees the stage / publishes the accumulator;
+// B200 design, one persistent CTA of 14 warps per SM, work item = (block b,
+// 256 output features: two MMA tiles of M = 128 sharing the activation
+// tile), pipeline step = 128 k (one scale group):
+//  * warp 0 (producer): lane 0 bulk-copies the step's packed int4 weights
+//    (16 KB for the tile pair) and group scales; the lanes gather the
+//    block's activation rows with TMA tile::gather4 (four 128-byte rows per
+//    load, two 64-k halves) straight into 128B-swizzled K-major tiles,
+//    padding rows as out-of-map rows that read as zeros; everything lands on
+//    one mbarrier per stage, six stages;
+//  * warps 2..9 (dequantisation): thread = feature row of one tile; the
+//    step's 128 k become 64 columns of bf16 pairs in tensor memory (two
+//    tcgen05.st), two buffers; the weights never pass through shared memory
+//    in bf16;
+//  * warp 1 (one lane): sixteen tcgen05.mma kind::f16 per step (2 tiles x
+//    8 x K16, A = the dequantised weights in tensor memory, B = the rows)
+//    into double-buffered accumulators, then one tcgen05.commit that frees
+//    the stage and the weight buffer together.  The MMA lane waits on one
+//    barrier per step (the dequantisation warps have seen the stage land),
+//    so a round of synchronisation serves sixteen MMAs;
 //  * warps 10..13: tcgen05.ld of the accumulator (one lane quarter each),
 //    topk weighting, bf16 stores of the block's rows.
 // Every wait is an mbarrier wait bounded in time; a wait that gives up sets
-// the device error word and the CTA abandons its remaining work items.
+// the device error word and the CTA abandons its remaining work items, then
+// waits (bounded) for its copies in flight and its MMAs before it releases
+// tensor memory and exits.
 #include "titan_common.cuh"
 
 namespace titan {
 namespace moeg {
 
-constexpr int kBM = 128;           // output features per MMA (M)
-constexpr int kNT = 2;             // MMAs (128-feature tiles) per work item, sharing one activation tile
-constexpr int kBK = 64;            // K per pipeline step: one 128-byte bf16 row
-constexpr int kStages = 10;        // raw stages (packed weights, scales, activation rows)
-constexpr int kWBufs = 3;          // dequantised weight buffers in tensor memory
+constexpr int kBM = 128;           // output features per MMA tile (M)
+constexpr int kNT = 2;             // MMA tiles per work item, sharing one activation tile
+constexpr int kBK = 128;           // K per pipeline step (one scale group)
+constexpr int kHalfK = 64;         // K per 128-byte swizzled row: the activation tile is two halves
+constexpr int kStages = 6;         // stages (packed weights, scales, activation rows)
+constexpr int kWBufs = 2;          // dequantised weight buffers in tensor memory
 constexpr int kMaxBS = 64;         // block rows (MMA N)
-constexpr int kProducers = 6;      // producer warps: 0 and 14..18, each issuing every 6th step
 constexpr int kDeqWarps = 8;
-constexpr int kWarps = 19;         // 0 producer, 1 MMA, 2..9 dequantisation, 10..13 epilogue, 14..18 producers
+constexpr int kWarps = 14;         // 0 producer, 1 MMA, 2..9 dequantisation, 10..13 epilogue
 constexpr int kThreads = kWarps * 32;
-constexpr int kStepWBytes = kBM * kBK / 2;  // packed int4 weights of one 128-feature tile per step: 4 KB
+constexpr int kStepWBytes = kBM * kBK / 2;   // packed int4 of one tile per step: 8 KB
+constexpr int kHalfBytes = kMaxBS * 128;     // one 64-k half of the activation tile: 8 KB
 constexpr int kTmemCols = 512;
 constexpr int kColAcc = 0;         // accumulators: [2 sets][kNT tiles][64 fp32 columns]
-constexpr int kColA = 256;         // dequantised weights: [kWBufs][kNT tiles][32 columns of bf16 pairs]
+constexpr int kColA = 256;         // dequantised weights: [kWBufs][kNT tiles][64 columns of bf16 pairs]
 
 struct Smem {
-  alignas(1024) uint8_t atile[kStages][kMaxBS * kBK * 2];   // 8 KB per stage, bf16, SW128 K-major
-  alignas(128) uint8_t wraw[kStages][kNT * kStepWBytes];    // 8 KB per stage: the pair's packed int4
-  alignas(16) uint16_t sscale[kStages][kNT * kBM];          // the step's group scales (bf16 bits)
-  alignas(8) uint64_t full[kStages];                        // weights + scales (tx bytes) and rows (32 lanes)
-  uint64_t empty[kStages];                                  // stage consumed (MMA commit)
+  alignas(1024) uint8_t act[kStages][2][kHalfBytes];       // bf16 rows, SW128 K-major, two 64-k halves
+  alignas(128) uint8_t wraw[kStages][kNT * kStepWBytes];   // the pair's packed int4 of the step
+  alignas(16) uint16_t sscale[kStages][kNT * kBM];         // the step's group scales (bf16 bits)
+  alignas(8) uint64_t full[kStages];                        // weights + scales + rows landed (tx bytes)
+  uint64_t done[kStages];                                   // the step's MMAs completed (commit)
   uint64_t deq[kWBufs];                                     // dequantised tiles written (8 warps)
-  uint64_t wfree[kWBufs];                                   // dequantised tiles consumed (MMA commit)
   uint64_t acc_full[2];                                     // accumulators ready (MMA commit)
   uint64_t acc_empty[2];                                    // accumulators read out (4 warps)
   uint64_t drain;                                           // every MMA of this CTA completed
@@ -75,9 +75,8 @@ struct Smem {
 };
 
 struct Params {
-  const uint8_t *a;                  // activations, bf16 rows a_stride elements apart
-  int64_t a_stride;
-  const uint8_t *wq;                 // packed weights: per expert, tile pairs x k steps x 4 KB tiles
+  int64_t a_stride;                  // elements between activation rows (the tensor map holds the rows)
+  const uint8_t *wq;                 // packed weights: per expert, tile pairs x k steps x 8 KB tiles
   const __nv_bfloat16 *scales;       // [E][K/128][N]
   const int32_t *sorted_ids;
   const int32_t *expert_ids;
@@ -208,18 +207,6 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
-// 16-byte asynchronous global -> shared copy reading `src_bytes` (16 or 0:
-// zeros, nothing read).
-__device__ __forceinline__ void cp_async_16_zfill(void *dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-// Arrive on the mbarrier once this thread's earlier cp.async copies have landed
-// (the barrier's expected count includes this arrival).
-__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Wait with the CTA-wide abort flag: once one role has given up, the others
 // stop waiting at their next wait.  Bounded like mbar_wait_bounded, but the
 // clock is read once per 32 polls, so waiting warps take fewer issue slots
@@ -240,8 +227,11 @@ __device__ __forceinline__ bool wait_or_abort(Smem &sm, uint64_t *bar, uint32_t 
   }
 }
 
+// Bounded wait for a stage's copies at exit (they land in microseconds).
+constexpr long long kDrainWaitCycles = 20000000LL;
+
 __global__ void __launch_bounds__(kThreads, 1)
-    moe_w4a16_gemm_kernel(const Params p) {
+    moe_w4a16_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap amap) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The dynamic window is 16-byte aligned by contract; align the tiles to 1024.
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -249,13 +239,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 33);  // producer lane 0 (with the bulk bytes) + 32 row-copy lanes
-      mbar_init(&sm.empty[s], 1);
+      mbar_init(&sm.full[s], 1);   // the producer's expect-tx arrival; the copies complete the bytes
+      mbar_init(&sm.done[s], 1);
     }
-    for (int w = 0; w < kWBufs; ++w) {
-      mbar_init(&sm.deq[w], kDeqWarps);
-      mbar_init(&sm.wfree[w], 1);
-    }
+    for (int w = 0; w < kWBufs; ++w) mbar_init(&sm.deq[w], kDeqWarps);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.acc_full[b], 1);
       mbar_init(&sm.acc_empty[b], 4);
@@ -264,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm.abort_flag = 0;
     fence_mbar_init();
   }
+  if (tid == 32) prefetch_tensormap(&amap);
   if (warp == 1) {  // tensor-memory owner
     tmem_alloc(&sm.tmem_base, kTmemCols);
     tmem_relinquish();
@@ -284,13 +272,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Item = (block b, feature tiles kNT np .. kNT np + nts - 1).
   auto tiles_of = [&](int np) { return min(kNT, ntn - kNT * np); };
 
-  if (warp == 0 || warp >= 2 + kDeqWarps + 4) {
-    // --------------------------------------------------------- producers
-    // Producer pi issues the steps g with g % kProducers == pi: the copies of
-    // one step are small (4 KB of weights per tile, 128-byte activation
-    // rows) and their issue cost, not their bytes, bounds a single issuing
-    // warp, so four warps issue in parallel.
-    const int pi = warp == 0 ? 0 : warp - (2 + kDeqWarps + 4) + 1;
+  if (warp == 0) {
+    // --------------------------------------------------------- producer
+    // Lane l < bs / 2 issues gather l of each step: half h = l / (bs / 4),
+    // rows 4 i .. 4 i + 3 with i = l % (bs / 4).
+    const int ng = bs >> 2;
+    const int gh = lane < 2 * ng ? lane / ng : 0, gi = lane < 2 * ng ? lane % ng : 0;
     uint32_t g = 0;  // step counter of this CTA
     bool ok = true;
     for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
@@ -298,49 +285,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int np = (int)(item - b * npairs), nts = tiles_of(np);
       const int e = __ldg(p.expert_ids + b);
       if (e < 0 || e >= p.num_experts) continue;
-      // Activation row of block rows lane and lane + 32 (-1: padding).
-      int row_lo = -1, row_hi = -1;
+      // Activation row of block rows lane and lane + 32 (size_m: padding,
+      // outside the map, reads as zeros), then this lane's four gather rows.
+      int row_lo, row_hi;
       {
         const int64_t s0 = lane < bs ? __ldg(p.sorted_ids + b * bs + lane) : -1;
         const int64_t s1 = lane + 32 < bs ? __ldg(p.sorted_ids + b * bs + lane + 32) : -1;
-        row_lo = (s0 >= 0 && s0 < pad_id) ? (int)(s0 / p.top_k) : -1;
-        row_hi = (s1 >= 0 && s1 < pad_id) ? (int)(s1 / p.top_k) : -1;
+        row_lo = (s0 >= 0 && s0 < pad_id) ? (int)(s0 / p.top_k) : p.size_m;
+        row_hi = (s1 >= 0 && s1 < pad_id) ? (int)(s1 / p.top_k) : p.size_m;
       }
-      // Packed weights of the pair: per step, its nts tiles' 4 KB back to back.
+      int gr[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int j = 4 * gi + m;
+        const int lo = __shfl_sync(0xffffffffu, row_lo, j & 31);
+        const int hi = __shfl_sync(0xffffffffu, row_hi, j & 31);
+        gr[m] = j < 32 ? lo : hi;
+      }
+      // Packed weights of the pair: per step, its nts tiles' 8 KB back to back.
       const uint8_t *wsrc = p.wq + ((int64_t)e * ntn * nk + (int64_t)kNT * np * nk) * kStepWBytes;
-      const __nv_bfloat16 *ssrc = p.scales + (int64_t)e * (p.K / 128) * p.N + kNT * np * kBM;
+      const __nv_bfloat16 *ssrc = p.scales + (int64_t)e * nk * p.N + kNT * np * kBM;
+      const uint32_t bytes = (uint32_t)(nts * (kStepWBytes + kBM * 2) + 2 * bs * 128);
       for (int kc = 0; kc < nk; ++kc, ++g) {
-        if ((int)(g % kProducers) != pi) continue;
         const int s = (int)(g % kStages);
         const uint32_t use = g / kStages;
-        if (use > 0) ok = wait_or_abort(sm, &sm.empty[s], (use - 1) & 1u);
+        if (use > 0) ok = wait_or_abort(sm, &sm.done[s], (use - 1) & 1u);
         if (!ok) break;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nts * (kStepWBytes + kBM * 2)));
+          mbar_arrive_expect_tx(&sm.full[s], bytes);
           bulk_g2s(sm.wraw[s], wsrc + (int64_t)kc * nts * kStepWBytes, (uint32_t)(nts * kStepWBytes), &sm.full[s]);
-          bulk_g2s(sm.sscale[s], ssrc + (int64_t)(kc >> 1) * p.N, (uint32_t)(nts * kBM * 2), &sm.full[s]);
+          bulk_g2s(sm.sscale[s], ssrc + (int64_t)kc * p.N, (uint32_t)(nts * kBM * 2), &sm.full[s]);
         }
-        // Activation rows: lane l copies 16-byte chunk l & 7 of rows
-        // (l >> 3) + 4 i into their swizzled slots; padding rows are
-        // zero-filled without reading memory.  Each lane arrives once its
-        // copies have landed.
-        {
-          const int ch = lane & 7;
-          uint8_t *dst = sm.atile[s];
-          const int64_t kbyte = (int64_t)kc * (kBK * 2) + ch * 16;
-#pragma unroll 4
-          for (int j = lane >> 3; j < kMaxBS; j += 4) {
-            const int row = __shfl_sync(0xffffffffu, j < 32 ? row_lo : row_hi, j & 31);
-            if (j < bs) {
-              const uint8_t *src = row >= 0 ? p.a + (int64_t)row * p.a_stride * 2 + kbyte : p.a;
-              cp_async_16_zfill(dst + sw128_offset(j, ch), src, row >= 0 ? 16u : 0u);
-            }
-          }
-          cp_async_mbar_arrive_noinc(&sm.full[s]);
-        }
+        __syncwarp();
+        if (lane < 2 * ng)
+          tma_gather4(&sm.act[s][gh][gi * 512], &amap, kc * kBK + gh * kHalfK, gr[0], gr[1], gr[2], gr[3],
+                      &sm.full[s]);
       }
     }
-    cp_async_wait<0>();
+    // Copies issued and not consumed (after an abort) land before the CTA
+    // releases its shared memory: wait for the last phase of every stage.
+    if (lane == 0) {
+      const uint32_t first = g > (uint32_t)kStages ? g - kStages : 0u;
+      for (uint32_t gg = first; gg < g; ++gg)
+        mbar_wait_bounded(&sm.full[gg % kStages], (gg / kStages) & 1u, kDrainWaitCycles);
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA
     const uint32_t idesc = idesc_bf16(kBM, bs);
@@ -358,21 +347,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       for (int kc = 0; kc < nk && ok; ++kc, ++g) {
         const int s = (int)(g % kStages), wb = (int)(g % kWBufs);
-        const uint32_t use = g / kStages, wuse = g / kWBufs;
-        ok = wait_or_abort(sm, &sm.full[s], use & 1u) && wait_or_abort(sm, &sm.deq[wb], wuse & 1u);
+        // The dequantisation warps arrive only after they have seen the
+        // stage land, so this one wait covers the rows as well.
+        ok = wait_or_abort(sm, &sm.deq[wb], (g / kWBufs) & 1u);
         if (!ok) break;
-        fence_proxy_async_smem();  // rows written by cp.async: visible to the tensor core
         tc_fence_after();
         if (lane == 0) {
           for (int t = 0; t < nts; ++t) {
             const uint32_t d = tmem + (uint32_t)(kColAcc + ab * (kNT * 64) + t * 64);
-            const uint32_t aw = tmem + (uint32_t)(kColA + wb * (kNT * 32) + t * 32);
+            const uint32_t aw = tmem + (uint32_t)(kColA + wb * (kNT * 64) + t * 64);
 #pragma unroll
             for (int k = 0; k < kBK / 16; ++k)
-              umma_bf16_ts(d, aw + 8 * k, sw128_desc(sm.atile[s], 32 * k), idesc, (kc > 0 || k > 0) ? 1u : 0u);
+              umma_bf16_ts(d, aw + 8 * k, sw128_desc(sm.act[s][k >> 2], 32 * (k & 3)), idesc,
+                           (kc > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&sm.empty[s]);
-          umma_commit(&sm.wfree[wb]);
+          umma_commit(&sm.done[s]);  // frees the stage and the weight buffer
         }
         __syncwarp();
       }
@@ -389,8 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 2 + kDeqWarps) {
     // ---------------------------------------------------- dequantisation
     // Warp w writes tensor-memory lanes 32 (w % 4) .. + 31: thread = feature
-    // row r of tile t, its 64 dequantised k of the step as 32 columns of bf16
-    // pairs (one tcgen05.st).
+    // row r of tile t, its 128 dequantised k of the step as 64 columns of
+    // bf16 pairs (two tcgen05.st).
     const int r = 32 * (warp & 3) + lane;
     const int t = (warp - 2) >> 2;
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
@@ -403,28 +392,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (e < 0 || e >= p.num_experts) continue;
       for (int kc = 0; kc < nk; ++kc, ++g) {
         const int s = (int)(g % kStages), wb = (int)(g % kWBufs);
-        const uint32_t use = g / kStages, wuse = g / kWBufs;
-        ok = wait_or_abort(sm, &sm.full[s], use & 1u);
-        if (ok && wuse > 0) ok = wait_or_abort(sm, &sm.wfree[wb], (wuse - 1) & 1u);
+        ok = wait_or_abort(sm, &sm.full[s], (g / kStages) & 1u);
+        // Buffer wb was last read by the MMAs of step g - kWBufs.
+        if (ok && g >= (uint32_t)kWBufs) {
+          const uint32_t gp = g - kWBufs;
+          ok = wait_or_abort(sm, &sm.done[gp % kStages], (gp / kStages) & 1u);
+        }
         if (!ok) break;
+        tc_fence_after();
         if (t < nts) {
-          // Packed layout of a tile step: [half h][row r][16 bytes], half h =
-          // the row's 16-byte bf16 chunks 4h .. 4h + 3.
-          const uint8_t *raw = sm.wraw[s] + t * kStepWBytes;
-          const uint4 w0 = *reinterpret_cast<const uint4 *>(raw + r * 16);
-          const uint4 w1 = *reinterpret_cast<const uint4 *>(raw + 2048 + r * 16);
-          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          // Packed layout of a tile step: [quarter c][row r][16 bytes],
+          // quarter c = the row's k 32 c .. 32 c + 31 (four 32-bit words of
+          // eight k each).
+          const uint8_t *raw = sm.wraw[s] + t * kStepWBytes + r * 16;
           const uint32_t sc = sm.sscale[s][t * kBM + r];
           const uint32_t sc2 = sc | (sc << 16);
-          uint32_t v[32];
+          const uint32_t col = (uint32_t)(kColA + wb * (kNT * 64) + t * 64);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {  // chunk c = k 8c .. 8c + 7 = columns 4c .. 4c + 3
-            uint32_t x[4];
-            nibbles_to_bf16x8(words[c], x);
+          for (int hh = 0; hh < 2; ++hh) {
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(raw + (2 * hh) * 2048);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(raw + (2 * hh + 1) * 2048);
+            const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            uint32_t v[32];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) v[4 * c + i] = bf16x2_mul(x[i], sc2);
+            for (int c = 0; c < 8; ++c) {  // word c = k 8c .. 8c + 7 of this half = columns 4c .. 4c + 3
+              uint32_t x[4];
+              nibbles_to_bf16x8(words[c], x);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) v[4 * c + i] = bf16x2_mul(x[i], sc2);
+            }
+            tmem_st32(tmem + lane_base + col + 32u * hh, v);
           }
-          tmem_st32(tmem + lane_base + (uint32_t)(kColA + wb * (kNT * 32) + t * 32), v);
           tmem_st_wait();
         }
         tc_fence_before();
@@ -497,6 +495,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 namespace {
 std::atomic<int> g_moeg_ready[64];
+
+// Tensor map of the activations for the row gather: bf16 [size_m][k], rows
+// a_stride elements apart, boxes of 64 elements (one 128-byte swizzled row)
+// by one row; row size_m and beyond (the padding rows' coordinate) read as
+// zeros.  The last encoding of each host thread is reused.
+int act_tensor_map(const void *a, int64_t size_m, int64_t k, int64_t a_stride, CUtensorMap *out) {
+  const EncodeTiledFn encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(TITAN_ERR_CUDA, "moe_w4a16_gemm: cuTensorMapEncodeTiled is unavailable");
+  static thread_local const void *last_a = nullptr;
+  static thread_local int64_t last_m = -1, last_k = -1, last_stride = -1;
+  static thread_local CUtensorMap last_map;
+  if (a == last_a && size_m == last_m && k == last_k && a_stride == last_stride) {
+    *out = last_map;
+    return TITAN_OK;
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)size_m};
+  const cuuint64_t strides[1] = {(cuuint64_t)a_stride * 2};
+  const cuuint32_t box[2] = {64, 1};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(a), dims, strides, box, elem,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TITAN_ERR_CUDA, "moe_w4a16_gemm: cuTensorMapEncodeTiled failed (%d) for rows=%lld k=%lld stride=%lld",
+                (int)r, (long long)size_m, (long long)k, (long long)a_stride);
+  last_a = a;
+  last_m = size_m;
+  last_k = k;
+  last_stride = a_stride;
+  last_map = *out;
+  return TITAN_OK;
+}
 std::atomic<int> g_moeg_sms[64];
 }  // namespace
 }  // namespace titan
@@ -523,8 +553,9 @@ extern "C" int titan_moe_w4a16_gemm(const void *a, int64_t a_stride, int64_t siz
   if (a == nullptr || c == nullptr || wq_packed == nullptr || scales == nullptr || sorted_ids == nullptr ||
       expert_ids == nullptr || ntpp == nullptr || (mul_topk_weights && topk_weights == nullptr))
     return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_w4a16_gemm: null pointer");
-  if ((uintptr_t)a % 16 || (a_stride * 2) % 16 || a_stride < k || (uintptr_t)wq_packed % 16)
-    return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_w4a16_gemm: A rows and packed weights must be 16-byte aligned");
+  if ((uintptr_t)a % 16 || (a_stride * 2) % 16 || a_stride < k || (uintptr_t)wq_packed % 16 || (uintptr_t)scales % 16)
+    return fail(TITAN_ERR_INVALID_ARGUMENT,
+                "moe_w4a16_gemm: A rows, packed weights and scales must be 16-byte aligned");
   if (c_stride < n) return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_w4a16_gemm: C rows shorter than N");
   if (size_m == 0 || max_blocks == 0) return TITAN_OK;
 
@@ -544,8 +575,10 @@ extern "C" int titan_moe_w4a16_gemm(const void *a, int64_t a_stride, int64_t siz
       g_moeg_ready[dev].store(1, std::memory_order_release);
     }
   }
+  CUtensorMap amap;
+  const int rc = act_tensor_map(a, size_m, k, a_stride, &amap);
+  if (rc != TITAN_OK) return rc;
   Params prm;
-  prm.a = static_cast<const uint8_t *>(a);
   prm.a_stride = a_stride;
   prm.wq = static_cast<const uint8_t *>(wq_packed);
   prm.scales = static_cast<const __nv_bfloat16 *>(scales);
@@ -574,7 +607,7 @@ extern "C" int titan_moe_w4a16_gemm(const void *a, int64_t a_stride, int64_t siz
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, moe_w4a16_gemm_kernel, prm);
+  e = cudaLaunchKernelEx(&cfg, moe_w4a16_gemm_kernel, prm, amap);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "moe_w4a16_gemm launch: %s", cudaGetErrorString(e));
   return TITAN_OK;
 }

@@ -15,9 +15,10 @@ s = sorted_ids[b * block_size : (b + 1) * block_size]:
 
 The kernel (`titan_moe_w4a16_gemm`, csrc/titan_moe_gemm.cu) runs on the
 5th-generation tensor cores: tcgen05.mma with the accumulator in tensor
-memory, activation rows gathered by TMA, weights dequantised in shared
-memory.  Weights use this build's own packing (`pack_weights`), not Marlin's
-tile permutation; the scales keep the [E, K / 128, N] layout.
+memory, activation rows gathered by TMA (tile::gather4), weights
+dequantised into tensor memory as the MMA's A operand.  Weights use this
+build's own packing (`pack_weights`), not Marlin's tile permutation; the
+scales keep the [E, K / 128, N] layout.
 """
 import ctypes
 
@@ -30,31 +31,31 @@ except ImportError:
 
 GROUP = 128
 TILE_N = 128
-STEP_K = 64
+STEP_K = 128
 _NIBBLE_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
 
 
 def pack_weights(q: torch.Tensor) -> torch.Tensor:
     """uint4b8 codes q (uint8 [E, N, K], values 0..15) -> the kernel's packed
     layout, uint8 [E * N * K / 2].  Per expert, the 128-feature tiles go in
-    pairs (a last odd tile alone); per pair and 64-wide k step, the pair's
-    tiles back to back, 4 KB each as [half][128 rows][16 B] (half h: the
-    row's k 32h .. 32h + 31).  A 32-bit word holds the eight k of one 16-byte
-    chunk of a bf16 row, its nibble positions 0..7 holding k offsets
-    0, 2, 4, 6, 1, 3, 5, 7, so that positions (i, i + 4) are the consecutive
-    pair (2i, 2i + 1)."""
+    pairs (a last odd tile alone); per pair and 128-wide k step (one scale
+    group), the pair's tiles back to back, 8 KB each as
+    [quarter c][128 rows][16 B] (quarter c: the row's k 32c .. 32c + 31).  A
+    32-bit word holds eight consecutive k, its nibble positions 0..7 holding
+    k offsets 0, 2, 4, 6, 1, 3, 5, 7, so that positions (i, i + 4) are the
+    consecutive pair (2i, 2i + 1)."""
     if q.dtype != torch.uint8 or q.dim() != 3:
         raise ValueError("pack_weights: q must be uint8 [E, N, K]")
     E, N, K = q.shape
     if N % TILE_N or K % GROUP:
         raise ValueError("pack_weights: N must be a multiple of 128 and K of 128")
     ntn, nk = N // TILE_N, K // STEP_K
-    x = q.reshape(E, ntn, TILE_N, nk, 2, 4, 8)[..., list(_NIBBLE_ORDER)]
-    b = (x[..., 0::2] & 15) | ((x[..., 1::2] & 15) << 4)        # [E, tile, r, kc, h, c, 4]
-    blocks = b.permute(0, 1, 3, 4, 2, 5, 6).reshape(E, ntn, nk, 4096)
+    x = q.reshape(E, ntn, TILE_N, nk, 4, 4, 8)[..., list(_NIBBLE_ORDER)]  # [E, tile, r, kc, c, w, 8]
+    b = (x[..., 0::2] & 15) | ((x[..., 1::2] & 15) << 4)                 # [E, tile, r, kc, c, w, 4]
+    blocks = b.permute(0, 1, 3, 4, 2, 5, 6).reshape(E, ntn, nk, 8192)
     parts = []
     if ntn >= 2:
-        full = blocks[:, :ntn // 2 * 2].reshape(E, ntn // 2, 2, nk, 4096).permute(0, 1, 3, 2, 4)
+        full = blocks[:, :ntn // 2 * 2].reshape(E, ntn // 2, 2, nk, 8192).permute(0, 1, 3, 2, 4)
         parts.append(full.reshape(E, -1))
     if ntn % 2:
         parts.append(blocks[:, ntn - 1].reshape(E, -1))

@@ -1,7 +1,7 @@
 # SPDX-License-Identifier: Apache-2.0
 """Host side of the W4A16 MoE GEMM (no GPU): the packed weight layout the
 kernel reads, checked by unpacking it the way the kernel does (per step of
-64 k, per half, per row, nibble pairs at positions (i, i + 4))."""
+128 k, per quarter, per row, nibble pairs at positions (i, i + 4))."""
 import numpy as np
 import pytest
 import torch
@@ -11,8 +11,8 @@ from kernels.titan_moe_gemm import pack_weights
 
 def _unpack_like_kernel(packed, E, N, K):
     """Read the packed bytes at the kernel's offsets: tile t of pair np at
-    step kc is at ((e ntn + 2 np) nk + kc nts + t) x 4 KB."""
-    ntn, nk = N // 128, K // 64
+    step kc is at ((e ntn + 2 np) nk + kc nts + t) x 8 KB."""
+    ntn, nk = N // 128, K // 128
     flat = packed.numpy()
     out = np.zeros((E, N, K), np.uint8)
     for e in range(E):
@@ -20,18 +20,17 @@ def _unpack_like_kernel(packed, E, N, K):
             nts = min(2, ntn - 2 * np_)
             for kc in range(nk):
                 for t in range(nts):
-                    off = ((e * ntn + 2 * np_) * nk + kc * nts + t) * 4096
-                    blk = flat[off:off + 4096].reshape(2, 128, 16)
+                    off = ((e * ntn + 2 * np_) * nk + kc * nts + t) * 8192
+                    blk = flat[off:off + 8192].reshape(4, 128, 16)
                     tile = 2 * np_ + t
-                    for h in range(2):
-                        words = blk[h].copy().view(np.uint32)                  # [128, 4]
-                        for c4 in range(4):
-                            w = words[:, c4].astype(np.uint64)
-                            c = 4 * h + c4                                     # 16-byte chunk of the bf16 row
+                    for c in range(4):
+                        words = blk[c].copy().view(np.uint32)                  # [128, 4]
+                        for w4 in range(4):
+                            w = words[:, w4].astype(np.uint64)
                             for i in range(4):
                                 lo = (w >> (4 * i)) & 15                       # position i      -> k 2i
                                 hi = (w >> (16 + 4 * i)) & 15                  # position i + 4  -> k 2i + 1
-                                k0 = kc * 64 + 8 * c + 2 * i
+                                k0 = kc * 128 + 32 * c + 8 * w4 + 2 * i
                                 out[e, tile * 128:(tile + 1) * 128, k0] = lo
                                 out[e, tile * 128:(tile + 1) * 128, k0 + 1] = hi
     return out
