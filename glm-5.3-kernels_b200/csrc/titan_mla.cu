@@ -23,17 +23,21 @@
 //    The indices reach shared memory through warp 0's 4-byte cp.async ring
 //    five tiles ahead (paged: positions eight and block-table entries five
 //    tiles ahead), so no thread waits on a load issued one tile earlier.
-//  * QK: mma.sync m16n8k16 f16 with fp32 accumulate (A = 16 heads x 16 dims
-//    of q in registers).  int8 -> f16 is exact (one PRMT + one packed add per
-//    pair); q enters as f16 scaled by a power of two per warp and head, undone
-//    in the score reduction.  The k dimension is permuted identically for q
-//    and k so that each lane's 16 contiguous bytes feed four k-steps.  The 8
-//    warps' partial scores meet in shared memory; 16 lanes per head run the
-//    online softmax, whose running max moves only by steps above 8 (log2).
-//  * PV: the f16 K fragments are transposed in registers with movmatrix (rows
-//    become the reduction dim), A = f16(p * scale * 2^-e) from shared memory
-//    (e: exponent of the largest row scale so far); each accumulator lane
-//    then owns 16 contiguous output dims.
+//  * QK: mma.sync m16n8k16 with fp32 accumulate (A = 16 heads x 16 dims of q
+//    in registers).  Decode-length CTAs keep the reference's bf16 operands
+//    (int8 -> bf16 exact through the fp32 magic number); single-pass CTAs of
+//    at least kF16MinTiles tiles (prefill shapes) use f16: int8 -> f16 exact
+//    in one PRMT + one packed add per pair, q scaled by a power of two per
+//    warp and head, undone in the score reduction.  The k dimension is
+//    permuted identically for q and k so that each lane's 16 contiguous bytes
+//    feed four k-steps.  The 8 warps' partial scores meet in shared memory;
+//    16 lanes per head run the online softmax, whose running max moves only
+//    by steps above kLazyMax (log2 units); tiles whose rows are all masked
+//    are skipped.
+//  * PV: the K fragments are transposed in registers with movmatrix (rows
+//    become the reduction dim), A = bf16(p * scale) (f16 path: f16(p * scale
+//    * 2^-e), e the exponent of the largest row scale so far) from shared
+//    memory; each accumulator lane then owns 16 contiguous output dims.
 //  * Split merge: the C <= 16 splits of a (token, head group) that form one
 //    thread-block cluster merge through distributed shared memory, each CTA
 //    reducing 512 / C dims; a single cluster writes the bf16 output directly.

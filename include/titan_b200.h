@@ -318,10 +318,11 @@ int titan_device_error(int *error_out, int clear_after, titan_stream_t stream);
  *   a            bf16 [size_m rows][k], rows a_stride elements apart (16-byte aligned)
  *   c            bf16, rows c_stride elements apart; only listed rows are written
  *   wq_packed    uint8, E x n x k / 2 bytes: per expert, 128-feature tiles in
- *                pairs, per pair and 64-wide k step the pair's 4 KB tiles back
- *                to back (kernels/titan_moe_gemm.py pack_weights); 16-byte
- *                aligned; titan_moe_w4a16_packed_bytes
- *   scales       bf16 [E][k/128][n]
+ *                pairs, per pair and 128-wide k step (one scale group) the
+ *                pair's 8 KB tiles back to back, each [k quarter][row][16 B]
+ *                (kernels/titan_moe_gemm.py pack_weights); 16-byte aligned;
+ *                titan_moe_w4a16_packed_bytes
+ *   scales       bf16 [E][k/128][n], 16-byte aligned
  *   sorted_ids, expert_ids (max_blocks entries), ntpp: one list of
  *                titan_moe_split_align; block_size in {16, 32, 48, 64}
  *   n % 128 == 0, k % 128 == 0.  One persistent launch, no scratch memory.
