@@ -50,6 +50,7 @@ inline EncodeTiledFn tensor_map_encoder() {
 enum DeviceError : int {
   kDevErrNone = 0,
   kDevErrMbarrierTimeout = 1,
+  kDevErrCapacity = 2,  // a count past a fixed-size list; the excess is dropped
 };
 __device__ int g_device_error = 0;
 

@@ -52,9 +52,14 @@ struct Smem {
   uint32_t hist[kHistCopies][kBins];  // copy 0 also serves the multi-pass selection
   uint32_t key[kCandCap];             // candidates, or the selected pairs (first kMaxK)
   int32_t pool[kCandCap];
+  uint32_t slice[kBins / 8];          // cluster form: this CTA's slice of the row's histogram
   uint32_t warp_sum[32];
-  uint32_t bin, above, cnt;
+  uint32_t bin, above, cnt;           // cnt is also the scan's total (block_exclusive_scan)
+  uint32_t ccnt;                      // cluster form: CTA 0's candidate count (nothing else writes it)
 };
+
+constexpr int kClusterMax = 16;       // CTAs per row in the cluster form
+static_assert(kBins / 8 >= kBins / kClusterMax && kBins % kClusterMax == 0, "histogram slices");
 
 // Block-wide exclusive scan of one value per thread (1024 threads).
 __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, Smem &sm, uint32_t &total) {
@@ -249,145 +254,121 @@ __device__ void select_multipass(const float *__restrict__ row, int n, int k, Sm
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    pool_topk_expand_kernel(const float *__restrict__ logits, int64_t ld, const int32_t *__restrict__ seq_lens, int k,
-                            int pool, int32_t *__restrict__ out, int64_t out_stride, int width) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
-  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float *row = logits + (int64_t)t * ld;
-  const int seq_len = __ldg(seq_lens + t);
-  const int64_t n64 = seq_len > 0 ? (int64_t)(seq_len / pool) : 0;
-  const int n = (int)(n64 < ld ? n64 : ld);
-  const int nsel = n < k ? n : k;
+// Histogram of the top 11 bits of the keys of elements [0, n) of `row`
+// (private copies, then summed into sm.hist[0]).
+__device__ __forceinline__ void histogram_top11(const float *__restrict__ row, int n, Smem &sm) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  for (int b = tid; b < kHistCopies * kBins; b += kThreads) (&sm.hist[0][0])[b] = 0;
+  __syncthreads();
+  uint32_t *h = sm.hist[warp >> 2];
+  visit_row(row, n, [&](int, float4 v, int nv) {
+    if (nv > 0) atomicAdd(&h[float_key(v.x) >> 21], 1u);
+    if (nv > 1) atomicAdd(&h[float_key(v.y) >> 21], 1u);
+    if (nv > 2) atomicAdd(&h[float_key(v.z) >> 21], 1u);
+    if (nv > 3) atomicAdd(&h[float_key(v.w) >> 21], 1u);
+  });
+  __syncthreads();
+  for (int b = tid; b < kBins; b += kThreads) {
+    uint32_t sum = 0;
+#pragma unroll
+    for (int c = 0; c < kHistCopies; ++c) sum += sm.hist[c][b];
+    sm.hist[0][b] = sum;
+  }
+  __syncthreads();
+}
 
-  if (n <= k) {
-    // Every valid pool is selected.
-    for (int i = tid; i < n; i += kThreads) {
-      sm.key[i] = float_key(__ldg(row + i));
-      sm.pool[i] = i;
-    }
-  } else {
-    // ---- fast path, pass 1: histograms of the keys' top 11 bits
-    for (int b = tid; b < kHistCopies * kBins; b += kThreads) (&sm.hist[0][0])[b] = 0;
-    __syncthreads();
-    uint32_t *h = sm.hist[warp >> 2];
-    visit_row(row, n, [&](int, float4 v, int nv) {
-      if (nv > 0) atomicAdd(&h[float_key(v.x) >> 21], 1u);
-      if (nv > 1) atomicAdd(&h[float_key(v.y) >> 21], 1u);
-      if (nv > 2) atomicAdd(&h[float_key(v.z) >> 21], 1u);
-      if (nv > 3) atomicAdd(&h[float_key(v.w) >> 21], 1u);
-    });
-    __syncthreads();
-    for (int b = tid; b < kBins; b += kThreads) {
-      uint32_t sum = 0;
+// Appends every element of [0, n) of `row` whose key's top 11 bits are >=
+// thr to a candidate list: push(key, row index) per kept element, called
+// by the lanes of a warp together with the base of the warp's block of
+// slots reserved through reserve(count) by lane 0.
+template <typename Reserve, typename Put>
+__device__ __forceinline__ void collect_candidates(const float *__restrict__ row, int n, uint32_t thr,
+                                                   Reserve &&reserve, Put &&put) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  visit_row(row, n, [&](int i, float4 v, int nv) {
+    const uint32_t kk[4] = {float_key(v.x), float_key(v.y), float_key(v.z), float_key(v.w)};
+    bool any = false;
 #pragma unroll
-      for (int c = 0; c < kHistCopies; ++c) sum += sm.hist[c][b];
-      sm.hist[0][b] = sum;
-    }
-    __syncthreads();
-    find_bin(sm.hist[0], kBins, (uint32_t)k, sm);
-    const uint32_t thr = sm.bin;
-    const uint32_t cand = sm.above + sm.hist[0][thr];  // keys in the bin or above it
-    if (cand <= (uint32_t)kCandCap) {
-      // ---- pass 2: every key of the threshold bin or above joins the list
-      if (tid == 0) sm.cnt = 0;
-      __syncthreads();
-      const uint32_t lt = (1u << lane) - 1u;
-      visit_row(row, n, [&](int i, float4 v, int nv) {
-        const uint32_t kk[4] = {float_key(v.x), float_key(v.y), float_key(v.z), float_key(v.w)};
-        bool any = false;
+    for (int q = 0; q < 4; ++q) any |= q < nv && (kk[q] >> 21) >= thr;
+    if (__ballot_sync(0xffffffffu, any) == 0) return;  // the common case: nothing to keep
 #pragma unroll
-        for (int q = 0; q < 4; ++q) any |= q < nv && (kk[q] >> 21) >= thr;
-        if (__ballot_sync(0xffffffffu, any) == 0) return;  // the common case: nothing to keep
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const bool take = q < nv && (kk[q] >> 21) >= thr;
-          const uint32_t m = __ballot_sync(0xffffffffu, take);
-          if (m) {
-            uint32_t base = 0;
-            if (lane == 0) base = atomicAdd(&sm.cnt, (uint32_t)__popc(m));
-            base = __shfl_sync(0xffffffffu, base, 0);
-            if (take) {
-              const uint32_t pos = base + (uint32_t)__popc(m & lt);
-              sm.key[pos] = kk[q];
-              sm.pool[pos] = i + q;
-            }
-          }
-        }
-      });
-      __syncthreads();
-      const int c = (int)sm.cnt;
-      // ---- refine within the threshold bin on the candidates (two radix
-      // passes over at most kCandCap keys in shared memory): the exact k-th
-      // key T and how many keys equal to T to take.
-      uint32_t *h0 = sm.hist[0];
-      uint32_t prefix = thr << 21, mask = 0xFFE00000u;
-      uint32_t remaining = (uint32_t)k - sm.above;
-      uint32_t ties = 0;
-#pragma unroll 1
-      for (int ps = 0; ps < 2; ++ps) {
-        const int sh = ps == 0 ? 10 : 0, nb = ps == 0 ? 2048 : 1024;
-        for (int b = tid; b < nb; b += kThreads) h0[b] = 0;
-        __syncthreads();
-        for (int i = tid; i < c; i += kThreads) {
-          const uint32_t key = sm.key[i];
-          if ((key & mask) == prefix) atomicAdd(&h0[(key >> sh) & (uint32_t)(nb - 1)], 1u);
-        }
-        __syncthreads();
-        find_bin(h0, nb, remaining, sm);
-        remaining -= sm.above;
-        prefix |= sm.bin << sh;
-        mask |= (uint32_t)(nb - 1) << sh;
-        if (ps == 1) ties = h0[sm.bin];  // candidates equal to T
-        __syncthreads();
+    for (int q = 0; q < 4; ++q) {
+      const bool take = q < nv && (kk[q] >> 21) >= thr;
+      const uint32_t m = __ballot_sync(0xffffffffu, take);
+      if (m) {
+        uint32_t base = 0;
+        if (lane == 0) base = reserve((uint32_t)__popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (take) put(base + (uint32_t)__popc(m & lt), kk[q], i + q);
       }
-      const uint32_t T = prefix;
-      const int sel = k - (int)remaining + (int)ties;  // keys above T, and every key equal to T
-      if (sel <= kMaxK) {
-        // ---- keep the keys >= T (at most kMaxK), sort them; the first k
-        // (ties by smaller pool) are the selection.
-        constexpr int kPer = kCandCap / kThreads;  // candidates per thread
-        uint32_t kept_key[kPer];
-        int32_t kept_pool[kPer];
-        bool keep[kPer];
-        uint32_t nk = 0;
+    }
+  });
+}
+
+// From c candidates in sm.key / sm.pool (every key whose top 11 bits are >=
+// thr; `above` of them in higher bins), the k selected pairs in their final
+// order in sm.key / sm.pool [0, k): one radix pass over the candidates (the
+// next 11 bits) finds the bin B of the k-th key; every candidate in B or
+// above it (k plus the few others that share B) is kept and sorted.  With
+// more than kMaxK of them (ties), the multi-pass selection over the row.
+__device__ void select_from_candidates(Smem &sm, int c, uint32_t thr, uint32_t above, int k,
+                                       const float *__restrict__ row, int n) {
+  const int tid = threadIdx.x;
+  uint32_t *h0 = sm.hist[0];
+  __syncthreads();  // the candidates are complete; the histogram space is free
+  for (int b = tid; b < kBins; b += kThreads) h0[b] = 0;
+  __syncthreads();
+  for (int i = tid; i < c; i += kThreads) {
+    const uint32_t key = sm.key[i];
+    if ((key >> 21) == thr) atomicAdd(&h0[(key >> 10) & (uint32_t)(kBins - 1)], 1u);
+  }
+  __syncthreads();
+  find_bin(h0, kBins, (uint32_t)k - above, sm);
+  // Keys >= T are the candidates of bin (thr, sm.bin) or above it.
+  const uint32_t T = (thr << 21) | (sm.bin << 10);
+  const int sel = (int)(above + sm.above + h0[sm.bin]);
+  __syncthreads();
+  if (sel > kMaxK) {
+    select_multipass(row, n, k, sm);
+    sort_pairs(sm, k);
+    return;
+  }
+  constexpr int kPer = kCandCap / kThreads;  // candidates per thread
+  uint32_t kept_key[kPer];
+  int32_t kept_pool[kPer];
+  bool keep[kPer];
+  uint32_t nk = 0;
 #pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-          const int i = tid + q * kThreads;
-          keep[q] = i < c && sm.key[i] >= T;
-          kept_key[q] = keep[q] ? sm.key[i] : 0u;
-          kept_pool[q] = keep[q] ? sm.pool[i] : 0;
-          nk += keep[q] ? 1u : 0u;
-        }
-        if (tid == 0) sm.cnt = 0;
-        __syncthreads();  // every candidate has been read before the list is rewritten
-        uint32_t pos = nk ? atomicAdd(&sm.cnt, nk) : 0u;
+  for (int q = 0; q < kPer; ++q) {
+    const int i = tid + q * kThreads;
+    keep[q] = i < c && sm.key[i] >= T;
+    kept_key[q] = keep[q] ? sm.key[i] : 0u;
+    kept_pool[q] = keep[q] ? sm.pool[i] : 0;
+    nk += keep[q] ? 1u : 0u;
+  }
+  if (tid == 0) sm.cnt = 0;
+  __syncthreads();  // every candidate has been read before the list is rewritten
+  uint32_t pos = nk ? atomicAdd(&sm.cnt, nk) : 0u;
 #pragma unroll
-        for (int q = 0; q < kPer; ++q) {
-          if (keep[q]) {
-            sm.key[pos] = kept_key[q];
-            sm.pool[pos] = kept_pool[q];
-            ++pos;
-          }
-        }
-        sort_pairs(sm, sel);
-      } else {
-        select_multipass(row, n, k, sm);
-        sort_pairs(sm, nsel);
-      }
-    } else {
-      select_multipass(row, n, k, sm);
-      sort_pairs(sm, nsel);
+  for (int q = 0; q < kPer; ++q) {
+    if (keep[q]) {
+      sm.key[pos] = kept_key[q];
+      sm.pool[pos] = kept_pool[q];
+      ++pos;
     }
   }
-  if (n <= k) sort_pairs(sm, nsel);
-  // Expansion into the index row.
-  int32_t *orow = out + (int64_t)t * out_stride;
+  sort_pairs(sm, sel);  // the first k (ties by smaller pool) are the selection
+}
+
+// The index row: pools sm.pool[0, nsel) expanded to their tokens, the tail
+// of the partial last pool, -1 up to `width`.
+__device__ __forceinline__ void expand_into(const Smem &sm, int nsel, int k, int pool, int seq_len,
+                                            int32_t *__restrict__ orow, int width) {
   const int span = k * pool;
   const int tail_start = (seq_len > 0 ? seq_len / pool : 0) * pool;
   const int tail_len = seq_len > 0 ? seq_len % pool : 0;
-  for (int j = tid; j < width; j += kThreads) {
+  for (int j = threadIdx.x; j < width; j += kThreads) {
     int v = -1;
     if (j < span) {
       const int i = j / pool, o = j - (j / pool) * pool;
@@ -400,10 +381,182 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Every valid pool selected (n <= k): load and sort them.
+__device__ __forceinline__ void select_all(const float *__restrict__ row, int n, Smem &sm) {
+  for (int i = threadIdx.x; i < n; i += kThreads) {
+    sm.key[i] = float_key(__ldg(row + i));
+    sm.pool[i] = i;
+  }
+  sort_pairs(sm, n);
+}
+
+// One CTA per query row (many rows).
+__global__ void __launch_bounds__(kThreads, 1)
+    pool_topk_expand_kernel(const float *__restrict__ logits, int64_t ld, const int32_t *__restrict__ seq_lens, int k,
+                            int pool, int32_t *__restrict__ out, int64_t out_stride, int width) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const float *row = logits + (int64_t)t * ld;
+  const int seq_len = __ldg(seq_lens + t);
+  const int64_t n64 = seq_len > 0 ? (int64_t)(seq_len / pool) : 0;
+  const int n = (int)(n64 < ld ? n64 : ld);
+  const int nsel = n < k ? n : k;
+
+  if (n <= k) {
+    select_all(row, n, sm);
+  } else {
+    histogram_top11(row, n, sm);
+    find_bin(sm.hist[0], kBins, (uint32_t)k, sm);
+    const uint32_t thr = sm.bin, above = sm.above;
+    const uint32_t cand = above + sm.hist[0][thr];  // keys in the bin or above it
+    if (cand <= (uint32_t)kCandCap) {
+      if (tid == 0) sm.cnt = 0;
+      __syncthreads();
+      collect_candidates(
+          row, n, thr, [&](uint32_t cnt) { return atomicAdd(&sm.cnt, cnt); },
+          [&](uint32_t pos, uint32_t key, int i) {
+            if (pos < (uint32_t)kCandCap) {  // pos < cand <= kCandCap by construction
+              sm.key[pos] = key;
+              sm.pool[pos] = i;
+            } else {
+              atomicCAS(&g_device_error, 0, kDevErrCapacity);
+            }
+          });
+      __syncthreads();
+      select_from_candidates(sm, (int)min(sm.cnt, (uint32_t)kCandCap), thr, above, k, row, n);
+    } else {
+      select_multipass(row, n, k, sm);
+      sort_pairs(sm, nsel);
+    }
+  }
+  expand_into(sm, nsel, k, pool, seq_len, out + (int64_t)t * out_stride, width);
+}
+
+// Distributed shared memory of the cluster form.
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_cluster_u32(uint32_t addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t v;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(v));
+  return v;
+}
+
+// Cluster form (few rows): the C CTAs of a cluster share one row.  CTA r
+// histograms its contiguous share of the pools; each CTA then sums one
+// slice of the bins over the cluster's histograms and every CTA reads the
+// summed slices back, so all find the same threshold bin; the CTAs append
+// their candidates straight into CTA 0's shared memory (one remote atomic
+// per warp and keep), and CTA 0 refines, sorts and expands.  The cluster
+// barriers are reached by every thread of every CTA on uniform control flow
+// (the row and its sizes are uniform across the cluster).
+__global__ void __launch_bounds__(kThreads, 1)
+    pool_topk_cluster_kernel(const float *__restrict__ logits, int64_t ld, const int32_t *__restrict__ seq_lens,
+                             int k, int pool, int32_t *__restrict__ out, int64_t out_stride, int width) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  const int C = (int)cluster_size(), r = (int)cluster_ctarank();
+  const int t = blockIdx.x / C, tid = threadIdx.x;
+  const float *row = logits + (int64_t)t * ld;
+  const int seq_len = __ldg(seq_lens + t);
+  const int64_t n64 = seq_len > 0 ? (int64_t)(seq_len / pool) : 0;
+  const int n = (int)(n64 < ld ? n64 : ld);
+  const int nsel = n < k ? n : k;
+  int32_t *orow = out + (int64_t)t * out_stride;
+
+  if (n <= k) {  // uniform across the cluster: CTA 0 alone
+    if (r == 0) {
+      select_all(row, n, sm);
+      expand_into(sm, nsel, k, pool, seq_len, orow, width);
+    }
+    return;
+  }
+  // This CTA's share of the pools: [lo, hi), lo a multiple of 4 (16-byte
+  // loads stay aligned when the row is).
+  const int per = ((n + C - 1) / C + 3) & ~3;
+  const int lo = min(n, r * per), hi = min(n, lo + per);
+  histogram_top11(row + lo, hi - lo, sm);
+  if (tid == 0) sm.ccnt = 0;  // CTA 0's candidate counter (every CTA clears its own)
+  cluster_sync_all();         // every CTA's histogram (sm.hist[0]) is complete
+  // Slice sums: CTA r owns bins [r S, r S + S).  C consecutive lanes (C
+  // divides 32) load one bin from the C CTAs at once and add by shuffles.
+  const int S = kBins / C;
+  for (int b0 = 0; b0 < S; b0 += kThreads / C) {
+    const int b = b0 + tid / C, q = tid % C;
+    uint32_t v = 0;
+    if (b < S) {
+      uint32_t a;
+      asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(&sm.hist[0][r * S + b])), "r"(q));
+      v = ld_cluster_u32(a);
+    }
+    for (int o = C >> 1; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o, C);
+    if (q == 0 && b < S) sm.slice[b] = v;
+  }
+  cluster_sync_all();  // every slice is summed
+  // The row's histogram, read back from the slices into sm.hist[1].
+  for (int b = tid; b < kBins; b += kThreads) {
+    uint32_t a;
+    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(&sm.slice[b % S])), "r"(b / S));
+    sm.hist[1][b] = ld_cluster_u32(a);
+  }
+  __syncthreads();
+  find_bin(sm.hist[1], kBins, (uint32_t)k, sm);
+  const uint32_t thr = sm.bin, above = sm.above;
+  const uint32_t cand = above + sm.hist[1][thr];
+  const bool fast = cand <= (uint32_t)kCandCap;  // uniform across the cluster
+  if (fast) {
+    const uint32_t cnt0 = [&] {
+      uint32_t a;
+      asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(&sm.ccnt)), "r"(0));
+      return a;
+    }();
+    uint32_t key0, pool0;
+    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(key0) : "r"(smem_u32(&sm.key[0])), "r"(0));
+    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(pool0) : "r"(smem_u32(&sm.pool[0])), "r"(0));
+    collect_candidates(
+        row + lo, hi - lo, thr, [&](uint32_t c) { return atom_add_cluster_u32(cnt0, c); },
+        [&](uint32_t pos, uint32_t key, int i) {
+          // pos < cand <= kCandCap by construction; checked, not trusted
+          if (pos < (uint32_t)kCandCap) {
+            st_cluster_u32(key0 + 4 * pos, key);
+            st_cluster_u32(pool0 + 4 * pos, (uint32_t)(lo + i));
+          } else {
+            atomicCAS(&g_device_error, 0, kDevErrCapacity);
+          }
+        });
+  }
+  // The candidates have reached CTA 0, and no CTA reads a peer's slice any
+  // more: the others may exit.
+  cluster_sync_all();
+  if (r != 0) return;
+  if (fast) {
+    select_from_candidates(sm, (int)min(sm.ccnt, (uint32_t)kCandCap), thr, above, k, row, n);
+  } else {
+    select_multipass(row, n, k, sm);
+    sort_pairs(sm, nsel);
+  }
+  expand_into(sm, nsel, k, pool, seq_len, orow, width);
+}
+
 }  // namespace idx
 
 namespace {
 std::atomic<int> g_topk_ready[64];
+std::atomic<int> g_topk_clusters[64][2];  // clusters of 16 / 8 CTAs the device runs at once
 }  // namespace
 }  // namespace titan
 
@@ -426,13 +579,64 @@ extern "C" int titan_pool_topk_expand(const float *logits, int64_t ld, const int
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "pool_topk_expand: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail(TITAN_ERR_CUDA, "pool_topk_expand: device ordinal %d out of range", dev);
+  // One-time set-up per device: shared-memory opt-in for both kernels,
+  // 16-CTA clusters allowed, and how many clusters of each size fit.
   if (!g_topk_ready[dev].load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lock(setup_mutex());
     if (!g_topk_ready[dev].load(std::memory_order_relaxed)) {
       e = cudaFuncSetAttribute(idx::pool_topk_expand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(idx::pool_topk_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(idx::pool_topk_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "pool_topk_expand: setup: %s", cudaGetErrorString(e));
+      // How many clusters of 16 and of 8 CTAs the device runs at once.
+      for (int ci = 0; ci < 2; ++ci) {
+        const int csize = ci == 0 ? idx::kClusterMax : 8;
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3((unsigned)csize);
+        q.blockDim = dim3(idx::kThreads);
+        q.dynamicSmemBytes = smem;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = (unsigned)csize;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        int nclusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&nclusters, idx::pool_topk_cluster_kernel, &q) != cudaSuccess) {
+          cudaGetLastError();
+          nclusters = 0;
+        }
+        g_topk_clusters[dev][ci].store(nclusters, std::memory_order_relaxed);
+      }
       g_topk_ready[dev].store(1, std::memory_order_release);
     }
+  }
+  const int n16 = g_topk_clusters[dev][0].load(std::memory_order_relaxed);
+  const int n8 = g_topk_clusters[dev][1].load(std::memory_order_relaxed);
+  // Few rows: a cluster per row (16 CTAs when the rows' clusters all run at
+  // once, else 8), so a decode step's rows spread over the SMs; many rows:
+  // one CTA per row.
+  const int cluster = num_rows <= n16 ? idx::kClusterMax : (num_rows <= n8 ? 8 : 0);
+  if (cluster > 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(num_rows * cluster));
+    cfg.blockDim = dim3(idx::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, idx::pool_topk_cluster_kernel, logits, ld, seq_lens, k, pool_size, out, out_stride,
+                           width);
+    if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "pool_topk_expand launch: %s", cudaGetErrorString(e));
+    return check_launch("pool_topk_expand launch");
   }
   idx::pool_topk_expand_kernel<<<(unsigned)num_rows, idx::kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       logits, ld, seq_lens, k, pool_size, out, out_stride, width);

@@ -37,13 +37,26 @@ def test_prefill_rows_all_lengths(native_lib, cuda_device):
     _check(logits, torch.tensor(lens, dtype=torch.int32), 512, 4, 2176, cuda_device)
 
 
+# Up to 9 rows take the cluster form (a cluster of 8-16 CTAs per row on a
+# 148-SM B200), 40 rows the one-CTA-per-row form.
+@pytest.mark.parametrize("rows", [5, 40])
 @pytest.mark.parametrize("levels", [3, 40])
-def test_heavy_ties(native_lib, cuda_device, levels):
+def test_heavy_ties(native_lib, cuda_device, levels, rows):
     """Logits on a few levels: the k-th largest value is shared by many pools,
-    taken in pool order."""
+    taken in pool order (3 levels: more than 4096 candidates, the multi-pass
+    selection; 40 levels: the candidate path with ~500 ties)."""
     g = torch.Generator().manual_seed(levels)
-    logits = torch.randint(0, levels, (5, 20000), generator=g).float()
-    _check(logits, torch.full((5,), 80000, dtype=torch.int32), 512, 4, 2176, cuda_device)
+    logits = torch.randint(0, levels, (rows, 20000), generator=g).float()
+    _check(logits, torch.full((rows,), 80000, dtype=torch.int32), 512, 4, 2176, cuda_device)
+
+
+def test_decode_shape_one_cta_per_row(native_lib, cuda_device):
+    """The decode shape with enough rows for the one-CTA-per-row form."""
+    g = torch.Generator().manual_seed(6)
+    logits = torch.randn(24, 65536, generator=g)
+    seq_lens = torch.randint(262000, 262145, (24,), generator=g, dtype=torch.int32)
+    seq_lens[3] = 5
+    _check(logits, seq_lens, 512, 4, 2176, cuda_device)
 
 
 def test_nan_inf_and_small_k(native_lib, cuda_device):
@@ -54,8 +67,11 @@ def test_nan_inf_and_small_k(native_lib, cuda_device):
     logits[2, ::7] = float("-inf")
     logits[3, 100:4000] = 0.0
     logits[3, 5] = -0.0
+    seq = torch.tensor([20000, 19999, 18000, 20003], dtype=torch.int32)
     for k, pool, width in ((512, 4, 2176), (1, 4, 8), (37, 1, 40), (1024, 2, 2049), (300, 16, 4815)):
-        _check(logits, torch.tensor([20000, 19999, 18000, 20003], dtype=torch.int32), k, pool, width, cuda_device)
+        _check(logits, seq, k, pool, width, cuda_device)
+    # the same rows repeated (40 rows: the one-CTA-per-row form)
+    _check(logits.repeat(10, 1), seq.repeat(10), 512, 4, 2176, cuda_device)
 
 
 def test_strided_rows_and_empty(native_lib, cuda_device):
