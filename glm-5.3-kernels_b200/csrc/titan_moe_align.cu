@@ -37,21 +37,28 @@ __global__ void __launch_bounds__(128) moe_align_small_kernel(const IdT *__restr
   // The whole layout is built by warp 0: no CTA-wide barrier sits on the
   // critical path, which starts with the route-id loads.  Extra warps (the
   // caller's num_warps) have nothing to do.
+  // Launched as a programmatic dependent: the next kernel on the stream may
+  // launch at once (it waits for this grid before reading its outputs), and
+  // this one waits for the previous grid (the router writing the ids, or the
+  // previous call writing the same outputs) only before its first global
+  // access, after the shared-memory set-up.
+  pdl_launch_dependents();
   if (threadIdx.x >= 32) return;
   __shared__ __align__(16) int s_sorted[kMoeMaxRoutes * 8];
   __shared__ __align__(16) int s_experts[kMoeMaxRoutes];
   const int lane = threadIdx.x;
 
+  // Initialise: padding = R, unused blocks = -1.
+  const int4 pad4 = make_int4(R, R, R, R);
+  for (int i = lane; i < 2 * R; i += 32) reinterpret_cast<int4 *>(s_sorted)[i] = pad4;  // 8R ints
+  for (int i = lane; i < R; i += 32) s_experts[i] = -1;
+
+  pdl_wait_primary();
   // Route lane (half 0) and lane + 32 (half 1).  Validity is decided on the
   // full-width id, before narrowing (an int64 id of 2^32 + 5 is invalid).
   long long raw0 = -1, raw1 = -1;
   if (lane < R) raw0 = (long long)ids[lane];
   if (kTwoHalves && lane + 32 < R) raw1 = (long long)ids[lane + 32];
-
-  // Initialise while the loads are in flight: padding = R, unused blocks = -1.
-  const int4 pad4 = make_int4(R, R, R, R);
-  for (int i = lane; i < 2 * R; i += 32) reinterpret_cast<int4 *>(s_sorted)[i] = pad4;  // 8R ints
-  for (int i = lane; i < R; i += 32) s_experts[i] = -1;
 
   // Invalid routes (and lanes past R) get expert -1: they match no valid
   // route, lead nothing and never scatter.
@@ -125,27 +132,37 @@ extern "C" int titan_moe_align_small(const void *topk_ids, int ids_is_int64, int
     return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_align_small: num_warps must be 1, 2 or 4");
   if (topk_ids == nullptr || sorted_ids == nullptr || expert_ids == nullptr || postpad == nullptr)
     return fail(TITAN_ERR_INVALID_ARGUMENT, "moe_align_small: null pointer");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int R = (int)num_routes;
   const bool vec_out = (uintptr_t)sorted_ids % 16 == 0 && (uintptr_t)expert_ids % 16 == 0;
-  const dim3 grid(1), block(32 * num_warps);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32 * num_warps);
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaSuccess;
   // One instantiation per route count (R = 8 B): the route walks unroll.
   auto launch = [&](auto ids) {
     using IdT = std::remove_const_t<std::remove_pointer_t<decltype(ids)>>;
+    auto go = [&](auto kernel) { e = cudaLaunchKernelEx(&cfg, kernel, ids, sorted_ids, expert_ids, postpad, vec_out); };
     switch (R) {
-      case 8: moe_align_small_kernel<IdT, 8><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
-      case 16: moe_align_small_kernel<IdT, 16><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
-      case 24: moe_align_small_kernel<IdT, 24><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
-      case 32: moe_align_small_kernel<IdT, 32><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
-      case 40: moe_align_small_kernel<IdT, 40><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
-      case 48: moe_align_small_kernel<IdT, 48><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
-      case 56: moe_align_small_kernel<IdT, 56><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
-      default: moe_align_small_kernel<IdT, 64><<<grid, block, 0, s>>>(ids, sorted_ids, expert_ids, postpad, vec_out); break;
+      case 8: go(moe_align_small_kernel<IdT, 8>); break;
+      case 16: go(moe_align_small_kernel<IdT, 16>); break;
+      case 24: go(moe_align_small_kernel<IdT, 24>); break;
+      case 32: go(moe_align_small_kernel<IdT, 32>); break;
+      case 40: go(moe_align_small_kernel<IdT, 40>); break;
+      case 48: go(moe_align_small_kernel<IdT, 48>); break;
+      case 56: go(moe_align_small_kernel<IdT, 56>); break;
+      default: go(moe_align_small_kernel<IdT, 64>); break;
     }
   };
   if (ids_is_int64)
     launch(static_cast<const long long *>(topk_ids));
   else
     launch(static_cast<const int32_t *>(topk_ids));
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "moe_align_small launch: %s", cudaGetErrorString(e));
   return check_launch("moe_align_small launch");
 }
