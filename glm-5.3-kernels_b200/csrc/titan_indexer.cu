@@ -397,6 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
   const int t = blockIdx.x, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait_primary();  // the logits and lengths come from earlier kernels
   const float *row = logits + (int64_t)t * ld;
   const int seq_len = __ldg(seq_lens + t);
   const int64_t n64 = seq_len > 0 ? (int64_t)(seq_len / pool) : 0;
@@ -471,6 +473,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
   const int C = (int)cluster_size(), r = (int)cluster_ctarank();
   const int t = blockIdx.x / C, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait_primary();  // the logits and lengths come from earlier kernels
   const float *row = logits + (int64_t)t * ld;
   const int seq_len = __ldg(seq_lens + t);
   const int64_t n64 = seq_len > 0 ? (int64_t)(seq_len / pool) : 0;
@@ -626,19 +630,22 @@ extern "C" int titan_pool_topk_expand(const float *logits, int64_t ld, const int
     cfg.blockDim = dim3(idx::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)cluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, idx::pool_topk_cluster_kernel, logits, ld, seq_lens, k, pool_size, out, out_stride,
                            width);
     if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "pool_topk_expand launch: %s", cudaGetErrorString(e));
     return check_launch("pool_topk_expand launch");
   }
-  idx::pool_topk_expand_kernel<<<(unsigned)num_rows, idx::kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      logits, ld, seq_lens, k, pool_size, out, out_stride, width);
+  e = launch_pdl(idx::pool_topk_expand_kernel, dim3((unsigned)num_rows), dim3(idx::kThreads), smem,
+                 reinterpret_cast<cudaStream_t>(stream), logits, ld, seq_lens, k, pool_size, out, out_stride, width);
+  if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "pool_topk_expand launch: %s", cudaGetErrorString(e));
   return check_launch("pool_topk_expand launch");
 }

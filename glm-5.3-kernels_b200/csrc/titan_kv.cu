@@ -118,8 +118,10 @@ __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
     store_int8_vec_kernel(const __nv_bfloat16 *__restrict__ x, int64_t x_row_stride, int8_t *__restrict__ cache,
                           int64_t num_blocks, int64_t block, int block_shift, int64_t cs0, int64_t cs1,
                           const SlotT *__restrict__ slots, int64_t n) {
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row0 = ((int64_t)blockIdx.x * kKvWarpsPerCta + (threadIdx.x >> 5)) * kKvRowsPerWarp;
+  pdl_wait_primary();  // the latents and slots come from earlier kernels
   int64_t slot[kKvRowsPerWarp];
   uint4 a[kKvRowsPerWarp], b[kKvRowsPerWarp];
 #pragma unroll
@@ -252,6 +254,8 @@ __global__ void __launch_bounds__(kKvStreamWarps * 32, 3)
   const int64_t nwarps = (int64_t)gridDim.x * kKvStreamWarps;
   const int64_t pairs = (n + 1) / 2;
   const int64_t my_steps = gwarp < pairs ? (pairs - 1 - gwarp) / nwarps + 1 : 0;
+  pdl_launch_dependents();
+  pdl_wait_primary();  // the latents and slots come from earlier kernels
   // Step i of this warp covers rows 2 (gwarp + i nwarps) + {0, 1}.
   auto row_of = [&](int64_t i) { return 2 * (gwarp + i * nwarps) + half; };
   auto fetch = [&](int64_t i) {  // this lane's 4 chunks of its row of step i
@@ -332,9 +336,11 @@ __global__ void __launch_bounds__(kKvWarpsPerCta * 32)
     store_int8_scalar_kernel(const __nv_bfloat16 *__restrict__ x, int64_t x_row_stride, int8_t *__restrict__ cache,
                              int64_t num_blocks, int64_t block, int block_shift, int64_t cs0, int64_t cs1,
                              const SlotT *__restrict__ slots, int64_t n) {
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kKvWarpsPerCta + (threadIdx.x >> 5);
   if (row >= n) return;
+  pdl_wait_primary();  // the latents and slots come from earlier kernels
   const int64_t slot = (int64_t)slots[row];
   if (slot < 0) return;
   int64_t blk, off;
@@ -424,34 +430,33 @@ extern "C" int titan_store_int8(const void *x, int64_t x_row_stride, void *cache
     const __nv_bfloat16 *xb = static_cast<const __nv_bfloat16 *>(x);
     int8_t *cb = static_cast<int8_t *>(cache);
     if (slots_is_int64)
-      store_int8_stream_kernel<int64_t><<<grid_s, kKvStreamWarps * 32, kKvStreamSmem, s>>>(
-          xb, x_row_stride, cb, num_blocks, block_size, block_shift, cache_stride0, cache_stride1,
-          static_cast<const int64_t *>(slots), n_slots);
+      e = launch_pdl(store_int8_stream_kernel<int64_t>, dim3(grid_s), dim3(kKvStreamWarps * 32), kKvStreamSmem, s, xb,
+                     x_row_stride, cb, num_blocks, block_size, block_shift, cache_stride0, cache_stride1,
+                     static_cast<const int64_t *>(slots), n_slots);
     else
-      store_int8_stream_kernel<int32_t><<<grid_s, kKvStreamWarps * 32, kKvStreamSmem, s>>>(
-          xb, x_row_stride, cb, num_blocks, block_size, block_shift, cache_stride0, cache_stride1,
-          static_cast<const int32_t *>(slots), n_slots);
+      e = launch_pdl(store_int8_stream_kernel<int32_t>, dim3(grid_s), dim3(kKvStreamWarps * 32), kKvStreamSmem, s, xb,
+                     x_row_stride, cb, num_blocks, block_size, block_shift, cache_stride0, cache_stride1,
+                     static_cast<const int32_t *>(slots), n_slots);
+    if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "store_int8 (stream) launch: %s", cudaGetErrorString(e));
     return check_launch("store_int8 (stream) launch");
   }
   const dim3 grid((unsigned)ctas), block(kKvWarpsPerCta * 32);
   const __nv_bfloat16 *xb = static_cast<const __nv_bfloat16 *>(x);
   int8_t *cb = static_cast<int8_t *>(cache);
+  cudaError_t le;
   if (slots_is_int64) {
     const int64_t *sl = static_cast<const int64_t *>(slots);
-    if (aligned)
-      store_int8_vec_kernel<int64_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                            block_shift, cache_stride0, cache_stride1, sl, n_slots);
-    else
-      store_int8_scalar_kernel<int64_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                               block_shift, cache_stride0, cache_stride1, sl, n_slots);
+    le = aligned ? launch_pdl(store_int8_vec_kernel<int64_t>, grid, block, 0, s, xb, x_row_stride, cb, num_blocks,
+                              block_size, block_shift, cache_stride0, cache_stride1, sl, n_slots)
+                 : launch_pdl(store_int8_scalar_kernel<int64_t>, grid, block, 0, s, xb, x_row_stride, cb, num_blocks,
+                              block_size, block_shift, cache_stride0, cache_stride1, sl, n_slots);
   } else {
     const int32_t *sl = static_cast<const int32_t *>(slots);
-    if (aligned)
-      store_int8_vec_kernel<int32_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                            block_shift, cache_stride0, cache_stride1, sl, n_slots);
-    else
-      store_int8_scalar_kernel<int32_t><<<grid, block, 0, s>>>(xb, x_row_stride, cb, num_blocks, block_size,
-                                                               block_shift, cache_stride0, cache_stride1, sl, n_slots);
+    le = aligned ? launch_pdl(store_int8_vec_kernel<int32_t>, grid, block, 0, s, xb, x_row_stride, cb, num_blocks,
+                              block_size, block_shift, cache_stride0, cache_stride1, sl, n_slots)
+                 : launch_pdl(store_int8_scalar_kernel<int32_t>, grid, block, 0, s, xb, x_row_stride, cb, num_blocks,
+                              block_size, block_shift, cache_stride0, cache_stride1, sl, n_slots);
   }
+  if (le != cudaSuccess) return fail(TITAN_ERR_CUDA, "store_int8 launch: %s", cudaGetErrorString(le));
   return check_launch("store_int8 launch");
 }

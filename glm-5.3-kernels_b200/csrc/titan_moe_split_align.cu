@@ -132,7 +132,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   const int gwarp = cta * kSplitWarps + warp, nwarps = ncta * kSplitWarps;
   const unsigned lower = (1u << lane) - 1u;
   const int nbits = E > 1 ? 32 - __clz(E - 1) : 0;
+  pdl_launch_dependents();
   for (int i = tid; i < kSplitWarps * hs; i += kSplitThreads) hist[i] = 0;
+  pdl_wait_primary();  // the route ids come from earlier kernels; the lists are rewritten below
   __syncthreads();
 
   // Pass 1: per-slice expert counts.
@@ -377,13 +379,15 @@ extern "C" int titan_moe_split_align(const void *topk_ids, int ids_is_int64, int
   cfg.blockDim = dim3(kSplitThreads);
   cfg.dynamicSmemBytes = (size_t)titan_moe_split_align_smem_bytes(num_experts);
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)cluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const int T = (int)num_routes, E = (int)num_experts;
   if (ids_is_int64)
     e = cudaLaunchKernelEx(&cfg, moe_split_align_kernel<long long>, static_cast<const long long *>(topk_ids), T, E,
