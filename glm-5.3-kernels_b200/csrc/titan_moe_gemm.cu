@@ -14,15 +14,18 @@
 // sums in fp32, C in bf16.  The dequantised weight is rounded to bf16 before
 // the MMA, as Marlin's W4A16 dequantisation does.
 //
-// B200 design, one persistent CTA of 14 warps per SM, work item = (block b,
+// B200 design, one persistent CTA of 15 warps per SM, work item = (block b,
 // 256 output features: two MMA tiles of M = 128 sharing the activation
 // tile), pipeline step = 128 k (one scale group):
-//  * warp 0 (producer): lane 0 bulk-copies the step's packed int4 weights
-//    (16 KB for the tile pair) and group scales; the lanes gather the
-//    block's activation rows with TMA tile::gather4 (four 128-byte rows per
-//    load, two 64-k halves) straight into 128B-swizzled K-major tiles,
-//    padding rows as out-of-map rows that read as zeros; everything lands on
-//    one mbarrier per stage, six stages;
+//  * warps 0 and 14 (producers): they gather the block's activation rows
+//    with TMA tile::gather4 (four 128-byte rows per load, two 64-k halves)
+//    straight into 128B-swizzled K-major tiles, padding rows as out-of-map
+//    rows that read as zeros; the gathers of a step are split between the
+//    two warps, because lanes of one warp issue them one after another
+//    (one warp: 2360 us at the bench shape, two: 1948, four: 2048, six:
+//    2096).  Warp 0's lane 0 also bulk-copies the step's packed int4
+//    weights (16 KB for the tile pair) and group scales.  Everything lands
+//    on one mbarrier per stage, six stages;
 //  * warps 2..9 (dequantisation): thread = feature row of one tile; the
 //    step's 128 k become 64 columns of bf16 pairs in tensor memory (two
 //    tcgen05.st), two buffers; the weights never pass through shared memory
@@ -52,7 +55,8 @@ constexpr int kStages = 6;         // stages (packed weights, scales, activation
 constexpr int kWBufs = 2;          // dequantised weight buffers in tensor memory
 constexpr int kMaxBS = 64;         // block rows (MMA N)
 constexpr int kDeqWarps = 8;
-constexpr int kWarps = 14;         // 0 producer, 1 MMA, 2..9 dequantisation, 10..13 epilogue
+constexpr int kGatherWarps = 2;    // warps issuing the row gathers: 0 and 14
+constexpr int kWarps = 15;         // 0 producer, 1 MMA, 2..9 dequantisation, 10..13 epilogue, 14 gathers
 constexpr int kThreads = kWarps * 32;
 constexpr int kStepWBytes = kBM * kBK / 2;   // packed int4 of one tile per step: 8 KB
 constexpr int kHalfBytes = kMaxBS * 128;     // one 64-k half of the activation tile: 8 KB
@@ -272,12 +276,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Item = (block b, feature tiles kNT np .. kNT np + nts - 1).
   auto tiles_of = [&](int np) { return min(kNT, ntn - kNT * np); };
 
-  if (warp == 0) {
-    // --------------------------------------------------------- producer
-    // Lane l < bs / 2 issues gather l of each step: half h = l / (bs / 4),
-    // rows 4 i .. 4 i + 3 with i = l % (bs / 4).
+  if (warp == 0 || warp >= 2 + kDeqWarps + 4) {
+    // --------------------------------------------------------- producers
+    // Gather l < bs / 2 of each step (half h = l / (bs / 4), rows 4 i .. 4 i
+    // + 3 with i = l % (bs / 4)) is issued by lane l / kGatherWarps of
+    // producer warp l % kGatherWarps.
+    // Warp 0 also arms the stage's barrier and bulk-copies the weights.
+    const int pw = warp == 0 ? 0 : warp - (2 + kDeqWarps + 4) + 1;
     const int ng = bs >> 2;
-    const int gh = lane < 2 * ng ? lane / ng : 0, gi = lane < 2 * ng ? lane % ng : 0;
+    const int l = kGatherWarps * lane + pw;
+    const bool gl = l < 2 * ng;
+    const int gh = gl ? l / ng : 0, gi = gl ? l % ng : 0;
     uint32_t g = 0;  // step counter of this CTA
     bool ok = true;
     for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
@@ -311,19 +320,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t use = g / kStages;
         if (use > 0) ok = wait_or_abort(sm, &sm.done[s], (use - 1) & 1u);
         if (!ok) break;
-        if (lane == 0) {
+        if (pw == 0 && lane == 0) {
           mbar_arrive_expect_tx(&sm.full[s], bytes);
           bulk_g2s(sm.wraw[s], wsrc + (int64_t)kc * nts * kStepWBytes, (uint32_t)(nts * kStepWBytes), &sm.full[s]);
           bulk_g2s(sm.sscale[s], ssrc + (int64_t)kc * p.N, (uint32_t)(nts * kBM * 2), &sm.full[s]);
         }
-        __syncwarp();
-        if (lane < 2 * ng)
+        if (gl)
           tma_gather4(&sm.act[s][gh][gi * 512], &amap, kc * kBK + gh * kHalfK, gr[0], gr[1], gr[2], gr[3],
                       &sm.full[s]);
       }
     }
     // Copies issued and not consumed (after an abort) land before the CTA
-    // releases its shared memory: wait for the last phase of every stage.
+    // releases its shared memory: each producer warp waits for the last
+    // phase of every stage it issued into.
     if (lane == 0) {
       const uint32_t first = g > (uint32_t)kStages ? g - kStages : 0u;
       for (uint32_t gg = first; gg < g; ++gg)
