@@ -665,9 +665,10 @@ def run_ours(args, dist):
     # projection of the whole-expert prefill shape, M = 2304 tokens x top-8
     # over 288 experts, 2N = 4096, K = 4096, uint4b8 group-128 weights
     # (profiles/sm74/titan_prefill/marlin.py:417-424), the four list GEMMs
-    # back to back in one CUDA graph; Zipf(1.1) routes.
+    # back to back in one CUDA graph; Zipf(1.1) routes.  vLLM's Marlin on the
+    # same inputs beside it in single-GPU runs only (a comparison line).
     if not args.skip_moe_gemm:
-        secondary["moe_w4a16_gemm"] = moe_gemm_line(dev, peak, gm)
+        secondary["moe_w4a16_gemm"] = moe_gemm_line(dev, peak, gm, marlin=world == 1)
     # ---- the reference's own Triton kernels on this B200 (rank 0 of a
     # single-GPU run only; comparison lines, not our path)
     if rank == 0 and world == 1 and not args.skip_reference_triton:
