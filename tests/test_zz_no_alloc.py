@@ -7,7 +7,8 @@ captures a stream in global mode (cudaMalloc is refused then).  For them the
 library keeps the split-KV scratch in a static 8 MiB device array.  This test
 calls that entry point directly through the C ABI, twice in a row on different
 inputs, and checks each output against the regular entry point (which takes a
-caller-allocated workspace), with the MLA tolerance used by the other tests.
+caller-allocated workspace) and against the FP32 oracle, with the MLA
+tolerance used by the other tests.
 It is collected last so a failure here cannot hide another test's result, and
 it sets up everything it needs so it also passes alone in a fresh process.
 """
@@ -62,6 +63,11 @@ def test_noalloc_matches_workspace_entry_point(native_lib, cuda_device, tokens, 
         o, r = out.float(), ref.float()
         assert torch.isfinite(o).all()
         assert bool(((o - r).abs() <= ATOL + RTOL * r.abs()).all()), (call, (o - r).abs().max().item())
+        # and on its own against the oracle
+        from oracle import oracle as O
+        want = O.mla_sparse_attention(q.cpu(), rows.cpu(), idx.cpu(), 512 ** -0.5)
+        oc = o.cpu()
+        assert bool(((oc - want).abs() <= ATOL + RTOL * want.abs()).all()), (call, (oc - want).abs().max().item())
 
 
 def test_noalloc_rejects_calls_beyond_the_scratch(native_lib, cuda_device):
