@@ -905,8 +905,10 @@ __global__ void __launch_bounds__(kCombineThreads) sparse_mla_combine_kernel(con
   const float *o_t = p.part_o + ((int64_t)t * S * p.Hp + hh) * kD + dim;
   const int64_t split_stride = (int64_t)p.Hp * kD;
 
-  // 0. issue this thread's first partial loads before the max/sum phase
-  constexpr int kPre = 2;
+  // 0. issue this thread's partial loads before the max/sum phase (all of
+  // them for up to 4 x kPre partials: 17 at B = 8), so the weighted sum
+  // below waits on no further load round trip
+  constexpr int kPre = 5;
   float4 o_pre[kPre];
   float lse_pre[kPre];
 #pragma unroll
