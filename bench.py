@@ -367,12 +367,12 @@ class PagedBench:
 def splits_and_launches(batch, sms, device_index):
     """Split count the B200 policy picks, its cluster size and kernel launches
     per call (the combine kernel runs only when the split kernel cannot merge
-    the cluster partials itself)."""
+    the partials itself: in its clusters, or flat across its CTAs)."""
     from kernels.titan_mla import _choose_kv_splits_b200, _cluster_tables, _launch_layout
     tables = _cluster_tables(device_index)
     S = _choose_kv_splits_b200(batch, 1, TOPK, sms, tables)
-    C, nc = _launch_layout(batch, S, tables)
-    return S, C, (1 if nc == 1 or (C >= 2 and nc <= C) else 2)
+    C, nc, flat = _launch_layout(batch, S, tables)
+    return S, C, (1 if nc == 1 or flat or (C >= 2 and nc <= C) else 2)
 
 
 def run_ours(args, dist):

@@ -51,6 +51,7 @@ enum DeviceError : int {
   kDevErrNone = 0,
   kDevErrMbarrierTimeout = 1,
   kDevErrCapacity = 2,  // a count past a fixed-size list; the excess is dropped
+  kDevErrSpinTimeout = 3,  // a CTA gave up waiting for the other CTAs of its barrier
 };
 __device__ int g_device_error = 0;
 
@@ -319,8 +320,37 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int *p, int v) {
   return old;
 }
 
+__device__ __forceinline__ int atom_add_relaxed_gpu(int *p, int v) {
+  int old;
+  asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void st_relaxed_gpu(int *p, int v) {
   asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded spin until the counter at p reaches `target` (acquire: what the
+// arriving CTAs released before their increments is visible afterwards).
+// Gives up after ~`limit_cycles` SM clocks, recording kDevErrSpinTimeout.
+// Only for counters whose arrivals come from CTAs of the same grid that are
+// resident together with the waiting one.
+__device__ __forceinline__ bool spin_until_at_least(const int *p, int target, long long limit_cycles) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (clock64() - t0 > limit_cycles) {
+      atomicCAS(&g_device_error, 0, kDevErrSpinTimeout);
+      return false;
+    }
+  }
 }
 
 __device__ __forceinline__ uint4 ld_global_nc_v4(const void *p) {

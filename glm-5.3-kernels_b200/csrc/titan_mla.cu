@@ -92,7 +92,7 @@ struct Smem {
   float cM[kHeads], cL[kHeads];
   alignas(8) uint64_t merge_bar;           // counts the bytes the cluster pushes here
   uint64_t row_bar[kRing];                 // per ring stage: one arrival per warp + its gather4 bytes
-  int last;                                // this CTA arrived last at its cross-cluster counter
+  int last;                                // cross-cluster merge: this CTA arrived last; flat merge: its wait ended
 };
 
 // Two CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
@@ -119,6 +119,7 @@ struct Params {
   int64_t split_topk;
   float scale_log2;  // sm_scale * log2(e)
   int *sem;          // [T][groups][16] arrival counters (zero between calls) or null: combine kernel
+                     // (cluster launches: one per cluster rank; flat merge: arrivals, departures)
   // Paged launches (kPaged): idx holds request-local token positions; row =
   // block_table[req_id[t], tok / block_size] * block_stride_rows + tok % block_size.
   const int32_t *req_id;
@@ -187,6 +188,129 @@ __device__ __forceinline__ void merge_cluster_partials(const Params &p, int t, i
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
       *reinterpret_cast<uint32_t *>(dst + 32 * k) = pack_bf16x2(sum[k].x * inv, sum[k].y * inv);
+  }
+}
+
+// Flat split merge (cluster-less launches given arrival counters): the S
+// CTAs of (token t, head group hg) have each written a normalised partial and
+// its LSE; they meet at a counter barrier, then each merges a share of the
+// 256 units (head, 32-dim block) of the token over all S partials: CTA
+// `split` takes units split, split + S, ...  Thread (group g, item = (unit
+// slot, float4 column)) loads partials g, g + groups, ... with their LSEs in
+// one round trip (each warp load is four whole 128-byte lines) and weighs
+// them against its own largest LSE m_g; the groups then meet in shared
+// memory: out = sum_g acc_g e^(m_g - M) / sum_g l_g e^(m_g - M), M = max m_g,
+// the combine kernel's result up to rounding.  The launcher uses this only
+// for 8 <= S <= 160 and grids that fit on the device at once, launched
+// cooperatively so that every CTA a waiter waits for is resident.  Counters:
+// [0] arrivals, [1] departures; the last CTA to depart (every CTA has
+// finished waiting by then) zeroes both for the next call.
+constexpr int kFlatPre = 15;    // partials per thread (at most 15 for 8 <= S <= 160), all loaded at once
+constexpr int kFlatMinS = 8;     // 8 x 32 = 256 (unit slot, column) items at most
+constexpr int kFlatMaxS = 160;
+constexpr int kFlatUnits = kHeads * (kD / 32);
+static_assert(6 * kThreads <= kHeads * kD, "the group sums and (m, l) pairs fit the dead staging area");
+// Every split count the flat merge takes gives each thread at most kFlatPre
+// partials (all loaded in one round trip) and at least one thread group.
+constexpr bool flat_shares_fit() {
+  for (int S = kFlatMinS; S <= kFlatMaxS; ++S) {
+    const int groups = kThreads / (8 * ((kFlatUnits + S - 1) / S));
+    if (groups < 1 || (S + groups - 1) / groups > kFlatPre) return false;
+  }
+  return true;
+}
+static_assert(flat_shares_fit(), "flat merge shares exceed the preloaded partials");
+
+__device__ __forceinline__ void merge_flat_share(const Params &p, Smem &sm, int t, int hg, int split, int tid) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int S = p.NC;
+  const int slots = (kFlatUnits + S - 1) / S;  // units of the widest share (<= 32)
+  const int items = 8 * slots;
+  const int groups = kThreads / items;  // ceil(S / groups) <= kFlatPre for every S the launcher allows
+  const int grp = tid / items, item = tid - grp * items;
+  const int u = split + S * (item >> 3), q4 = item & 7;
+  const int h = u & (kHeads - 1), blk = u >> 4;  // head and 32-dim block of unit u
+  const int hh = hg * kHeads + h;
+  const bool mine = grp < groups && u < kFlatUnits && hh < p.H;
+  const int64_t split_stride = (int64_t)p.Hp * kD;
+  const float *o_t = p.part_o + ((int64_t)t * S * p.Hp + hh) * kD + 32 * blk + 4 * q4;
+  const float *lse_t = p.part_lse + (int64_t)t * S * p.Hp + hh;
+
+  float4 o_pre[kFlatPre];
+  float lse_pre[kFlatPre];
+#pragma unroll
+  for (int k = 0; k < kFlatPre; ++k) {
+    const int s = grp + groups * k;
+    const bool ld = mine && s < S;
+    o_pre[k] = ld ? __ldcg(reinterpret_cast<const float4 *>(o_t + s * split_stride)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    lse_pre[k] = ld ? __ldcg(lse_t + (int64_t)s * p.Hp) : -INFINITY;
+  }
+  float m = kNegLarge;
+#pragma unroll
+  for (int k = 0; k < kFlatPre; ++k) m = fmaxf(m, lse_pre[k]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float l = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kFlatPre; ++k) {
+    const float w = ex2_approx((lse_pre[k] - m) * kLog2e);
+    l += w;
+    acc.x += w * o_pre[k].x;
+    acc.y += w * o_pre[k].y;
+    acc.z += w * o_pre[k].z;
+    acc.w += w * o_pre[k].w;
+  }
+  float4 *part = reinterpret_cast<float4 *>(sm.u.stage);  // [groups][items] sums; the ring is dead
+  float2 *part_ml = reinterpret_cast<float2 *>(sm.u.stage + 4 * kThreads);  // [groups][items] (m_g, l_g)
+  if (grp < groups) {
+    part[tid] = acc;
+    part_ml[tid] = make_float2(m, l);
+  }
+  __syncthreads();
+  if (grp == 0 && mine) {
+    float M = m;
+    for (int g2 = 1; g2 < groups; ++g2) M = fmaxf(M, part_ml[g2 * items + item].x);
+    const float a0 = ex2_approx((m - M) * kLog2e);
+    float L = l * a0;
+    acc.x *= a0;
+    acc.y *= a0;
+    acc.z *= a0;
+    acc.w *= a0;
+    for (int g2 = 1; g2 < groups; ++g2) {
+      const float2 ml = part_ml[g2 * items + item];
+      const float4 v = part[g2 * items + item];
+      const float a = ex2_approx((ml.x - M) * kLog2e);
+      L += ml.y * a;
+      acc.x += a * v.x;
+      acc.y += a * v.y;
+      acc.z += a * v.z;
+      acc.w += a * v.w;
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 1.0f;
+    uint2 r;
+    r.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+    r.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2 *>(p.out + (int64_t)t * p.out_st + (int64_t)hh * p.out_sh + 32 * blk + 4 * q4) = r;
+  }
+}
+
+__device__ __forceinline__ void merge_flat(const Params &p, Smem &sm, int t, int hg, int split, int tid) {
+  const int S = p.NC;
+  __syncthreads();  // every partial store of this CTA precedes thread 0's release below
+  int *ctr = p.sem + ((int64_t)t * gridDim.y + hg) * kMaxCluster;
+  int departed = 0;
+  if (tid == 0) {
+    // The last to arrive knows it from its own ticket; the others poll.
+    sm.last = atom_add_acq_rel_gpu(ctr, 1) == S - 1 || spin_until_at_least(ctr, S, kLongWaitCycles);
+    // Departure ticket: relaxed, yet ordered after the arrival / wait by
+    // their acquire; the result is first read after the merge, so the round
+    // trip overlaps it.
+    departed = atom_add_relaxed_gpu(ctr + 1, 1);
+  }
+  __syncthreads();
+  if (sm.last) merge_flat_share(p, sm, t, hg, split, tid);  // else: the error word says so
+  if (tid == 0 && departed == S - 1) {
+    st_relaxed_gpu(ctr, 0);
+    st_relaxed_gpu(ctr + 1, 0);
   }
 }
 
@@ -670,6 +794,42 @@ __global__ void __launch_bounds__(kThreads, 2)
   if ((tid & 15) == 0) sm.ml[red_h] = make_float2(m_run, l_run);
   const int C = kCluster ? p.C : 1;
   const int cl = split / C;  // partial index when kPartialOut
+  if constexpr (!kCluster && kPartialOut) {
+    // Partial of this split: the normalised accumulator goes through shared
+    // memory (the cluster merge's swizzled [16][512] staging, conflict free)
+    // and leaves as fully coalesced 512-byte warp stores; stored straight
+    // from the MMA fragments every warp store touched 16 half-written lines.
+    __syncthreads();
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int hl = g + 8 * half;
+      const float l = sm.ml[hl].y;
+      const float inv = l > 0.0f ? 1.0f / l : 1.0f;
+      float *row = &sm.u.stage[hl * kD];
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        *reinterpret_cast<float4 *>(row + merge_pos(hl, 0, dim0 + 4 * s)) =
+            make_float4(acc[2 * s][2 * half] * inv, acc[2 * s][2 * half + 1] * inv, acc[2 * s + 1][2 * half] * inv,
+                        acc[2 * s + 1][2 * half + 1] * inv);
+    }
+    __syncthreads();
+    float *dst = p.part_o + (((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads) * kD;
+#pragma unroll
+    for (int k = 0; k < kHeads * kD / 4 / kThreads; ++k) {
+      const int e = tid + kThreads * k;  // float4 e of the CTA's 16 x 512 block
+      const int hl = e / (kD / 4), q4 = e % (kD / 4);
+      if (hg * kHeads + hl < p.H)
+        *reinterpret_cast<float4 *>(dst + hl * kD + 4 * q4) =
+            *reinterpret_cast<const float4 *>(&sm.u.stage[hl * kD + merge_pos(hl, 0, 4 * q4)]);
+    }
+    if (tid < kHeads && hg * kHeads + tid < p.H) {
+      const float2 ml = sm.ml[tid];
+      // (m + log2 l) * ln 2; l == 0 gives -inf, which the merge weighs as 0.
+      p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (ml.x + lg2_approx(ml.y)) * kLn2;
+    }
+    if (p.sem != nullptr) merge_flat(p, sm, t, hg, split, tid);
+    return;
+  }
   if constexpr (!kCluster) {
     __syncthreads();
 #pragma unroll
@@ -687,33 +847,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           v[4 * s + 2 * x + 0] = acc[2 * s + x][2 * half + 0] * inv;
           v[4 * s + 2 * x + 1] = acc[2 * s + x][2 * half + 1] * inv;
         }
-      if constexpr (!kPartialOut) {
-        uint4 o0, o1;
-        o0.x = pack_bf16x2(v[0], v[1]);
-        o0.y = pack_bf16x2(v[2], v[3]);
-        o0.z = pack_bf16x2(v[4], v[5]);
-        o0.w = pack_bf16x2(v[6], v[7]);
-        o1.x = pack_bf16x2(v[8], v[9]);
-        o1.y = pack_bf16x2(v[10], v[11]);
-        o1.z = pack_bf16x2(v[12], v[13]);
-        o1.w = pack_bf16x2(v[14], v[15]);
-        uint4 *dst = reinterpret_cast<uint4 *>(p.out + (int64_t)t * p.out_st + (int64_t)h * p.out_sh + dim0);
-        dst[0] = o0;
-        dst[1] = o1;
-      } else {
-        float4 *dst = reinterpret_cast<float4 *>(p.part_o + (((int64_t)t * p.NC + cl) * p.Hp + h) * kD + dim0);
-        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-        dst[2] = make_float4(v[8], v[9], v[10], v[11]);
-        dst[3] = make_float4(v[12], v[13], v[14], v[15]);
-      }
-    }
-    if constexpr (kPartialOut) {
-      if (tid < kHeads && hg * kHeads + tid < p.H) {
-        const float2 ml = sm.ml[tid];
-        // (m + log2 l) * ln 2; l == 0 gives -inf, which the combine weighs as 0.
-        p.part_lse[((int64_t)t * p.NC + cl) * p.Hp + hg * kHeads + tid] = (ml.x + lg2_approx(ml.y)) * kLn2;
-      }
+      uint4 o0, o1;
+      o0.x = pack_bf16x2(v[0], v[1]);
+      o0.y = pack_bf16x2(v[2], v[3]);
+      o0.z = pack_bf16x2(v[4], v[5]);
+      o0.w = pack_bf16x2(v[6], v[7]);
+      o1.x = pack_bf16x2(v[8], v[9]);
+      o1.y = pack_bf16x2(v[10], v[11]);
+      o1.z = pack_bf16x2(v[12], v[13]);
+      o1.w = pack_bf16x2(v[14], v[15]);
+      uint4 *dst = reinterpret_cast<uint4 *>(p.out + (int64_t)t * p.out_st + (int64_t)h * p.out_sh + dim0);
+      dst[0] = o0;
+      dst[1] = o1;
     }
     return;
   }
@@ -1249,11 +1394,20 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   int rc = prepare_device(smem, &capacity);
   if (rc != TITAN_OK) return rc;
   // NC clusters (partials) of C splits per (token, head group).
-  const int C = choose_cluster(num_tokens * groups, num_kv_splits, capacity);
-  const int64_t NC = num_kv_splits / C;
-  // The split kernel merges only when every lane of the last CTA loads at
-  // most 16 partial values (NC <= C); larger merges go to the combine kernel.
+  int C = choose_cluster(num_tokens * groups, num_kv_splits, capacity);
+  int64_t NC = num_kv_splits / C;
+  // The split kernel merges cluster partials itself only when every lane of
+  // the last CTA loads at most 16 partial values (NC <= C).  Otherwise, with
+  // counters given and a grid that is resident all at once, the CTAs of a
+  // token merge among themselves without clusters (merge_flat); else the
+  // combine kernel merges.
   const bool in_kernel_merge = sem != nullptr && C >= 2 && NC > 1 && NC <= C;
+  const bool flat_merge = sem != nullptr && !in_kernel_merge && NC > 1 && num_kv_splits >= kFlatMinS &&
+                          num_kv_splits <= kFlatMaxS && num_tokens * groups * num_kv_splits <= capacity[1];
+  if (flat_merge) {
+    C = 1;
+    NC = num_kv_splits;
+  }
   if (sem != nullptr && sem_count < titan_mla_semaphore_count(num_tokens, num_heads))
     return fail(TITAN_ERR_INVALID_ARGUMENT, "mla: %lld semaphores given, %lld needed", (long long)sem_count,
                 (long long)titan_mla_semaphore_count(num_tokens, num_heads));
@@ -1283,7 +1437,7 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   prm.scale_log2 = sm_scale * 1.4426950408889634f;
   prm.part_o = nullptr;
   prm.part_lse = nullptr;
-  prm.sem = in_kernel_merge ? sem : nullptr;
+  prm.sem = in_kernel_merge || flat_merge ? sem : nullptr;
   prm.req_id = nullptr;
   prm.block_table = nullptr;
   prm.bt_st0 = prm.bt_st1 = 0;
@@ -1323,12 +1477,20 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = (unsigned)C;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
+  if (flat_merge) {
+    // The CTAs of a token wait for one another: a cooperative launch makes
+    // the runtime guarantee that the whole grid is resident at once, also
+    // next to other work on other streams.
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+  } else {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)C;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = C > 1 ? 2 : 1;
+  cfg.numAttrs = C > 1 || flat_merge ? 2 : 1;
   cudaError_t e;
   // Single-pass CTAs that walk at least kF16MinTiles tiles (prefill shapes)
   // take the f16 arithmetic.
@@ -1347,7 +1509,7 @@ static int launch_mla(const void *q, int64_t q_stride_token, int64_t q_stride_he
               : (NC > 1 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<true, false, false>, prm, rows_map)
                         : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<false, false, false>, prm, rows_map));
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla launch (C=%d): %s", C, cudaGetErrorString(e));
-  if (NC == 1 || in_kernel_merge) return TITAN_OK;
+  if (NC == 1 || in_kernel_merge || flat_merge) return TITAN_OK;
   // Combine the NC cluster partials: 32 CTAs per (token, head group).
   e = launch_combine(prm, (int)groups, s);
   if (e != cudaSuccess) return fail(TITAN_ERR_CUDA, "mla combine launch: %s", cudaGetErrorString(e));

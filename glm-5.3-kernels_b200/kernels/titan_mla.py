@@ -58,7 +58,12 @@ def _cdiv(a, b):
 # B200 sweep of every split count with at most one CTA per SM for B = 1..8
 # (calls back to back in CUDA graphs, cold L2, the current reader): the
 # median of the parameter sets whose picks match the best measured split
-# count at every batch size.
+# count at every batch size.  Split counts whose partials would otherwise
+# need the combine kernel (8 <= S <= 160, grid resident at once) are merged
+# by the split CTAs themselves without clusters (flat merge: a counter
+# barrier per token, then each CTA merges a share of the columns); its terms
+# reproduce the measured best split count of every batch size 1..8 (68, 68,
+# 34, 34, 23, 23, 17, 17).
 _TILE_ROWS = 32
 _COST_TILE_US = 0.5
 _COST_CLUSTER_MERGE_US = {2: 1.0, 4: 1.0, 8: 0.8, 16: 0.6}
@@ -67,6 +72,9 @@ _COST_SPLIT_MERGE_PER_PARTIAL_US = 0.05
 _COST_COMBINE_US = 1.0
 _COST_COMBINE_PER_PARTIAL_US = 0.05
 _COST_SHARED_SM_US = 1.5
+_COST_FLAT_MERGE_US = 0.8
+_COST_FLAT_MERGE_PER_PARTIAL_US = 0.005
+_FLAT_MIN_SPLITS, _FLAT_MAX_SPLITS = 8, 160
 _MAX_CLUSTER = 16
 _CLUSTER_SIZES = (1, 2, 4, 8, 16)
 _cluster_tables_cache = {}
@@ -86,8 +94,11 @@ def _cluster_tables(device_index):
 
 
 def _launch_layout(units, S, tables):
-    """(C, NC) as the launcher picks them: C = the largest power of two <= 16
-    dividing S whose units * S / C clusters are all co-resident."""
+    """(C, NC, flat) as the launcher picks them when given arrival counters:
+    C = the largest power of two <= 16 dividing S whose units * S / C
+    clusters are all co-resident; when the NC = S / C cluster partials would
+    need the combine kernel (NC > C) and the flat merge applies (16 <= S <=
+    160, all units * S CTAs co-resident), C = 1, NC = S, flat."""
     C = 1
     for c, capacity, _ in tables:
         if c == 1:
@@ -96,7 +107,12 @@ def _launch_layout(units, S, tables):
             break
         if units * (S // c) <= max(0, capacity):
             C = c
-    return C, S // C
+    nc = S // C
+    resident = dict((c, cap) for c, cap, _ in tables).get(1, 0)
+    if (nc > 1 and not (C >= 2 and nc <= C) and _FLAT_MIN_SPLITS <= S <= _FLAT_MAX_SPLITS
+            and units * S <= resident):
+        return 1, S, True
+    return C, nc, False
 
 
 @functools.lru_cache(maxsize=1024)
@@ -115,11 +131,13 @@ def _choose_kv_splits_b200(num_tokens, num_head_groups, index_topk, sm_count, ta
     exclusive = {c: e for c, _, e in tables}
     best, best_cost = 1, None
     for S in range(1, sm_count // units + 1):
-        C, nc = _launch_layout(units, S, tables)
+        C, nc, flat = _launch_layout(units, S, tables)
         rows = -(-index_topk // S)
         cost = max(1, -(-rows // _TILE_ROWS)) * _COST_TILE_US
         cost += _COST_CLUSTER_MERGE_US[C] if C > 1 else 0.0
-        if nc > 1:
+        if flat:
+            cost += _COST_FLAT_MERGE_US + _COST_FLAT_MERGE_PER_PARTIAL_US * S
+        elif nc > 1:
             if C >= 2 and nc <= C:
                 cost += _COST_SPLIT_MERGE_US + _COST_SPLIT_MERGE_PER_PARTIAL_US * nc
             else:

@@ -166,7 +166,7 @@ def test_deterministic_and_graph_capturable(big_cache, native_lib, cuda_device):
     q = torch.randn(2, 16, 512, generator=g).to(torch.bfloat16).to(cuda_device)
     idx = torch.randint(0, n, (2, 1, 2176), generator=g, dtype=torch.int32).to(cuda_device)
     kv = cache.view(n, 1, 528)
-    for splits in (1, 32):
+    for splits in (1, 17, 32):  # single pass, flat merge (cooperative launch), cluster merge
         a = attn(q, kv, idx, 512 ** -0.5, num_kv_splits=splits)
         b = attn(q, kv, idx, 512 ** -0.5, num_kv_splits=splits)
         assert torch.equal(a, b)
@@ -198,10 +198,13 @@ def test_empty_tokens_and_topk(native_lib, cuda_device):
 
 @pytest.mark.parametrize("tokens,heads", [(1, 16), (2, 20), (3, 32)])
 def test_in_kernel_merge_matches_combine_kernel(big_cache, native_lib, cuda_device, tokens, heads):
-    """titan_mla_sparse_attention_sem (last-arriving CTA merges the cluster
-    partials) against titan_mla_sparse_attention (combine kernel) and the
-    oracle, for split counts that give several clusters per token; the
-    arrival counters are zero again after every call."""
+    """titan_mla_sparse_attention_sem against titan_mla_sparse_attention
+    (combine kernel) and the oracle, for split counts that give several
+    clusters per token (the last-arriving CTA merges the cluster partials)
+    or, where those would need the combine kernel, the cluster-less flat
+    merge (17, 34, 68, 79 and 136 splits: the CTAs of a token meet at a
+    counter barrier and each merges a share of the columns); the counters are
+    zero again after every call."""
     import ctypes
     lib = native_lib
     latent, cache, rows = big_cache
@@ -215,7 +218,7 @@ def test_in_kernel_merge_matches_combine_kernel(big_cache, native_lib, cuda_devi
     need = lib.titan_mla_semaphore_count(tokens, heads)
     assert need == tokens * -(-heads // 16) * 16
     sem = torch.zeros(need, dtype=torch.int32, device=cuda_device)
-    for splits in (12, 24, 32, 40, 48, 56, 64, 80, 96, 136):
+    for splits in (12, 17, 24, 32, 34, 40, 48, 56, 64, 68, 79, 80, 96, 136):
         ws = torch.empty(lib.titan_mla_workspace_bytes(tokens, heads, splits), dtype=torch.uint8,
                          device=cuda_device)
         args = (qd.data_ptr(), qd.stride(0), qd.stride(1), kv.data_ptr(), kv.stride(0), n,
@@ -245,6 +248,38 @@ def test_in_kernel_merge_matches_combine_kernel(big_cache, native_lib, cuda_devi
     assert titan_native.device_error(qd) == 0
 
 
+@pytest.mark.parametrize("splits", [9, 17, 37, 49])
+def test_flat_merge_edge_cases(big_cache, native_lib, cuda_device, splits):
+    """Flat merge (cluster-less split CTAs meeting at a counter barrier):
+    a head count that is not a multiple of 16 (two head groups, the second
+    half empty), a token with no valid index (exact zeros: every partial has
+    LSE -inf), a token whose indices are one row repeated, splits whose
+    column shares differ in width (128 / S not whole), back-to-back calls
+    (the counters are zeroed by the last CTA of each token); at 9 splits
+    one thread group walks all partials; at 49 splits the 294 CTAs run two
+    per SM."""
+    from kernels import titan_native
+    from kernels.titan_mla import triton_mla_sparse_attention as attn
+    latent, cache, rows = big_cache
+    n = rows.shape[0]
+    g = torch.Generator().manual_seed(70 + splits)
+    q = torch.randn(3, 20, 512, generator=g).to(torch.bfloat16)
+    idx = torch.randint(-8, n + 8, (3, 1, 2176), generator=g, dtype=torch.int32)
+    idx[1] = -1
+    idx[2, 0, :] = idx[2, 0, 5].clamp(0, n - 1)
+    ref = O.mla_sparse_attention(q, rows, idx, 512 ** -0.5)
+    qd, idxd, kv = q.to(cuda_device), idx.to(cuda_device), cache.view(n, 1, 528)
+    first = attn(qd, kv, idxd, 512 ** -0.5, num_kv_splits=splits, sm_count=148)
+    for _ in range(3):
+        again = attn(qd, kv, idxd, 512 ** -0.5, num_kv_splits=splits, sm_count=148)
+    torch.cuda.synchronize()
+    assert torch.equal(first, again)
+    ok, err = within(first, ref)
+    assert ok, (splits, err)
+    assert not first[1].any()
+    assert titan_native.device_error(qd) == 0
+
+
 @pytest.mark.parametrize("tokens,heads,topk", [(160, 16, 2176), (150, 20, 96), (148, 16, 2208)])
 def test_large_single_pass(big_cache, native_lib, cuda_device, tokens, heads, topk):
     """Single-pass launches that fill the device (prefill shapes): against the
@@ -268,10 +303,12 @@ def test_large_single_pass(big_cache, native_lib, cuda_device, tokens, heads, to
     assert titan_native.device_error(out) == 0
 
 
-def test_concurrent_streams_use_separate_split_scratch(big_cache, native_lib, cuda_device):
+@pytest.mark.parametrize("splits", [80, 68])
+def test_concurrent_streams_use_separate_split_scratch(big_cache, native_lib, cuda_device, splits):
     """Split launches issued on two streams at once (no ordering between
     them) each use their own stream's partials workspace and arrival
-    counters: results equal the same calls issued one after another."""
+    counters: results equal the same calls issued one after another (80
+    splits: cluster merges; 68: flat merges, cooperative grids side by side)."""
     from kernels.titan_mla import triton_mla_sparse_attention as attn
     latent, cache, rows = big_cache
     n = rows.shape[0]
@@ -279,7 +316,7 @@ def test_concurrent_streams_use_separate_split_scratch(big_cache, native_lib, cu
     g = torch.Generator().manual_seed(21)
     qs = [torch.randn(1, 16, 512, generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(8)]
     ids = [torch.randint(0, n, (1, 1, 2176), generator=g, dtype=torch.int32).to(cuda_device) for _ in range(8)]
-    want = [attn(qs[k], kv, ids[k], 512 ** -0.5, num_kv_splits=80) for k in range(8)]
+    want = [attn(qs[k], kv, ids[k], 512 ** -0.5, num_kv_splits=splits) for k in range(8)]
     torch.cuda.synchronize()
     streams = [torch.cuda.Stream(), torch.cuda.Stream()]
     for s in streams:
@@ -288,7 +325,7 @@ def test_concurrent_streams_use_separate_split_scratch(big_cache, native_lib, cu
     for rep in range(4):
         for k in range(8):
             with torch.cuda.stream(streams[k % 2]):
-                got[k] = attn(qs[k], kv, ids[k], 512 ** -0.5, num_kv_splits=80)
+                got[k] = attn(qs[k], kv, ids[k], 512 ** -0.5, num_kv_splits=splits)
         for s in streams:
             torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()

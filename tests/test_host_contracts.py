@@ -66,15 +66,22 @@ def test_b200_split_policy_picks():
     layout (cluster size C, clusters per token NC) the launcher derives."""
     from kernels.titan_mla import _choose_kv_splits_b200, _launch_layout
     picks = {B: _choose_kv_splits_b200(B, 1, 2176, 148, B200_CLUSTER_TABLES) for B in range(1, 9)}
-    assert picks == {1: 80, 2: 48, 3: 40, 4: 16, 5: 16, 6: 16, 7: 16, 8: 17}, picks
-    assert _launch_layout(1, 80, B200_CLUSTER_TABLES) == (16, 5)   # last-arriver merge (NC <= C)
-    assert _launch_layout(2, 40, B200_CLUSTER_TABLES) == (8, 5)
-    assert _launch_layout(2, 48, B200_CLUSTER_TABLES) == (16, 3)   # last-arriver merge
-    assert _launch_layout(4, 16, B200_CLUSTER_TABLES) == (16, 1)   # one cluster per token
-    assert _launch_layout(8, 17, B200_CLUSTER_TABLES) == (1, 17)   # combine kernel
-    assert _launch_layout(8, 16, B200_CLUSTER_TABLES) == (16, 1)
-    assert _launch_layout(7, 16, B200_CLUSTER_TABLES) == (16, 1)   # one cluster per token
-    assert _launch_layout(4, 24, B200_CLUSTER_TABLES) == (8, 3)
+    assert picks == {1: 68, 2: 68, 3: 34, 4: 34, 5: 23, 6: 23, 7: 17, 8: 17}, picks
+    assert _launch_layout(1, 68, B200_CLUSTER_TABLES) == (1, 68, True)     # flat merge
+    assert _launch_layout(1, 80, B200_CLUSTER_TABLES) == (16, 5, False)    # last-arriver merge (NC <= C)
+    assert _launch_layout(2, 40, B200_CLUSTER_TABLES) == (8, 5, False)
+    assert _launch_layout(2, 48, B200_CLUSTER_TABLES) == (16, 3, False)    # last-arriver merge
+    assert _launch_layout(4, 16, B200_CLUSTER_TABLES) == (16, 1, False)    # one cluster per token
+    assert _launch_layout(8, 17, B200_CLUSTER_TABLES) == (1, 17, True)     # flat merge
+    assert _launch_layout(4, 34, B200_CLUSTER_TABLES) == (1, 34, True)     # C = 2 would need the combine
+    assert _launch_layout(3, 136, B200_CLUSTER_TABLES) == (1, 136, False)  # 408 CTAs: combine kernel
+    assert _launch_layout(1, 8, B200_CLUSTER_TABLES) == (8, 1, False)
+    assert _launch_layout(1, 12, B200_CLUSTER_TABLES) == (4, 3, False)     # last-arriver merge
+    assert _launch_layout(1, 13, B200_CLUSTER_TABLES) == (1, 13, True)     # flat merge
+    assert _launch_layout(1, 7, B200_CLUSTER_TABLES) == (1, 7, False)      # fewer than 8: combine
+    assert _launch_layout(8, 16, B200_CLUSTER_TABLES) == (16, 1, False)
+    assert _launch_layout(7, 16, B200_CLUSTER_TABLES) == (16, 1, False)    # one cluster per token
+    assert _launch_layout(4, 24, B200_CLUSTER_TABLES) == (8, 3, False)
     for T in (148, 149, 4096):
         assert _choose_kv_splits_b200(T, 1, 2176, 148, B200_CLUSTER_TABLES) == 1
     assert _choose_kv_splits_b200(0, 1, 2176, 148, B200_CLUSTER_TABLES) == 1
