@@ -365,14 +365,25 @@ class PagedBench:
 
 
 def splits_and_launches(batch, sms, device_index):
-    """Split count the B200 policy picks, its cluster size and kernel launches
+    """Split count the B200 policy picks, its cluster size, kernel launches
     per call (the combine kernel runs only when the split kernel cannot merge
-    the partials itself: in its clusters, or flat across its CTAs)."""
+    the partials itself: in its clusters, or flat across its CTAs) and how
+    the partials are merged."""
     from kernels.titan_mla import _choose_kv_splits_b200, _cluster_tables, _launch_layout
     tables = _cluster_tables(device_index)
     S = _choose_kv_splits_b200(batch, 1, TOPK, sms, tables)
     C, nc, flat = _launch_layout(batch, S, tables)
-    return S, C, (1 if nc == 1 or flat or (C >= 2 and nc <= C) else 2)
+    if S == 1:
+        merge = "single pass"
+    elif flat:
+        merge = f"flat merge of {S} split CTAs per token"
+    elif nc == 1:
+        merge = f"cluster merge ({C} CTAs)"
+    elif C >= 2 and nc <= C:
+        merge = f"cluster merge ({C} CTAs) + last-arriver merge of {nc} clusters"
+    else:
+        merge = f"combine kernel over {nc} partials"
+    return S, C, (1 if nc == 1 or flat or (C >= 2 and nc <= C) else 2), merge
 
 
 def run_ours(args, dist):
@@ -412,7 +423,7 @@ def run_ours(args, dist):
     dist.barrier()
     # ---- headline: B=1 decode, K calls back to back (CUDA graphs), cold rows
     J = graph_calls(K)
-    S1, C1, launches_per_call = splits_and_launches(1, sms, dev.index)
+    S1, C1, launches_per_call, merge1 = splits_and_launches(1, sms, dev.index)
     d1 = DecodeBench(attn, kvs, 1, J, 99 + rank, "fixed", sms)
     d1.time(max(1, W // J + 1), flush)                     # warm-up replays (>= W calls)
     dist.barrier()
@@ -557,10 +568,10 @@ def run_ours(args, dist):
     d8.time(1, flush)
     dist.barrier()
     b8_ms = dist.max(sum(d8.time(max(1, min(K, 256) // J8), flush)) / (max(1, min(K, 256) // J8) * J8))
-    S8, C8, _ = splits_and_launches(per, sms, dev.index)
+    S8, C8, _, merge8 = splits_and_launches(per, sms, dev.index)
     secondary["decode_b8"] = {
         "tokens_per_rank": per, "us_per_call": b8_ms * 1000, "tokens_per_s": per * world / (b8_ms * 1e-3),
-        "GBps_per_rank": d8.bytes_per_call / (b8_ms * 1e-3) / 1e9, "splits": S8, "cluster": C8}
+        "GBps_per_rank": d8.bytes_per_call / (b8_ms * 1e-3) / 1e9, "splits": S8, "cluster": C8, "merge": merge8}
     d8.close()
 
     # ---- config 4: prefill-shaped, T=4096 tokens sharded over ranks
@@ -711,7 +722,8 @@ def run_ours(args, dist):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "algorithmic_bytes_per_call": bytes_per_call,
-                         "kernel": ("sparse_mla_kernel<true> (split + cluster merge + last-arriver merge), whole call, back to back" if launches_per_call == 1 else "sparse_mla_kernel + combine (whole call, back to back)")},
+                         "kernel": f"sparse_mla_kernel ({S1} splits, {merge1}; {launches_per_call} launch(es) per call), "
+                                   "whole call, back to back"},
             "e2e": {"value": e2e_us, "unit": UNIT, "h2d_bytes_per_step": staging.shape[1],
                     "d2h_bytes_per_step": HEADS * 512 * 2,
                     "transfers_per_step": "H2D: q + indices, one pinned staging row, read by titan_copy's kernel "
