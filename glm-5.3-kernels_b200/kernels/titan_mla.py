@@ -9,8 +9,10 @@ compute runs in libtitan_b200.so (csrc/titan_mla.cu): rows gathered by the
 tensor memory accelerator (`tile::gather4`, four rows per load) into a
 shared-memory ring laid out as the lanes' tensor-core fragments, bf16 MMAs
 with fp32 online softmax, and split
-partials merged inside thread-block clusters and, across clusters, by the
-last CTA to finish (arrival counters).
+partials merged in the same launch: by the split CTAs of a token after a
+counter barrier (flat merge, decode batches up to 16), or inside
+thread-block clusters and, across clusters, by the last CTA to finish
+(arrival counters).
 
 528 bytes/token: 512 signed INT8 values followed by 1 FP32 scale + 12 zero bytes.
 """

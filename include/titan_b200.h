@@ -138,10 +138,16 @@ int64_t titan_mla_semaphore_count(int64_t num_tokens, int64_t num_heads);
  * tolerance) as titan_mla_sparse_attention, which this also replaces
  * (kernels/titan_mla.py:452-581: the split kernel :258-354 and the combine
  * kernel :357-429 become one launch).  When the splits of a token form several
- * thread-block clusters, each cluster CTA publishes its partial slice and
- * takes a ticket from an arrival counter; the last CTA of each cluster rank
- * merges that rank's slice over all clusters and writes the bf16 output, then
- * resets its counter to zero.
+ * thread-block clusters and at most as many clusters as CTAs per cluster,
+ * each cluster CTA publishes its partial slice and takes a ticket from an
+ * arrival counter; the last CTA of each cluster rank merges that rank's slice
+ * over all clusters and writes the bf16 output, then resets its counter to
+ * zero.  Otherwise, for 8 <= num_kv_splits <= 160 and a grid of at most the
+ * CTAs that fit on the device at once, the launch is cooperative and without
+ * clusters: the split CTAs of a token publish their partials, meet at the
+ * token's counter (bounded wait: device error 3 if it runs out) and each
+ * merges a share of the columns; the last CTA to leave zeroes the counters.
+ * Larger grids fall back to the combine kernel.
  *
  *   semaphores       int32 [semaphore_count] device array, all zero before the
  *                    first call; every call leaves it zero again.  Calls that
@@ -302,7 +308,11 @@ int titan_device_pointer(const void *ptr, void **device_ptr_out);
 /*
  * Device-side error word: kernels set it instead of trapping when a bounded
  * wait gives up.  Reads (and, if clear_after is non-zero, resets) the word of
- * the current device; synchronises the stream first.  0 = no error.
+ * the current device; synchronises the stream first.  0 = no error, 1 = an
+ * mbarrier wait (a TMA or bulk copy that did not land) ran out, 2 = a count
+ * exceeded a fixed-size list (the excess was dropped), 3 = a CTA of a flat
+ * split merge gave up waiting for the other CTAs of its token.  The first
+ * error since the last reset is kept.
  */
 int titan_device_error(int *error_out, int clear_after, titan_stream_t stream);
 
