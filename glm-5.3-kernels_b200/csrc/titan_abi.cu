@@ -72,7 +72,21 @@ __global__ void selftest_bounded_wait_kernel(long long limit_cycles) {
   mbar_wait_bounded(&bar, 0u, limit_cycles);  // phase 0 never completes
 }
 
+// A counter that no kernel writes: the spin self-test waits for it to reach 1.
+__device__ int g_selftest_counter = 0;
+
+__global__ void selftest_bounded_spin_kernel(long long limit_cycles) {
+  if (threadIdx.x == 0) spin_until_at_least(&g_selftest_counter, 1, limit_cycles);
+}
+
 }  // namespace titan
+
+extern "C" int titan_selftest_bounded_spin(long long limit_cycles, titan_stream_t stream) {
+  if (limit_cycles < 1 || limit_cycles > 4000000000LL)
+    return titan::fail(TITAN_ERR_INVALID_ARGUMENT, "selftest: limit_cycles must be in [1, 4e9]");
+  titan::selftest_bounded_spin_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_cycles);
+  return titan::check_launch("selftest_bounded_spin launch");
+}
 
 extern "C" int titan_selftest_bounded_wait(long long limit_cycles, titan_stream_t stream) {
   if (limit_cycles < 1 || limit_cycles > 4000000000LL)

@@ -81,6 +81,7 @@ SIGNATURES = {
     "titan_moe_split_align_smem_bytes": (_i64, [_i64]),
     "titan_device_error": (_int, [ctypes.POINTER(_int), _int, _vp]),
     "titan_selftest_bounded_wait": (_int, [ctypes.c_longlong, _vp]),
+    "titan_selftest_bounded_spin": (_int, [ctypes.c_longlong, _vp]),
     "titan_moe_w4a16_packed_bytes": (_i64, [_i64, _i64, _i64]),
     "titan_pool_topk_expand": (_int, [_vp, _i64, _vp, _i64, _int, _int, _vp, _i64, _int, _vp]),
     "titan_moe_w4a16_gemm": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _int, _int, _int,

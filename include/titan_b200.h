@@ -371,6 +371,14 @@ int titan_pool_topk_expand(const float *logits, int64_t ld, const int32_t *seq_l
  */
 int titan_selftest_bounded_wait(long long limit_cycles, titan_stream_t stream);
 
+/*
+ * Self-test of the bounded counter wait of the flat split merge (no
+ * counterpart in the reference): one thread waits for a device counter that
+ * nothing increments, gives up after about `limit_cycles` SM clocks (1 ..
+ * 4e9), sets the device error word to 3 and returns; the context stays usable.
+ */
+int titan_selftest_bounded_spin(long long limit_cycles, titan_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -3,8 +3,9 @@
 
 Every wait in the kernels is bounded: a wait that runs out sets the device
 error word (read by titan_device_error) and the kernel returns instead of
-trapping.  The self-test kernel waits on an mbarrier that nothing completes,
-so its wait runs out by construction; the host then reads the status, and
+trapping.  The self-test kernels wait on an mbarrier that nothing completes
+and on a counter that nothing increments, so their waits run out by
+construction; the host then reads the status, and
 the context is shown to be usable by a normal call checked against the
 oracle.
 """
@@ -29,6 +30,12 @@ def test_wait_that_runs_out_is_reported_and_context_survives(native_lib, cuda_de
     assert titan_native.device_error(probe) == 0
     with pytest.raises(titan_native.TitanError):
         titan_native.check(native_lib.titan_selftest_bounded_wait(0, stream), "selftest")
+    # The flat split merge's counter wait: a counter nothing increments.
+    titan_native.check(native_lib.titan_selftest_bounded_spin(2_000_000, stream), "selftest")
+    assert titan_native.device_error(probe) == 3                 # kDevErrSpinTimeout
+    assert titan_native.device_error(probe) == 0
+    with pytest.raises(titan_native.TitanError):
+        titan_native.check(native_lib.titan_selftest_bounded_spin(0, stream), "selftest")
 
     g = torch.Generator().manual_seed(3)
     n = 4096
