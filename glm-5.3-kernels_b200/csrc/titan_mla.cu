@@ -566,7 +566,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
   }
 
-  // Softmax state of head red_h, replicated over its 16 lanes.
+  // Softmax state of head red_h: m_run replicated over its 16 lanes, l_run
+  // one share per lane until the loop ends.
   float m_run = kNegLarge, l_run = 0.0f;
   float acc[8][4];
 #pragma unroll
@@ -699,15 +700,23 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Largest valid row scale of the tile, as bits (positive floats: bit
       // order = value order; masked rows may hold stale bytes and count as 0).
       uint32_t top = max(v0 ? __float_as_uint(sc0) : 0u, v1 ? __float_as_uint(sc1) : 0u);
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if constexpr (kF16) top = max(top, __shfl_xor_sync(0xffffffffu, top, o));
-      }
       // The running max moves only when the tile's max exceeds it by more
       // than kLazyMax (log2 units): p stays <= 2^kLazyMax, and most tiles
       // leave the accumulator unscaled (alpha == 1 skips the rescale below).
       // Any reference value gives the same softmax: acc and l share it.
+      // The head-wide max (and, f16, largest row scale) is needed only when
+      // some lane would move m_run (or e_acc): a warp vote decides, and the
+      // shuffle reductions run only then (always at the first tile).  Without
+      // them every lane's own max leaves m_run and e_acc unchanged, as the
+      // head-wide values would.
+      const bool grow = mx > m_run + kLazyMax || (kF16 && (int)(top >> 23) - 127 > e_acc);
+      if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          if constexpr (kF16) top = max(top, __shfl_xor_sync(0xffffffffu, top, o));
+        }
+      }
       const float m_cand = fmaxf(m_run, mx);
       const float m_new = m_cand > m_run + kLazyMax ? m_cand : m_run;
       const int e_new = kF16 ? max(e_acc, (int)(top >> 23) - 127) : 0;
@@ -715,10 +724,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float alpha = kF16 ? am * exp2i(e_acc - e_new) : am;
       const float p0 = v0 ? ex2_approx(x0 - m_new) : 0.0f;
       const float p1 = v1 ? ex2_approx(x1 - m_new) : 0.0f;
-      float ps = p0 + p1;
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      l_run = l_run * am + ps;
+      l_run = l_run * am + (p0 + p1);  // this lane's share; the head's 16 lanes are summed after the loop
       m_run = m_new;
       // P = bf16(p s_r), rounded as kernels/titan_mla.py:175-176 does; f16:
       // p s_r 2^-e_new (11 significant bits against bf16's 8).
@@ -788,6 +794,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       acc[n][3] *= es;
     }
   }
+
+  // The softmax denominator of head red_h: the sum of its 16 lanes' shares
+  // (each rescaled with the head's common factors along the way).
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, o);
 
   // ---- Epilogue.  Lane (g, c) of warp w holds, for heads g and g + 8,
   // dims 64 w + 16 c + j at acc[2 s + x][2 half + e] with j = 4 s + 2 x + e.
