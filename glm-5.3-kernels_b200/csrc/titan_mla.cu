@@ -98,6 +98,7 @@ struct Smem {
 // Two CTAs per SM: 228 KB of shared memory per SM, 1 KB reserved per CTA.
 static_assert(2 * (sizeof(Smem) + 1024) <= 228 * 1024, "the reader must fit twice per SM");
 static_assert(kGroups == kWarps, "warp w issues gather4 group w");
+static_assert(offsetof(Smem, p) % 16 == 0 && (kPStrideWords * 4) % 16 == 0, "ldmatrix reads 16-byte rows of P");
 static_assert(offsetof(Smem, u) % 128 == 0 && kGroupBytes % 128 == 0, "gather4 destinations are 128-byte aligned");
 
 struct Params {
@@ -751,13 +752,24 @@ __global__ void __launch_bounds__(kThreads, 2)
           acc[n][3] *= al1;
         }
       }
+      // P's A fragments.  Long (f16) CTAs take them with one ldmatrix per
+      // k-step: lane i addresses row (i & 7) + 8 ((i >> 3) & 1), column block
+      // i >> 4 (rows 144 bytes apart: conflict free); prefill T = 4096
+      // 1.405 -> 1.394 ms.  Decode CTAs keep four 4-byte loads, whose first
+      // values reach the MMA sooner (ldmatrix there: B=1 +0.06 us, B=8
+      // +0.13 us).
+      const uint32_t *p_row = &sm.p[((lane & 7) + 8 * ((lane >> 3) & 1)) * kPStrideWords + 4 * (lane >> 4)];
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) {
         uint32_t a[4];
-        a[0] = sm.p[g * kPStrideWords + 8 * ks + c];
-        a[1] = sm.p[(g + 8) * kPStrideWords + 8 * ks + c];
-        a[2] = sm.p[g * kPStrideWords + 8 * ks + 4 + c];
-        a[3] = sm.p[(g + 8) * kPStrideWords + 8 * ks + 4 + c];
+        if constexpr (kF16) {
+          ldmatrix_x4(a, p_row + 8 * ks);
+        } else {
+          a[0] = sm.p[g * kPStrideWords + 8 * ks + c];
+          a[1] = sm.p[(g + 8) * kPStrideWords + 8 * ks + c];
+          a[2] = sm.p[g * kPStrideWords + 8 * ks + 4 + c];
+          a[3] = sm.p[(g + 8) * kPStrideWords + 8 * ks + 4 + c];
+        }
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
 #pragma unroll
