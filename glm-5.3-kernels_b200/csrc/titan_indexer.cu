@@ -23,7 +23,9 @@
 // atomics); the bin holding the k-th largest key follows from a suffix scan;
 // a second pass appends every key of that bin or above to a candidate list
 // (warp-aggregated); a bitonic sort of the candidates (key descending, pool
-// ascending) puts the k selected pools first, in their final order.  When
+// ascending; four per thread, fully unrolled) puts the k selected pools
+// first, in their final order.  The cluster form (few rows) keeps each CTA's
+// share of the row in registers between the two passes.  When
 // more than 4096 keys reach the candidate list (heavy ties or a degenerate
 // distribution), the exact multi-pass selection runs instead: three radix
 // passes (11 + 11 + 10 bits) find the k-th key, keys above it are collected,
@@ -59,6 +61,7 @@ struct Smem {
 };
 
 constexpr int kClusterMax = 16;       // CTAs per row in the cluster form
+constexpr int kRegVec = 2;            // cluster form: 16-byte vectors per thread kept in registers (8192 pools per CTA)
 static_assert(kBins / 8 >= kBins / kClusterMax && kBins % kClusterMax == 0, "histogram slices");
 
 // Block-wide exclusive scan of one value per thread (1024 threads).
@@ -112,50 +115,115 @@ __device__ __forceinline__ void find_bin(const uint32_t *hist, int nb, uint32_t 
 
 // Bitonic sort of the first s (<= kMaxK) pairs of sm.key / sm.pool: key
 // descending, pool ascending; the result goes back to sm.key / sm.pool
-// [0, s).  Thread t holds element t in registers (entries past s sort last).
-// Partners closer than 32 are exchanged by shuffles; farther ones through
-// two alternating shared-memory buffers (in the histogram's space, free by
-// now), one block barrier per such sub-stage.
+// [0, s).  Four elements per thread in the first kSortThreads threads:
+// element e = 4 t + r (entries past s sort last).  Partners 1 or 2 apart are
+// in the same thread, 4..124 apart in the same warp (shuffles), 128 or more
+// through two alternating shared-memory buffers (in the histogram's space,
+// free by now), one block barrier per such sub-stage: 6 of the 55 sub-stages
+// of a 1024-wide sort (one element per thread needed 15).  Every thread of
+// the block takes the barriers.  The network is unrolled at full width:
+// with run-time strides (a network sized to s) the in-thread partners
+// became run-time register selects and the sort took ~10 us longer than the
+// one-element-per-thread network it replaces.
+constexpr int kSortThreads = kMaxK / 4;
+static_assert(kSortThreads % 32 == 0 && 2 * kSortThreads * 4 <= kBins, "sort buffers fit two histogram copies");
+
+__device__ __forceinline__ bool first_ordered(uint32_t ka, int32_t pa, uint32_t kb, int32_t pb) {
+  return ka > kb || (ka == kb && pa < pb);
+}
+
 __device__ __forceinline__ void sort_pairs(Smem &sm, int s) {
   const int tid = threadIdx.x;
-  int sw = 1;
-  while (sw < s) sw <<= 1;
+  const bool active = tid < kSortThreads;  // whole warps
+  // The network is always kMaxK wide and fully unrolled, so every partner and
+  // direction is a compile-time choice (entries past s are padding).
+  constexpr int sw = kMaxK;
   __syncthreads();  // the pairs were written by other threads; the histogram space is free
-  uint32_t key = tid < s ? sm.key[tid] : 0u;
-  int32_t pl = tid < s ? sm.pool[tid] : 0x7fffffff;
-  uint32_t *xk = &sm.hist[0][0];                              // [2][kThreads] keys
-  int32_t *xp = reinterpret_cast<int32_t *>(&sm.hist[1][0]);  // [2][kThreads] pools
+  uint32_t key[4];
+  int32_t pl[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int e = 4 * tid + r;
+    key[r] = active && e < s ? sm.key[e] : 0u;
+    pl[r] = active && e < s ? sm.pool[e] : 0x7fffffff;
+  }
+  uint4 *xk = reinterpret_cast<uint4 *>(&sm.hist[0][0]);  // [2][kSortThreads]
+  int4 *xp = reinterpret_cast<int4 *>(&sm.hist[1][0]);    // [2][kSortThreads]
   int buf = 0;
+#pragma unroll
   for (int size = 2; size <= sw; size <<= 1) {
+#pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      uint32_t ok;
-      int32_t op;
-      if (stride < 32) {
-        ok = __shfl_xor_sync(0xffffffffu, key, stride);
-        op = __shfl_xor_sync(0xffffffffu, pl, stride);
+      if (stride < 4) {  // partner in this thread: pairs (a, a + stride), a & stride == 0
+        if (active) {
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            if (a & stride) continue;
+            const int b = a + stride;
+            const bool asc = ((4 * tid + a) & size) == 0;  // this pair's lower slot takes the first-ordered
+            if (first_ordered(key[a], pl[a], key[b], pl[b]) != asc) {
+              const uint32_t tk = key[a];
+              key[a] = key[b];
+              key[b] = tk;
+              const int32_t tp = pl[a];
+              pl[a] = pl[b];
+              pl[b] = tp;
+            }
+          }
+        }
+        continue;
+      }
+      const int ts = stride >> 2;  // partner thread: tid ^ ts, same r
+      uint32_t ok[4];
+      int32_t op[4];
+      if (ts < 32) {
+        if (active) {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            ok[r] = __shfl_xor_sync(0xffffffffu, key[r], ts);
+            op[r] = __shfl_xor_sync(0xffffffffu, pl[r], ts);
+          }
+        }
       } else {
-        xk[buf * kThreads + tid] = key;
-        xp[buf * kThreads + tid] = pl;
+        if (active) {
+          xk[buf * kSortThreads + tid] = make_uint4(key[0], key[1], key[2], key[3]);
+          xp[buf * kSortThreads + tid] = make_int4(pl[0], pl[1], pl[2], pl[3]);
+        }
         __syncthreads();
-        ok = xk[buf * kThreads + (tid ^ stride)];
-        op = xp[buf * kThreads + (tid ^ stride)];
+        if (active) {
+          const uint4 k4 = xk[buf * kSortThreads + (tid ^ ts)];
+          const int4 p4 = xp[buf * kSortThreads + (tid ^ ts)];
+          ok[0] = k4.x, ok[1] = k4.y, ok[2] = k4.z, ok[3] = k4.w;
+          op[0] = p4.x, op[1] = p4.y, op[2] = p4.z, op[3] = p4.w;
+        }
         buf ^= 1;
       }
-      // This thread's slot takes the pair's first-ordered element when it is
-      // the lower slot of a "first-ordered first" block (or the upper slot
-      // of a reversed one).
-      const bool lower = (tid & stride) == 0;
-      const bool ascending_block = (tid & size) == 0;
-      const bool me_first = key > ok || (key == ok && pl < op);
-      if ((lower == ascending_block) != me_first) {
-        key = ok;
-        pl = op;
+      if (active) {
+        // This thread's slots take the pair's first-ordered element when they
+        // are the lower slots of a "first-ordered first" block (or the upper
+        // slots of a reversed one); size >= 8 here, the same for all r.
+        const bool lower = (tid & ts) == 0;
+        const bool ascending_block = ((4 * tid) & size) == 0;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const bool me_first = first_ordered(key[r], pl[r], ok[r], op[r]);
+          if ((lower == ascending_block) != me_first) {
+            key[r] = ok[r];
+            pl[r] = op[r];
+          }
+        }
       }
     }
   }
-  if (tid < s) {
-    sm.key[tid] = key;
-    sm.pool[tid] = pl;
+  if (active) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int e = 4 * tid + r;
+      if (e < s) {
+        sm.key[e] = key[r];
+        sm.pool[e] = pl[r];
+      }
+    }
   }
   __syncthreads();
 }
@@ -493,7 +561,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   // loads stay aligned when the row is).
   const int per = ((n + C - 1) / C + 3) & ~3;
   const int lo = min(n, r * per), hi = min(n, lo + per);
-  histogram_top11(row + lo, hi - lo, sm);
+  const int m = hi - lo;
+  // A share of at most kRegVec 16-byte vectors per thread (an aligned row)
+  // stays in registers, as keys, from the histogram to the candidate pass:
+  // no second read of the row.  Its loads are issued before the histogram
+  // copies are cleared, so the clearing hides their latency.
+  const bool in_regs = m <= kRegVec * 4 * kThreads && (reinterpret_cast<uintptr_t>(row + lo) & 15u) == 0;
+  uint32_t kk[kRegVec][4];
+  int nv[kRegVec];
+  if (in_regs) {
+    const float4 *r4 = reinterpret_cast<const float4 *>(row + lo);
+    const int n4 = (m + 3) >> 2;  // the last vector may run past m (same 16-byte line)
+    float4 v[kRegVec];
+#pragma unroll
+    for (int j = 0; j < kRegVec; ++j) {
+      const int c = tid + j * kThreads;
+      v[j] = c < n4 ? __ldg(r4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      nv[j] = max(0, min(4, m - 4 * c));
+    }
+    for (int b = tid; b < kHistCopies * kBins; b += kThreads) (&sm.hist[0][0])[b] = 0;
+#pragma unroll
+    for (int j = 0; j < kRegVec; ++j) {
+      kk[j][0] = float_key(v[j].x);
+      kk[j][1] = float_key(v[j].y);
+      kk[j][2] = float_key(v[j].z);
+      kk[j][3] = float_key(v[j].w);
+    }
+    __syncthreads();
+    uint32_t *h = sm.hist[(tid >> 5) >> 2];
+#pragma unroll
+    for (int j = 0; j < kRegVec; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (q < nv[j]) atomicAdd(&h[kk[j][q] >> 21], 1u);
+    __syncthreads();
+    for (int b = tid; b < kBins; b += kThreads) {
+      uint32_t sum = 0;
+#pragma unroll
+      for (int c = 0; c < kHistCopies; ++c) sum += sm.hist[c][b];
+      sm.hist[0][b] = sum;
+    }
+    __syncthreads();
+  } else {
+    histogram_top11(row + lo, m, sm);
+  }
   if (tid == 0) sm.ccnt = 0;  // CTA 0's candidate counter (every CTA clears its own)
   cluster_sync_all();         // every CTA's histogram (sm.hist[0]) is complete
   // Slice sums: CTA r owns bins [r S, r S + S).  C consecutive lanes (C
@@ -531,17 +642,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t key0, pool0;
     asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(key0) : "r"(smem_u32(&sm.key[0])), "r"(0));
     asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(pool0) : "r"(smem_u32(&sm.pool[0])), "r"(0));
-    collect_candidates(
-        row + lo, hi - lo, thr, [&](uint32_t c) { return atom_add_cluster_u32(cnt0, c); },
-        [&](uint32_t pos, uint32_t key, int i) {
-          // pos < cand <= kCandCap by construction; checked, not trusted
-          if (pos < (uint32_t)kCandCap) {
-            st_cluster_u32(key0 + 4 * pos, key);
-            st_cluster_u32(pool0 + 4 * pos, (uint32_t)(lo + i));
-          } else {
-            atomicCAS(&g_device_error, 0, kDevErrCapacity);
+    auto put = [&](uint32_t pos, uint32_t key, int i) {
+      // pos < cand <= kCandCap by construction; checked, not trusted
+      if (pos < (uint32_t)kCandCap) {
+        st_cluster_u32(key0 + 4 * pos, key);
+        st_cluster_u32(pool0 + 4 * pos, (uint32_t)(lo + i));
+      } else {
+        atomicCAS(&g_device_error, 0, kDevErrCapacity);
+      }
+    };
+    if (in_regs) {
+      // One remote atomic per warp reserves the slots of all its keeps: one
+      // ballot per key slot, offsets by popcount.
+      const int lane = tid & 31;
+      const uint32_t lt = (1u << lane) - 1u;
+      uint32_t ball[kRegVec][4];
+      uint32_t total = 0;
+#pragma unroll
+      for (int j = 0; j < kRegVec; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          ball[j][q] = __ballot_sync(0xffffffffu, q < nv[j] && (kk[j][q] >> 21) >= thr);
+          total += (uint32_t)__popc(ball[j][q]);
+        }
+      if (total) {  // warp-uniform
+        uint32_t base = 0;
+        if (lane == 0) base = atom_add_cluster_u32(cnt0, total);
+        base = __shfl_sync(0xffffffffu, base, 0);
+#pragma unroll
+        for (int j = 0; j < kRegVec; ++j)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if ((ball[j][q] >> lane) & 1u) put(base + (uint32_t)__popc(ball[j][q] & lt), kk[j][q], 4 * (tid + j * kThreads) + q);
+            base += (uint32_t)__popc(ball[j][q]);
           }
-        });
+      }
+    } else {
+      collect_candidates(row + lo, m, thr, [&](uint32_t c) { return atom_add_cluster_u32(cnt0, c); }, put);
+    }
   }
   // The candidates have reached CTA 0, and no CTA reads a peer's slice any
   // more: the others may exit.
