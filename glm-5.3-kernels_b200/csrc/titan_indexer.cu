@@ -62,6 +62,11 @@ struct Smem {
 
 constexpr int kClusterMax = 16;       // CTAs per row in the cluster form
 constexpr int kRegVec = 2;            // cluster form: 16-byte vectors per thread kept in registers (8192 pools per CTA)
+// Slice-sum rounds of the cluster form: S = kBins / C bins per CTA, kThreads / C
+// of them per round, for both cluster sizes (8 and 16).
+constexpr int kSliceRounds = kBins / kThreads;
+static_assert((kBins / 8) / (kThreads / 8) == kSliceRounds && (kBins / 16) / (kThreads / 16) == kSliceRounds,
+              "slice rounds");
 static_assert(kBins / 8 >= kBins / kClusterMax && kBins % kClusterMax == 0, "histogram slices");
 
 // Block-wide exclusive scan of one value per thread (1024 threads).
@@ -609,24 +614,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();         // every CTA's histogram (sm.hist[0]) is complete
   // Slice sums: CTA r owns bins [r S, r S + S).  C consecutive lanes (C
   // divides 32) load one bin from the C CTAs at once and add by shuffles.
+  // (kSliceRounds rounds of kThreads / C bins; every remote load is issued
+  // before the first sum, one round trip instead of one per round.)
   const int S = kBins / C;
-  for (int b0 = 0; b0 < S; b0 += kThreads / C) {
-    const int b = b0 + tid / C, q = tid % C;
-    uint32_t v = 0;
-    if (b < S) {
-      uint32_t a;
-      asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(&sm.hist[0][r * S + b])), "r"(q));
-      v = ld_cluster_u32(a);
+  {
+    uint32_t v[kSliceRounds];
+#pragma unroll
+    for (int j = 0; j < kSliceRounds; ++j) {
+      const int b = j * (kThreads / C) + tid / C, q = tid % C;
+      v[j] = 0;
+      if (b < S) {
+        uint32_t a;
+        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(&sm.hist[0][r * S + b])), "r"(q));
+        v[j] = ld_cluster_u32(a);
+      }
     }
-    for (int o = C >> 1; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o, C);
-    if (q == 0 && b < S) sm.slice[b] = v;
+#pragma unroll
+    for (int j = 0; j < kSliceRounds; ++j) {
+      const int b = j * (kThreads / C) + tid / C, q = tid % C;
+      for (int o = C >> 1; o > 0; o >>= 1) v[j] += __shfl_down_sync(0xffffffffu, v[j], o, C);
+      if (q == 0 && b < S) sm.slice[b] = v[j];
+    }
   }
   cluster_sync_all();  // every slice is summed
-  // The row's histogram, read back from the slices into sm.hist[1].
-  for (int b = tid; b < kBins; b += kThreads) {
-    uint32_t a;
-    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(&sm.slice[b % S])), "r"(b / S));
-    sm.hist[1][b] = ld_cluster_u32(a);
+  // The row's histogram, read back from the slices into sm.hist[1] (both
+  // remote loads of a thread in flight together).
+  {
+    uint32_t v[kBins / kThreads];
+#pragma unroll
+    for (int j = 0; j < kBins / kThreads; ++j) {
+      const int b = tid + j * kThreads;
+      uint32_t a;
+      asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(&sm.slice[b % S])), "r"(b / S));
+      v[j] = ld_cluster_u32(a);
+    }
+#pragma unroll
+    for (int j = 0; j < kBins / kThreads; ++j) sm.hist[1][tid + j * kThreads] = v[j];
   }
   __syncthreads();
   find_bin(sm.hist[1], kBins, (uint32_t)k, sm);
