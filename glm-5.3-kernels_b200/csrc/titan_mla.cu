@@ -331,8 +331,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int t = blockIdx.x / p.S;
-  const int split = blockIdx.x - t * p.S;
+  // Long single-pass (f16) launches take the tokens last first: in a causal
+  // prefill a token's valid indices grow with its position, so the longest
+  // CTAs start first and the short ones fill the last wave (T = 4096:
+  // 1.396 -> 1.386 ms).  Decode launches keep the natural order (reversed,
+  // B=1 was 0.03 us slower).
+  const int tb = blockIdx.x / p.S;
+  const int split = blockIdx.x - tb * p.S;
+  const int t = kF16 ? p.T - 1 - tb : tb;
   const int hg = blockIdx.y;
 
   // Ring-stage barriers (one arrival per warp, plus the gather bytes, per
