@@ -22,9 +22,9 @@
 // eight private copies (few hot bins would otherwise serialise the shared
 // atomics); the bin holding the k-th largest key follows from a suffix scan;
 // a second pass appends every key of that bin or above to a candidate list
-// (warp-aggregated); a bitonic sort of the candidates (key descending, pool
-// ascending; four per thread, fully unrolled) puts the k selected pools
-// first, in their final order.  The cluster form (few rows) keeps each CTA's
+// (warp-aggregated); one refinement pass over the candidates and bitonic
+// sorts (key descending, pool ascending; unrolled networks in registers) put
+// the k selected pools first, in their final order.  The cluster form (few rows) keeps each CTA's
 // share of the row in registers between the two passes.  When
 // more than 4096 keys reach the candidate list (heavy ties or a degenerate
 // distribution), the exact multi-pass selection runs instead: three radix
@@ -58,6 +58,7 @@ struct Smem {
   uint32_t warp_sum[32];
   uint32_t bin, above, cnt;           // cnt is also the scan's total (block_exclusive_scan)
   uint32_t ccnt;                      // cluster form: CTA 0's candidate count (nothing else writes it)
+  uint32_t bcnt;                      // boundary-bin entries of the split selection
 };
 
 constexpr int kClusterMax = 16;       // CTAs per row in the cluster form
@@ -118,54 +119,48 @@ __device__ __forceinline__ void find_bin(const uint32_t *hist, int nb, uint32_t 
   __syncthreads();
 }
 
-// Bitonic sort of the first s (<= kMaxK) pairs of sm.key / sm.pool: key
-// descending, pool ascending; the result goes back to sm.key / sm.pool
-// [0, s).  Four elements per thread in the first kSortThreads threads:
-// element e = 4 t + r (entries past s sort last).  Partners 1 or 2 apart are
-// in the same thread, 4..124 apart in the same warp (shuffles), 128 or more
-// through two alternating shared-memory buffers (in the histogram's space,
-// free by now), one block barrier per such sub-stage: 6 of the 55 sub-stages
-// of a 1024-wide sort (one element per thread needed 15).  Every thread of
-// the block takes the barriers.  The network is unrolled at full width:
-// with run-time strides (a network sized to s) the in-thread partners
-// became run-time register selects and the sort took ~10 us longer than the
-// one-element-per-thread network it replaces.
-constexpr int kSortThreads = kMaxK / 4;
-static_assert(kSortThreads % 32 == 0 && 2 * kSortThreads * 4 <= kBins, "sort buffers fit two histogram copies");
-
 __device__ __forceinline__ bool first_ordered(uint32_t ka, int32_t pa, uint32_t kb, int32_t pb) {
   return ka > kb || (ka == kb && pa < pb);
 }
 
-__device__ __forceinline__ void sort_pairs(Smem &sm, int s) {
-  const int tid = threadIdx.x;
-  const bool active = tid < kSortThreads;  // whole warps
-  // The network is always kMaxK wide and fully unrolled, so every partner and
-  // direction is a compile-time choice (entries past s are padding).
-  constexpr int sw = kMaxK;
-  __syncthreads();  // the pairs were written by other threads; the histogram space is free
-  uint32_t key[4];
-  int32_t pl[4];
+static_assert(2 * kMaxK <= kBins, "sort exchange buffers fit one histogram copy each");
+
+// Bitonic network over the first s (<= W) pairs of keys / pools (key
+// descending, pool ascending), sorted in place.  E elements per thread in
+// threads lt = 0 .. W / E - 1 of the calling group (active; the others only
+// take the barriers): element e = E lt + r, entries past s sort last.
+// Partners closer than E are in the same thread, closer than 32 E in the
+// same warp (shuffles), farther ones are exchanged through two alternating
+// buffers xk / xp (2 W words each; one block barrier per such sub-stage,
+// taken by every thread of the block).  Unrolled at full width: with
+// run-time strides the in-thread partners became run-time register selects
+// and a 1024-wide sort took ~10 us longer.  A network of W <= 32 E has no
+// barrier and may run in one warp.
+template <int W, int E>
+__device__ __forceinline__ void sort_net(uint32_t *keys, int32_t *pools, int s, int lt, bool active, uint32_t *xk,
+                                         int32_t *xp) {
+  constexpr int T = W / E;
+  static_assert(E == 1 || E == 2 || E == 4, "elements per thread");
+  uint32_t key[E];
+  int32_t pl[E];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int e = 4 * tid + r;
-    key[r] = active && e < s ? sm.key[e] : 0u;
-    pl[r] = active && e < s ? sm.pool[e] : 0x7fffffff;
+  for (int r = 0; r < E; ++r) {
+    const int e = E * lt + r;
+    key[r] = active && e < s ? keys[e] : 0u;
+    pl[r] = active && e < s ? pools[e] : 0x7fffffff;
   }
-  uint4 *xk = reinterpret_cast<uint4 *>(&sm.hist[0][0]);  // [2][kSortThreads]
-  int4 *xp = reinterpret_cast<int4 *>(&sm.hist[1][0]);    // [2][kSortThreads]
   int buf = 0;
 #pragma unroll
-  for (int size = 2; size <= sw; size <<= 1) {
+  for (int size = 2; size <= W; size <<= 1) {
 #pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride < 4) {  // partner in this thread: pairs (a, a + stride), a & stride == 0
+      if (stride < E) {  // partner in this thread: pairs (a, a + stride), a & stride == 0
         if (active) {
 #pragma unroll
-          for (int a = 0; a < 4; ++a) {
+          for (int a = 0; a < E; ++a) {
             if (a & stride) continue;
             const int b = a + stride;
-            const bool asc = ((4 * tid + a) & size) == 0;  // this pair's lower slot takes the first-ordered
+            const bool asc = ((E * lt + a) & size) == 0;  // this pair's lower slot takes the first-ordered
             if (first_ordered(key[a], pl[a], key[b], pl[b]) != asc) {
               const uint32_t tk = key[a];
               key[a] = key[b];
@@ -178,39 +173,43 @@ __device__ __forceinline__ void sort_pairs(Smem &sm, int s) {
         }
         continue;
       }
-      const int ts = stride >> 2;  // partner thread: tid ^ ts, same r
-      uint32_t ok[4];
-      int32_t op[4];
+      const int ts = stride / E;  // partner thread: lt ^ ts, same r
+      uint32_t ok[E];
+      int32_t op[E];
       if (ts < 32) {
         if (active) {
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
+          for (int r = 0; r < E; ++r) {
             ok[r] = __shfl_xor_sync(0xffffffffu, key[r], ts);
             op[r] = __shfl_xor_sync(0xffffffffu, pl[r], ts);
           }
         }
       } else {
         if (active) {
-          xk[buf * kSortThreads + tid] = make_uint4(key[0], key[1], key[2], key[3]);
-          xp[buf * kSortThreads + tid] = make_int4(pl[0], pl[1], pl[2], pl[3]);
+#pragma unroll
+          for (int r = 0; r < E; ++r) {
+            xk[(buf * T + lt) * E + r] = key[r];
+            xp[(buf * T + lt) * E + r] = pl[r];
+          }
         }
         __syncthreads();
         if (active) {
-          const uint4 k4 = xk[buf * kSortThreads + (tid ^ ts)];
-          const int4 p4 = xp[buf * kSortThreads + (tid ^ ts)];
-          ok[0] = k4.x, ok[1] = k4.y, ok[2] = k4.z, ok[3] = k4.w;
-          op[0] = p4.x, op[1] = p4.y, op[2] = p4.z, op[3] = p4.w;
+#pragma unroll
+          for (int r = 0; r < E; ++r) {
+            ok[r] = xk[(buf * T + (lt ^ ts)) * E + r];
+            op[r] = xp[(buf * T + (lt ^ ts)) * E + r];
+          }
         }
         buf ^= 1;
       }
       if (active) {
         // This thread's slots take the pair's first-ordered element when they
         // are the lower slots of a "first-ordered first" block (or the upper
-        // slots of a reversed one); size >= 8 here, the same for all r.
-        const bool lower = (tid & ts) == 0;
-        const bool ascending_block = ((4 * tid) & size) == 0;
+        // slots of a reversed one); size > stride >= E, the same for all r.
+        const bool lower = (lt & ts) == 0;
+        const bool ascending_block = ((E * lt) & size) == 0;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
+        for (int r = 0; r < E; ++r) {
           const bool me_first = first_ordered(key[r], pl[r], ok[r], op[r]);
           if ((lower == ascending_block) != me_first) {
             key[r] = ok[r];
@@ -222,14 +221,30 @@ __device__ __forceinline__ void sort_pairs(Smem &sm, int s) {
   }
   if (active) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int e = 4 * tid + r;
+    for (int r = 0; r < E; ++r) {
+      const int e = E * lt + r;
       if (e < s) {
-        sm.key[e] = key[r];
-        sm.pool[e] = pl[r];
+        keys[e] = key[r];
+        pools[e] = pl[r];
       }
     }
   }
+}
+
+// Sort of the first s (<= kMaxK) pairs of sm.key / sm.pool, key descending,
+// pool ascending, in place: a 512-wide network (two per thread, 256 threads,
+// 45 sub-stages, 6 behind barriers) when s <= 512, else a 1024-wide one (four
+// per thread, 55 sub-stages, 6 behind barriers).  The exchange buffers are
+// in the histogram's space, free by now.
+__device__ __forceinline__ void sort_pairs(Smem &sm, int s) {
+  const int tid = threadIdx.x;
+  __syncthreads();  // the pairs were written by other threads; the histogram space is free
+  uint32_t *xk = &sm.hist[0][0];
+  int32_t *xp = reinterpret_cast<int32_t *>(&sm.hist[1][0]);
+  if (s <= kMaxK / 2)
+    sort_net<kMaxK / 2, 2>(sm.key, sm.pool, s, tid, tid < kMaxK / 4, xk, xp);
+  else
+    sort_net<kMaxK, 4>(sm.key, sm.pool, s, tid, tid < kMaxK / 4, xk, xp);
   __syncthreads();
 }
 
@@ -420,18 +435,63 @@ __device__ void select_from_candidates(Smem &sm, int c, uint32_t thr, uint32_t a
     kept_pool[q] = keep[q] ? sm.pool[i] : 0;
     nk += keep[q] ? 1u : 0u;
   }
-  if (tid == 0) sm.cnt = 0;
+  // Split selection: the a keys above the boundary bin (bits 31..10 of T)
+  // all precede its b keys, and a < k <= a + b.  With a <= 512 and b <= 32
+  // the a keys are sorted by a 512-wide network while one warp sorts the
+  // boundary bin and appends its first k - a, instead of one 1024-wide sort
+  // of all a + b (which the usual ~530 kept keys need).
+  const int a_above = (int)(above + sm.above);
+  const int b_bin = (int)h0[sm.bin];
+  const bool split = a_above <= kMaxK / 2 && b_bin <= 32;
+  if (tid == 0) {
+    sm.cnt = 0;
+    sm.bcnt = 0;
+  }
   __syncthreads();  // every candidate has been read before the list is rewritten
-  uint32_t pos = nk ? atomicAdd(&sm.cnt, nk) : 0u;
+  if (!split) {
+    uint32_t pos = nk ? atomicAdd(&sm.cnt, nk) : 0u;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      if (keep[q]) {
+        sm.key[pos] = kept_key[q];
+        sm.pool[pos] = kept_pool[q];
+        ++pos;
+      }
+    }
+    sort_pairs(sm, sel);  // the first k (ties by smaller pool) are the selection
+    return;
+  }
+  // Above the bin -> [0, a); in the bin -> [kBinSlot, kBinSlot + b).
+  constexpr int kBinSlot = kCandCap / 2;
+  const uint32_t tb = T >> 10;
+  uint32_t na = 0, nb = 0;
 #pragma unroll
   for (int q = 0; q < kPer; ++q) {
-    if (keep[q]) {
-      sm.key[pos] = kept_key[q];
-      sm.pool[pos] = kept_pool[q];
-      ++pos;
+    na += keep[q] && (kept_key[q] >> 10) > tb ? 1u : 0u;
+    nb += keep[q] && (kept_key[q] >> 10) == tb ? 1u : 0u;
+  }
+  uint32_t pa = na ? atomicAdd(&sm.cnt, na) : 0u;
+  uint32_t pb = nb ? atomicAdd(&sm.bcnt, nb) : 0u;
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    if (!keep[q]) continue;
+    const uint32_t slot = (kept_key[q] >> 10) > tb ? pa++ : kBinSlot + pb++;
+    sm.key[slot] = kept_key[q];
+    sm.pool[slot] = kept_pool[q];
+  }
+  __syncthreads();
+  if ((tid >> 5) == kThreads / 32 - 1) {  // the last warp: the boundary bin, then the a-sort's barriers
+    const int lane = tid & 31;
+    sort_net<32, 1>(sm.key + kBinSlot, sm.pool + kBinSlot, b_bin, lane, true, nullptr, nullptr);
+    __syncwarp();
+    if (lane < k - a_above) {
+      sm.key[a_above + lane] = sm.key[kBinSlot + lane];
+      sm.pool[a_above + lane] = sm.pool[kBinSlot + lane];
     }
   }
-  sort_pairs(sm, sel);  // the first k (ties by smaller pool) are the selection
+  sort_net<kMaxK / 2, 2>(sm.key, sm.pool, a_above, tid, tid < kMaxK / 4, &sm.hist[0][0],
+                         reinterpret_cast<int32_t *>(&sm.hist[1][0]));
+  __syncthreads();
 }
 
 // The index row: pools sm.pool[0, nsel) expanded to their tokens, the tail
@@ -441,10 +501,12 @@ __device__ __forceinline__ void expand_into(const Smem &sm, int nsel, int k, int
   const int span = k * pool;
   const int tail_start = (seq_len > 0 ? seq_len / pool : 0) * pool;
   const int tail_len = seq_len > 0 ? seq_len % pool : 0;
+  const bool pow2 = (pool & (pool - 1)) == 0;  // shifts instead of a division per entry
+  const int sh = __ffs(pool) - 1;
   for (int j = threadIdx.x; j < width; j += kThreads) {
     int v = -1;
     if (j < span) {
-      const int i = j / pool, o = j - (j / pool) * pool;
+      const int i = pow2 ? j >> sh : j / pool, o = pow2 ? j & (pool - 1) : j - (j / pool) * pool;
       if (i < nsel) v = sm.pool[i] * pool + o;
     } else if (j < span + pool - 1) {
       const int o = j - span;
