@@ -11,10 +11,11 @@
 //   :357-429 combine: sum_s exp(lse_s - M) o_s / sum_s exp(lse_s - M), bf16
 //
 // B200 design: one CTA (8 warps) per (token, split, 16-head group).
-//  * Row gather by the tensor memory accelerator: per 32-row tile, warp 0
-//    issues eight `cp.async.bulk.tensor ... tile::gather4` loads (four rows
-//    each, by row index, 544-byte boxes) into a three-stage shared-memory
-//    ring, two tiles ahead of the math, completing on the stage's mbarrier.
+//  * Row gather by the tensor memory accelerator: per 32-row tile, lane 0 of
+//    each of the eight warps issues one `cp.async.bulk.tensor ...
+//    tile::gather4` load (four rows by row index, 544-byte boxes) into a
+//    three-stage shared-memory ring, two tiles ahead of the math, completing
+//    on the stage's mbarrier.
 //    Rows outside [0, seq_kv) read as zeros (TMA bounds fill); a group whose
 //    four rows are all masked is not issued.  The row scale arrives with the
 //    row (bytes 512..515).  Warp w owns latent dims [64 w, 64 w + 64); lane
@@ -43,8 +44,13 @@
 //    reducing 512 / C dims; a single cluster writes the bf16 output directly.
 //    With more clusters than one, each cluster writes one partial (o, lse);
 //    given arrival counters, the last CTA of each rank to finish merges that
-//    rank's slice over all partials (no second kernel), otherwise a combine
-//    kernel, launched as a programmatic dependent, merges them.
+//    rank's slice over all partials (no second kernel).  When that does not
+//    apply (more partials than CTAs per cluster), counters are given and the
+//    grid fits on the device, the launch drops the clusters and is
+//    cooperative: every split CTA writes its partial, the CTAs of a token
+//    meet at a counter barrier and each merges a share of the output (flat
+//    merge).  Otherwise a combine kernel, launched as a programmatic
+//    dependent, merges the partials.
 #include <cuda.h>  // CUtensorMap
 
 #include "titan_common.cuh"
