@@ -37,9 +37,10 @@ def test_prefill_rows_all_lengths(native_lib, cuda_device):
     _check(logits, torch.tensor(lens, dtype=torch.int32), 512, 4, 2176, cuda_device)
 
 
-# Up to 9 rows take the cluster form (a cluster of 8-16 CTAs per row on a
-# 148-SM B200), 40 rows the one-CTA-per-row form.
-@pytest.mark.parametrize("rows", [5, 40])
+# Up to 9 rows take the cluster form on a 148-SM B200 (5 rows: clusters of
+# 16 CTAs, the slice-sum reduction; 8 rows: clusters of 8, every CTA summing
+# the whole histogram), 40 rows the one-CTA-per-row form.
+@pytest.mark.parametrize("rows", [5, 8, 40])
 @pytest.mark.parametrize("levels", [3, 40])
 def test_heavy_ties(native_lib, cuda_device, levels, rows):
     """Logits on a few levels: the k-th largest value is shared by many pools,
@@ -70,7 +71,8 @@ def test_nan_inf_and_small_k(native_lib, cuda_device):
     seq = torch.tensor([20000, 19999, 18000, 20003], dtype=torch.int32)
     for k, pool, width in ((512, 4, 2176), (1, 4, 8), (37, 1, 40), (1024, 2, 2049), (300, 16, 4815)):
         _check(logits, seq, k, pool, width, cuda_device)
-    # the same rows repeated (40 rows: the one-CTA-per-row form)
+    # the same rows repeated (8 rows: clusters of 8; 40 rows: one CTA per row)
+    _check(logits.repeat(2, 1), seq.repeat(2), 512, 4, 2176, cuda_device)
     _check(logits.repeat(10, 1), seq.repeat(10), 512, 4, 2176, cuda_device)
 
 
