@@ -1180,6 +1180,16 @@ def run_profile(args):
             run()
         torch.cuda.synchronize()
         return
+    if args.profile == "moe_align":  # config 5: B = 1 and B = 8 decode tokens x top-8 of 288 experts
+        from kernels.titan_moe_align import titan_moe_align_small
+        gm = torch.Generator().manual_seed(37)
+        sets = [torch.stack([torch.randperm(288, generator=gm)[:8] for _ in range(B)]).to(torch.int32).to(dev)
+                for B in (1, 8)]
+        for _ in range(n):
+            for ids in sets:
+                titan_moe_align_small(ids)
+        torch.cuda.synchronize()
+        return
     if args.profile == "split_align":  # M = 2304 tokens x top-8, 288 uniform experts
         from kernels import titan_moe_split_align as split_mod
         g = torch.Generator().manual_seed(1)
@@ -1240,7 +1250,7 @@ def main():
     ap.add_argument("--skip-reference-triton", action="store_true",
                     help="skip the secondary lines of the reference's Triton kernels run on this GPU")
     ap.add_argument("--profile", choices=("decode_b1", "decode_b8", "store_int8", "prefill", "paged_b1", "split_align",
-                                          "moe_gemm", "pool_topk"),
+                                          "moe_gemm", "pool_topk", "moe_align"),
                     default=None,
                     help="run only this workload (warmup + steps calls) as an ncu target; prints nothing")
     args = ap.parse_args()
